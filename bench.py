@@ -1,0 +1,424 @@
+"""Benchmark: Tensor Logic hot path on B200.
+
+Headline: the transitive-closure fixpoint at n = 32768 (a seeded random DAG,
+4n edges u < v): Reach = step(Edge); Reach max= step(Reach Edge) to
+convergence.  One step = one full program run (base equation + every
+fixpoint sweep).  metric = fixpoint sweeps per second over the whole n x n
+relation; with --gpus N the Reach rows are dealt cyclically over N ranks
+(one process per GPU, NCCL all-reduce of the changed word each sweep).
+At N = 1 the line also carries the einsum configurations (MLP forward,
+attention, MLP training step with autodiff, 2-layer GNN) as TFLOP/s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's own algorithm on the host cores: the
+literal loop nest of one fixpoint sweep (fixpoint.zig:167-297, x and z outer,
+y inner, in place), restated in f64 C (oracle/, built with -O2), on a bounded
+sample of rows, extrapolated to sweeps/s of the whole relation.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+N_CLOSURE = 32768
+DEG_CLOSURE = 4
+METRIC = "closure_fixpoint_iters_per_s"
+UNIT = "sweeps/s"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- dist
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Dist:
+    def __init__(self, world, rank, local):
+        self.world, self.rank, self.local = world, rank, local
+        self.pg = None
+        if world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as td
+            torch.cuda.set_device(local)
+            td.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+            self.td = td
+
+    def barrier(self):
+        if self.world > 1:
+            self.td.barrier()
+
+    def bcast_bytes(self, b):
+        if self.world == 1:
+            return b
+        obj = [b]
+        self.td.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def max(self, x):
+        if self.world == 1:
+            return x
+        import torch
+        t = torch.tensor([float(x)], dtype=torch.float64)
+        self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x):
+        if self.world == 1:
+            return x
+        import torch
+        t = torch.tensor([float(x)], dtype=torch.float64)
+        self.td.all_reduce(t, op=self.td.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.td.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------- timing
+class StreamTimer:
+    """CUDA events on the runtime's own stream."""
+
+    def __init__(self, ctx):
+        import torch
+        self.torch = torch
+        self.stream = torch.cuda.ExternalStream(ctx.stream_ptr)
+
+    def event(self):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record(self.stream)
+        return e
+
+
+def l2_flush(buf):
+    buf.add_(1)   # writes 256 MiB (> 126 MB L2) on torch's stream
+
+
+def time_steps(ctx, step, steps, warmup, dist, flush):
+    import torch
+    timer = StreamTimer(ctx)
+    for _ in range(warmup):
+        step()
+    ctx.sync()
+    torch.cuda.synchronize()
+    dist.barrier()
+    total = 0.0
+    launches0 = ctx.launches
+    for _ in range(steps):
+        l2_flush(flush)
+        torch.cuda.synchronize()
+        a = timer.event()
+        step()
+        b = timer.event()
+        ctx.sync()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return total, ctx.launches - launches0
+
+
+# ---------------------------------------------------------------------------- closure
+def closure_program(dist, resident):
+    from tensor_logic_lang_b200 import configs, lang
+    src, _, sparse, _ = configs.closure(n=N_CLOSURE, degree=DEG_CLOSURE)
+    rows, cols, _ = sparse["Edge"]
+    if resident:
+        # the Edge CSR is uploaded once; each run re-validates it (load with no host data)
+        p = lang.Program(src, sparse_inputs={"Edge": (rows, cols, None)})
+        p_res = lang.Program(src, sparse_inputs={"Edge": (rows, cols, None)})
+        # mark the sparse load of the resident program as "already on the device"
+        for k in range(p_res.n):
+            if p_res.stmts[k].kind == 7:
+                p_res.stmts[k].coo_rows = None
+                p_res.stmts[k].coo_cols = None
+        return p, p_res, rows, cols
+    return lang.Program(src, sparse_inputs={"Edge": (rows, cols, None)}), None, rows, cols
+
+
+def run_closure(args, dist, peaks):
+    import torch
+
+    from tensor_logic_lang_b200 import abi
+    from tensor_logic_lang_b200.runtime import Context, unique_id
+    nid = dist.bcast_bytes(unique_id() if dist.rank == 0 else None) if dist.world > 1 else None
+    ctx = Context(device=dist.local, rank=dist.rank, world_size=dist.world, nccl_id=nid)
+    if dist.world > 1:
+        ctx.set_sharding("Reach", abi.SHARD_ROWS)
+    full, resident, rows, cols = closure_program(dist, resident=True)
+    ctx.run(full)                                # uploads Edge (CSR) once
+    sweeps = ctx.sweeps
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=f"cuda:{dist.local}")
+
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    ctx.profile(True)
+    ctx.profile_reset()
+    ms, launches = time_steps(ctx, lambda: ctx.run(resident), args.steps, args.warmup, dist, flush)
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    clk = clocks.stop()
+    ms_max = dist.max(ms)
+    total_sweeps = sweeps * args.steps
+    value = total_sweeps / (ms_max / 1e3)
+
+    # roofline of the dominant kernel: one sweep reads and writes the local bit
+    # rows and reads the Edge CSR (int64 row pointers, int32 columns)
+    n = N_CLOSURE
+    local_rows = (n - dist.rank + dist.world - 1) // dist.world
+    nnz = len(rows)
+    sweep_bytes = 2.0 * local_rows * (n // 8) + (n + 1) * 8.0 + nnz * 4.0
+    st = prof.get("closure_sweep", {"launches": 0, "total_ms": float("nan")})
+    per_launch_ms = st["total_ms"] / max(1, st["launches"])
+    achieved = sweep_bytes / (per_launch_ms / 1e3) / 1e9
+    roof = {"kernel": "closure_sweep", "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks[0],
+            "unit": "GB/s", "frac": round(achieved / peaks[0], 4), "peak_source": peaks[2],
+            "traffic": None, "algo_bytes_per_launch": sweep_bytes, "avg_launch_ms": per_launch_ms,
+            "share_of_step": round(st["total_ms"] / max(ms, 1e-9), 3)}
+
+    # end to end: host COO -> CSR -> device, the fixpoint, full Reach bits back to the host
+    e2e_total = 0.0
+    h2d = rows.nbytes + cols.nbytes
+    d2h = local_rows * (n // 8)
+    out_bits = np.empty((local_rows, n // 32), dtype=np.uint32)
+    for i in range(args.warmup + args.steps):
+        dist.barrier()
+        t0 = time.perf_counter()
+        ctx.run(full)
+        out = ctx.bits("Reach", rows=local_rows)
+        ctx.sync()
+        t1 = time.perf_counter()
+        if i >= args.warmup:
+            e2e_total += t1 - t0
+        out_bits = out
+    e2e_s = dist.max(e2e_total)
+    e2e = {"value": total_sweeps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h)}
+    reach_pairs = dist.sum(int(np.unpackbits(out_bits.view(np.uint8)).sum()))
+    res = dict(value=value, ms=ms_max, sweeps=sweeps, launches=launches, roofline=roof, clocks=clk, e2e=e2e,
+               reach_pairs=int(reach_pairs), nnz=nnz, kernels=prof)
+    ctx.close()
+    return res
+
+
+# ---------------------------------------------------------------------------- einsum configs
+def run_einsum_configs(args, peaks):
+    import torch
+
+    from tensor_logic_lang_b200 import configs
+    from tensor_logic_lang_b200.runtime import Context
+    out = {}
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda:0")
+
+    class One:
+        world, rank = 1, 0
+
+        def barrier(self):
+            pass
+    for name, builder in [("mlp_forward", configs.mlp_forward), ("attention", configs.attention),
+                          ("mlp_train", configs.mlp_train), ("gnn", configs.gnn)]:
+        ctx = Context(device=0)
+        p, data, sparse, flops = configs.program(builder)
+        ctx.run(p)
+        # resident variant: inputs stay on the device, loads only re-validate them
+        p_res = configs.program(builder)[0]
+        for k in range(p_res.n):
+            s = p_res.stmts[k]
+            if s.kind == 6:
+                s.host_data = None
+                s.path = b""
+            if s.kind == 7:
+                s.coo_rows = None
+                s.coo_cols = None
+        ctx.profile(True)
+        ctx.profile_reset()
+        ms, launches = time_steps(ctx, lambda: ctx.run(p_res), args.steps, args.warmup, One(), flush)
+        prof = ctx.profile_read()
+        ctx.profile(False)
+        per = ms / args.steps
+        top = max(prof.items(), key=lambda kv: kv[1]["total_ms"]) if prof else ("", {})
+        tc = prof.get("gemm_tcgen05_tf32")
+        entry = {"tflops": round(flops / (per / 1e3) / 1e12, 3), "ms_per_step": round(per, 4),
+                 "algo_flops": flops, "gpu_launches_per_step": launches / args.steps,
+                 "top_kernel": top[0], "top_kernel_share": round(top[1].get("total_ms", 0) / max(ms, 1e-9), 3)}
+        if tc and tc["launches"]:
+            tflops = tc["flops"] / (tc["total_ms"] / 1e3) / 1e12
+            # TF32 issues at half the bf16 rate on the same tensor cores
+            peak_tf32 = peaks[1] / 2.0
+            entry["tcgen05_gemm"] = {"achieved_tflops": round(tflops, 1), "peak_tflops_tf32": peak_tf32,
+                                     "frac": round(tflops / peak_tf32, 4),
+                                     "peak_source": f"{peaks[2]} bf16 / 2"}
+        out[name] = entry
+        ctx.close()
+    return out
+
+
+# ---------------------------------------------------------------------------- reference arm
+def literal_sample(seconds=12.0):
+    """Time the literal reference sweep on sample rows; returns sweeps/s of the whole relation."""
+    from oracle import oracle
+    from tensor_logic_lang_b200 import configs
+    _, _, sparse, _ = configs.closure(n=N_CLOSURE, degree=DEG_CLOSURE)
+    rows, cols, _ = sparse["Edge"]
+    n = N_CLOSURE
+    W = n // 32
+    E = np.zeros((n, W), dtype=np.uint32)
+    np.bitwise_or.at(E, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
+    done_rows, t = 0, 0.0
+    while t < seconds:
+        x = done_rows % 64
+        R = np.zeros((1, n), dtype=np.float64)
+        sel = rows == x
+        R[0, cols[sel]] = 1.0                       # Reach[x,:] = step(Edge[x,:])
+        t0 = time.perf_counter()
+        oracle.closure_literal_rows(n, E, R, x0=x)
+        t += time.perf_counter() - t0
+        done_rows += 1
+    per_row = t / done_rows
+    return 1.0 / (per_row * n), done_rows, t
+
+
+def reference_arm(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    sps, rows_done, secs = literal_sample(seconds=min(20.0, 4.0 * args.steps + 4.0))
+    line = {"metric": METRIC, "value": sps, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded random DAG, 4n edges u<v)",
+            "config": {"workload": f"transitive-closure fixpoint n={N_CLOSURE}, mean out-degree {DEG_CLOSURE}",
+                       "n": N_CLOSURE},
+            "cpu_baseline": {"value": sps, "unit": UNIT, "cores": 1, "kind": "port",
+                             "sample": f"literal x,z,y loop nest of one sweep on {rows_done} rows "
+                                       f"({secs:.1f} s), scaled by n rows per sweep"},
+            "e2e": {"value": sps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-einsum", action="store_true")
+    ap.add_argument("--cpu-sample-s", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+    if args.warmup < 3:
+        args.warmup = 3
+    import torch
+    world, rank, local = dist_env()
+    dist = Dist(world, rank, local)
+    torch.cuda.set_device(local)
+    peaks = load_peaks()
+    res = run_closure(args, dist, peaks)
+    einsum = None
+    cpu = None
+    if world == 1 and not args.no_einsum:
+        einsum = run_einsum_configs(args, peaks)
+    if rank == 0 and world == 1:
+        sps, rows_done, secs = literal_sample(seconds=args.cpu_sample_s)
+        cpu = {"value": sps, "unit": UNIT, "cores": 1, "kind": "port",
+               "sample": f"literal x,z,y loop nest of one sweep (oracle/, -O2) on {rows_done} rows "
+                         f"({secs:.1f} s), scaled by n rows per sweep; cores used 1 of {os.cpu_count()}"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms"] / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u32 bit rows (Boolean)",
+            "data": "synthetic (seeded random DAG, 4n distinct edges u<v)",
+            "config": {"workload": f"transitive-closure fixpoint n={N_CLOSURE}, mean out-degree {DEG_CLOSURE}",
+                       "n": N_CLOSURE, "edges": res["nnz"], "sweeps_per_step": res["sweeps"],
+                       "reach_pairs": res["reach_pairs"], "parallelism": f"rows cyclic over {world} GPU(s)",
+                       "l2": "256 MiB buffer written between timed steps"},
+            "gpu_launches": int(res["launches"]), "roofline": res["roofline"], "cpu_baseline": cpu,
+            "e2e": res["e2e"], "clocks": res["clocks"],
+        }
+        if einsum:
+            line["einsum"] = einsum
+        print(json.dumps(line))
+    dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

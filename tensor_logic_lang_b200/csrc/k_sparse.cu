@@ -1,0 +1,291 @@
+// Sparse and Boolean storages: CSR of `sparse` tensors, bit rows of 0/1
+// tensors, the Boolean closure sweeps of the fixpoint driver, and CSR SpMM
+// for message passing.
+//
+// Reference semantics:
+//   sparse decl dense view          src/codegen/llvm.zig:482-516
+//   recursive max= step(...) sweep  src/codegen/fixpoint.zig:167-297
+//     right form  R[x,z] max= step(R[x,y] E[y,z])   (C4 transitive closure)
+//     left form   R[x,y] max= step(E[x,z] R[z,y])   (examples/ancestor.tl)
+//   per-term relu message passing   src/codegen/einsum.zig:20-196, expr.zig:245-249
+//
+// Closure on bit rows.  With R in {0,1} and E >= 0, step(R[x,y] E[y,z]) is
+// R[x,y] AND (E[y,z] > 0), and `max=` is OR, so one sweep of the right form
+// over row x is R[x] |= OR_{y in R[x]} succ(y).  A warp keeps row x (n bits)
+// in shared memory and expands its set bits in ascending y, re-reading a
+// 32-word chunk until it is stable; bits a successor sets at higher indices
+// are expanded later in the same sweep.  This is the reference's in-place
+// (Gauss-Seidel) order restricted to one row, so on an edge set with u < v
+// a row closes in its first sweep and the second sweep only confirms, the
+// same two sweeps the reference takes; on any edge set the fixpoint reached
+// is the least one above the start, bit for bit.  A device-side changed word
+// records whether any row gained a bit.
+#include "tl_internal.h"
+
+namespace tl {
+namespace {
+
+__global__ void k_csr_to_dense(const int64_t* rowptr, const int32_t* colidx, const float* vals, int64_t rows,
+                               int64_t cols, float* out) {
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < rows;
+         r += (int64_t)gridDim.x * (blockDim.x / 32)) {
+        for (int64_t e = rowptr[r] + (threadIdx.x & 31); e < rowptr[r + 1]; e += 32)
+            out[r * cols + colidx[e]] = vals[e];
+    }
+}
+
+// Output row r takes source row r * stride + offset (a rank's cyclic rows of
+// a replicated source; stride 1, offset 0 otherwise).
+__global__ void k_csr_to_bits(const int64_t* rowptr, const int32_t* colidx, const float* vals, int64_t rows,
+                              int64_t words, uint32_t* bits, int64_t stride, int64_t offset) {
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < rows;
+         r += (int64_t)gridDim.x * (blockDim.x / 32)) {
+        const int64_t s = r * stride + offset;
+        for (int64_t e = rowptr[s] + (threadIdx.x & 31); e < rowptr[s + 1]; e += 32) {
+            if (vals[e] > 0.f) {   // step(E)
+                const int32_t c = colidx[e];
+                atomicOr(&bits[r * words + (c >> 5)], 1u << (c & 31));
+            }
+        }
+    }
+}
+
+__global__ void k_dense_to_bits(const float* in, int64_t rows, int64_t cols, int64_t words, uint32_t* bits) {
+    const int64_t total = rows * words;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / words, w = i % words;
+        uint32_t b = 0;
+        for (int j = 0; j < 32; ++j) {
+            const int64_t c = w * 32 + j;
+            if (c < cols && in[r * cols + c] > 0.f) b |= 1u << j;
+        }
+        bits[i] = b;
+    }
+}
+
+__global__ void k_bits_to_dense(const uint32_t* bits, int64_t rows, int64_t cols, int64_t words, float* out) {
+    const int64_t total = rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / cols, c = i % cols;
+        out[i] = (bits[r * words + (c >> 5)] >> (c & 31)) & 1u ? 1.f : 0.f;
+    }
+}
+
+// Right-form sweep.  One warp per local row; `row_of(i)` maps a local row to
+// its global index (rows are dealt cyclically across ranks).
+__global__ void __launch_bounds__(128) k_closure_right(uint32_t* R, int64_t local_rows, int64_t words, int64_t n,
+                                                       const int64_t* __restrict__ rowptr,
+                                                       const int32_t* __restrict__ colidx, int* changed) {
+    extern __shared__ uint32_t srow_all[];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    uint32_t* row = srow_all + (int64_t)wib * words;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + wib; r < local_rows; r += warps) {
+        uint32_t* grow = R + r * words;
+        for (int64_t w = lane; w < words; w += 32) row[w] = grow[w];
+        __syncwarp();
+        bool grew = false;
+        for (int64_t c0 = 0; c0 < words; c0 += 32) {
+            const int64_t w = c0 + lane;
+            uint32_t done = 0;
+            for (;;) {
+                const uint32_t cur = w < words ? row[w] : 0u;
+                uint32_t pend = cur & ~done;
+                if (__ballot_sync(0xffffffffu, pend != 0) == 0) break;
+                done |= pend;
+                while (pend) {
+                    const int b = __ffs(pend) - 1;
+                    pend &= pend - 1;
+                    const int64_t y = w * 32 + b;
+                    for (int64_t e = rowptr[y]; e < rowptr[y + 1]; ++e) {
+                        const int32_t z = colidx[e];
+                        const uint32_t bit = 1u << (z & 31);
+                        if (!(row[z >> 5] & bit)) {
+                            const uint32_t old = atomicOr(&row[z >> 5], bit);
+                            grew = grew || !(old & bit);
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        __syncwarp();
+        const bool any = __any_sync(0xffffffffu, grew);
+        if (any) {
+            for (int64_t w = lane; w < words; w += 32) grow[w] = row[w];
+            if (lane == 0) *changed = 1;
+        }
+        __syncwarp();
+    }
+    (void)n;
+}
+
+// Left-form sweep Rnew[x] = R[x] | OR_{z in succ(x)} R[z] from the previous
+// sweep's rows.  The reference sweeps x upward in place; on an edge set with
+// u < v every row it reads (z > x) has not been updated yet in that sweep,
+// so its sweep is exactly this Jacobi step and the sweep counts agree.
+__global__ void __launch_bounds__(256) k_closure_left(const uint32_t* __restrict__ R, uint32_t* __restrict__ Rnew,
+                                                      int64_t n, int64_t words, const int64_t* __restrict__ rowptr,
+                                                      const int32_t* __restrict__ colidx, int* changed) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t x = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); x < n; x += warps) {
+        bool grew = false;
+        for (int64_t w = lane; w < words; w += 32) {
+            const uint32_t cur = R[x * words + w];
+            uint32_t acc = cur;
+            for (int64_t e = rowptr[x]; e < rowptr[x + 1]; ++e) acc |= R[(int64_t)colidx[e] * words + w];
+            Rnew[x * words + w] = acc;
+            grew = grew || (acc != cur);
+        }
+        if (__any_sync(0xffffffffu, grew) && lane == 0) *changed = 1;
+    }
+}
+
+// out[v, :] (+)= sum_e vals[e] * P[col(e), :], one warp per row, 4 columns
+// per lane per step (128-bit loads of P rows).
+__global__ void __launch_bounds__(256) k_spmm(int64_t rows, const int64_t* __restrict__ rowptr,
+                                              const int32_t* __restrict__ colidx, const float* __restrict__ vals,
+                                              const float* __restrict__ P, int64_t ldp, int64_t f, float* out,
+                                              int64_t ldo, int beta, int col_world, int64_t col_local) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const bool vec = (f % 4) == 0 && (ldp % 4) == 0 && (ldo % 4) == 0 && (((uintptr_t)P | (uintptr_t)out) & 15) == 0;
+    for (int64_t v = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); v < rows; v += warps) {
+        const int64_t e0 = rowptr[v], e1 = rowptr[v + 1];
+        if (vec) {
+            for (int64_t j = lane * 4; j < f; j += 128) {
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int64_t e = e0; e < e1; ++e) {
+                    int64_t u = colidx[e];
+                    if (col_world > 1) u = (u % col_world) * col_local + u / col_world;
+                    const float a = vals[e];
+                    const float4 pv = __ldg(reinterpret_cast<const float4*>(P + u * ldp + j));
+                    acc.x = fmaf(a, pv.x, acc.x); acc.y = fmaf(a, pv.y, acc.y);
+                    acc.z = fmaf(a, pv.z, acc.z); acc.w = fmaf(a, pv.w, acc.w);
+                }
+                float4* op = reinterpret_cast<float4*>(out + v * ldo + j);
+                if (beta) { const float4 o = *op; acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w; }
+                *op = acc;
+            }
+        } else {
+            for (int64_t j = lane; j < f; j += 32) {
+                float acc = 0.f;
+                for (int64_t e = e0; e < e1; ++e) {
+                    int64_t u = colidx[e];
+                    if (col_world > 1) u = (u % col_world) * col_local + u / col_world;
+                    acc = fmaf(vals[e], P[u * ldp + j], acc);
+                }
+                float* op = out + v * ldo + j;
+                *op = beta ? *op + acc : acc;
+            }
+        }
+    }
+}
+
+unsigned grid_for(tl_ctx* c, int64_t items, int per_block) {
+    int64_t b = (items + per_block - 1) / per_block;
+    const int64_t cap = (int64_t)c->sm_count * 16;
+    if (b > cap) b = cap;
+    return (unsigned)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+tl_status launch_csr_to_dense(tl_ctx* c, Tensor* t) {
+    const int64_t rows = t->csr_rows;
+    TL_CK(c, cudaMemsetAsync(t->dense, 0, (size_t)rows * t->dims[1] * 4, c->stream));
+    if (t->nnz == 0) return TL_OK;
+    LaunchScope L(c, "csr_to_dense", (double)t->nnz * 12.0);
+    k_csr_to_dense<<<grid_for(c, rows, 8), 256, 0, c->stream>>>(t->rowptr, t->colidx, t->vals, rows, t->dims[1], t->dense);
+    return L.done();
+}
+
+tl_status launch_csr_to_bits(tl_ctx* c, Tensor* src, Tensor* dst) {
+    TL_TRY(alloc_bits_public(c, dst));
+    TL_CK(c, cudaMemsetAsync(dst->bits, 0, (size_t)dst->bits_rows * dst->bits_words * 4, c->stream));
+    if (src->nnz == 0) return TL_OK;
+    // a replicated source feeding a row-sharded destination: rank's cyclic rows
+    int64_t stride = 1, offset = 0;
+    if (src->csr_rows != dst->bits_rows) {
+        const bool dst_sharded = dst->shard == TL_SHARD_ROWS && c->world > 1;
+        if (!(dst_sharded && src->csr_rows == dst->dims[0]))
+            return fail(c, TL_ERR_INVALID, "csr/bit row mismatch");
+        stride = c->world;
+        offset = c->rank;
+    }
+    if (dst->bits_rows > 0 && (dst->bits_rows - 1) * stride + offset >= src->csr_rows)
+        return fail(c, TL_ERR_INVALID, "csr/bit row mapping out of range");
+    LaunchScope L(c, "csr_to_bits", (double)src->nnz * 12.0);
+    k_csr_to_bits<<<grid_for(c, dst->bits_rows, 8), 256, 0, c->stream>>>(src->rowptr, src->colidx, src->vals,
+                                                                          dst->bits_rows, dst->bits_words, dst->bits,
+                                                                          stride, offset);
+    return L.done();
+}
+
+tl_status launch_dense_to_bits(tl_ctx* c, Tensor* t) {
+    const int64_t rows = t->bits_rows;
+    LaunchScope L(c, "dense_to_bits", (double)rows * t->dims[1] * 4.0);
+    k_dense_to_bits<<<grid_for(c, rows * t->bits_words, 256), 256, 0, c->stream>>>(t->dense, rows, t->dims[1],
+                                                                                     t->bits_words, t->bits);
+    return L.done();
+}
+
+tl_status launch_bits_to_dense(tl_ctx* c, Tensor* t) {
+    const int64_t rows = t->bits_rows;
+    LaunchScope L(c, "bits_to_dense", (double)rows * t->dims[1] * 4.0);
+    k_bits_to_dense<<<grid_for(c, rows * t->dims[1], 256), 256, 0, c->stream>>>(t->bits, rows, t->dims[1],
+                                                                                  t->bits_words, t->dense);
+    return L.done();
+}
+
+tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed) {
+    const int64_t words = R->bits_words;
+    const int warps_per_block = 4;
+    const size_t smem = (size_t)warps_per_block * words * 4;
+    if (smem > 200 * 1024) return fail(c, TL_ERR_UNSUPPORTED, "closure rows of %lld bits exceed shared memory", (long long)R->dims[1]);
+    static size_t attr = 0;
+    if (smem > 48 * 1024 && smem > attr) {
+        TL_CK(c, cudaFuncSetAttribute(k_closure_right, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr = smem;
+    }
+    const int64_t rows = R->bits_rows;
+    // per sweep: read and write the local bit rows once, plus the CSR
+    const double bytes = (double)rows * words * 4.0 * 2.0 + (double)(E->csr_rows + 1) * 8.0 + (double)E->nnz * 4.0;
+    LaunchScope L(c, "closure_sweep", bytes, 0);
+    const int blocks_per_sm = (int)std::max<size_t>(1, std::min<size_t>(16, (200 * 1024) / std::max<size_t>(smem, 1)));
+    unsigned grid = (unsigned)std::min<int64_t>((rows + warps_per_block - 1) / warps_per_block,
+                                                (int64_t)c->sm_count * blocks_per_sm);
+    if (grid < 1) grid = 1;
+    k_closure_right<<<grid, 32 * warps_per_block, smem, c->stream>>>(R->bits, rows, words, R->dims[1], E->rowptr,
+                                                                     E->colidx, d_changed);
+    return L.done();
+}
+
+tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed) {
+    const int64_t n = R->dims[0], words = R->bits_words;
+    const size_t bytes = (size_t)n * words * 4;
+    void* ws = nullptr;
+    TL_TRY(workspace(c, bytes, &ws));
+    {
+        LaunchScope L(c, "closure_left_sweep", (double)E->nnz * words * 4.0 + (double)n * words * 8.0, 0);
+        k_closure_left<<<grid_for(c, n, 8), 256, 0, c->stream>>>(R->bits, (uint32_t*)ws, n, words, E->rowptr,
+                                                                 E->colidx, d_changed);
+        TL_TRY(L.done());
+    }
+    TL_CK(c, cudaMemcpyAsync(R->bits, ws, bytes, cudaMemcpyDeviceToDevice, c->stream));
+    return TL_OK;
+}
+
+tl_status launch_spmm(tl_ctx* c, int64_t rows, const int64_t* rowptr, const int32_t* colidx, const float* vals,
+                      const float* P, int64_t ldp, int64_t f, float* out, int64_t ldo, int beta, int relu_out,
+                      int col_world, int64_t col_local) {
+    (void)relu_out;
+    if (rows <= 0) return TL_OK;
+    LaunchScope L(c, "spmm_csr", 0, 0);
+    k_spmm<<<grid_for(c, rows, 8), 256, 0, c->stream>>>(rows, rowptr, colidx, vals, P, ldp, f, out, ldo, beta, col_world,
+                                                       col_local);
+    return L.done();
+}
+
+}  // namespace tl

@@ -1,0 +1,951 @@
+// Lowering of statements to kernels, the fixpoint driver and the program
+// schedule.
+//
+// Reference anchors (Zollicoff/tensor_logic_lang):
+//   LLVMCodegen.generate       src/codegen/llvm.zig:131-336
+//   genEquation                src/codegen/llvm.zig:357-459
+//   collectExprIndices         src/codegen/expr.zig:303-359
+//   genEinsumLoops / accum     src/codegen/einsum.zig:20-278
+//   genSoftmax / genLayerNorm  src/codegen/softmax.zig:19-267, layernorm.zig:25-348
+//   genFixpointLoop            src/codegen/fixpoint.zig:21-297
+//   genSparseDecl              src/codegen/llvm.zig:482-516
+//   genSave / genLoad          src/codegen/llvm.zig:565-633 (paths without quotes)
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "tl_internal.h"
+
+using namespace tl;
+
+namespace {
+
+// ----------------------------------------------------------------------------
+// Index analysis (llvm.zig:383-455)
+// ----------------------------------------------------------------------------
+struct Var {
+    std::string name;
+    int64_t size;
+    bool contracted;
+};
+
+struct Analysis {
+    std::vector<Var> vars;       // free (LHS order) then contracted
+    int n_free = 0;
+    bool has_contraction = false;
+    bool scalar = false;         // no index at all → genScalarAssign
+    // LHS address terms: (var, divisor) paired with strides in emission order
+    int n_lhs_terms = 0;
+    int lhs_var[TL_MAX_RANK];
+    int64_t lhs_div[TL_MAX_RANK];
+    int64_t avg_div = 1;
+};
+
+std::string primed(const char* n) { return std::string(n) + "'"; }
+
+int var_index(const std::vector<Var>& v, const std::string& n) {
+    for (size_t i = 0; i < v.size(); ++i) if (v[i].name == n) return (int)i;
+    return -1;
+}
+
+// collectExprIndices: RHS index variables in expression order.
+void collect_rhs(tl_ctx* c, const tl_equation* eq, std::vector<Var>& all) {
+    for (int r = 0; r < eq->n_refs; ++r) {
+        const tl_ref* ref = &eq->refs[r];
+        for (int k = 0; k < ref->rank; ++k) {
+            const tl_index* ix = &ref->idx[k];
+            std::string nm;
+            int64_t size;
+            switch (ix->kind) {
+            case TL_IX_NAME: case TL_IX_ADD: case TL_IX_SUB: case TL_IX_DIV:
+                nm = ix->name; size = domain_size(c, ix->name); break;
+            case TL_IX_PRIMED: nm = primed(ix->name); size = domain_size(c, ix->name); break;
+            case TL_IX_SLICE: {
+                char b[64];
+                snprintf(b, sizeof b, "_slice_%lld_%lld", (long long)ix->value, (long long)ix->value2);
+                nm = b;
+                size = ix->value2 > ix->value ? ix->value2 - ix->value : 1;
+                break;
+            }
+            default: continue;
+            }
+            int at = var_index(all, nm);
+            if (at < 0) all.push_back({nm, size, false});
+            else all[at].size = size;
+        }
+    }
+}
+
+tl_status analyze(tl_ctx* c, const tl_equation* eq, bool recursive, Analysis* a) {
+    std::vector<Var> all;
+    std::vector<std::string> lhs_set;
+    for (int k = 0; k < eq->lhs.rank; ++k) {
+        const tl_index* ix = &eq->lhs.idx[k];
+        std::string nm;
+        bool ok = ix->kind == TL_IX_NAME || ix->kind == TL_IX_NORMALIZE;
+        if (!recursive) ok = ok || ix->kind == TL_IX_DIV || ix->kind == TL_IX_PRIMED;
+        if (!ok) continue;
+        nm = ix->kind == TL_IX_PRIMED ? primed(ix->name) : std::string(ix->name);
+        lhs_set.push_back(nm);
+        int at = var_index(all, nm);
+        if (at < 0) all.push_back({nm, domain_size(c, ix->name), false});
+        else all[at].size = domain_size(c, ix->name);
+    }
+    collect_rhs(c, eq, all);
+    if (all.empty()) { a->scalar = true; return TL_OK; }
+    // free variables: LHS order (the fixpoint also loops the normalize index)
+    for (int k = 0; k < eq->lhs.rank; ++k) {
+        const tl_index* ix = &eq->lhs.idx[k];
+        std::string nm;
+        if (ix->kind == TL_IX_NAME || ix->kind == TL_IX_DIV) nm = ix->name;
+        else if (ix->kind == TL_IX_PRIMED && !recursive) nm = primed(ix->name);
+        else if (ix->kind == TL_IX_NORMALIZE && recursive) nm = ix->name;
+        else continue;
+        if (recursive && ix->kind == TL_IX_DIV) continue;
+        if (var_index(a->vars, nm) >= 0 && recursive) continue;
+        int at = var_index(all, nm);
+        a->vars.push_back({nm, at >= 0 ? all[at].size : 10, false});
+    }
+    a->n_free = (int)a->vars.size();
+    for (auto& v : all) {
+        if (std::find(lhs_set.begin(), lhs_set.end(), v.name) != lhs_set.end()) continue;
+        a->vars.push_back({v.name, v.size, true});
+        a->has_contraction = true;
+    }
+    if ((int)a->vars.size() > kMaxVars)
+        return fail(c, TL_ERR_UNSUPPORTED, "%s: more than %d index variables", eq->lhs.tensor, kMaxVars);
+    // LHS address terms (einsum.zig:87-123; fixpoint.zig:212-225)
+    for (int k = 0; k < eq->lhs.rank; ++k) {
+        const tl_index* ix = &eq->lhs.idx[k];
+        std::string nm;
+        int64_t div = 1;
+        if (recursive) {
+            if (ix->kind != TL_IX_NAME && ix->kind != TL_IX_NORMALIZE) continue;
+            nm = ix->name;
+        } else if (ix->kind == TL_IX_NAME) nm = ix->name;
+        else if (ix->kind == TL_IX_PRIMED) nm = primed(ix->name);
+        else if (ix->kind == TL_IX_DIV) { nm = ix->name; div = ix->value; a->avg_div *= ix->value; }
+        else continue;
+        int at = var_index(a->vars, nm);
+        if (at < 0) continue;
+        if (div <= 0) return fail(c, TL_ERR_INVALID, "division index by %lld", (long long)div);
+        a->lhs_var[a->n_lhs_terms] = at;
+        a->lhs_div[a->n_lhs_terms++] = div;
+    }
+    return TL_OK;
+}
+
+// Every LHS element is addressed by exactly one free tuple.
+bool lhs_bijective(const Analysis& a, const Tensor* lhs) {
+    if (a.n_lhs_terms != lhs->rank || a.n_lhs_terms != a.n_free) return false;
+    bool seen[kMaxVars] = {false};
+    for (int t = 0; t < a.n_lhs_terms; ++t) {
+        int v = a.lhs_var[t];
+        if (seen[v] || a.lhs_div[t] != 1 || a.vars[v].size != lhs->dims[t]) return false;
+        seen[v] = true;
+    }
+    return true;
+}
+
+// One thread per LHS element is safe (no two tuples share an element).
+bool lhs_injective(const Analysis& a, const Tensor* lhs) {
+    bool seen[kMaxVars] = {false};
+    int covered = 0;
+    for (int t = 0; t < a.n_lhs_terms && t < lhs->rank; ++t) {
+        int v = a.lhs_var[t];
+        if (seen[v] || a.lhs_div[t] != 1 || a.vars[v].size > lhs->dims[t]) return false;
+        seen[v] = true;
+        covered++;
+    }
+    return covered == a.n_free;
+}
+
+// ----------------------------------------------------------------------------
+// Generic per-term loop nest on the GPU (einsum.zig:20-254 semantics)
+// ----------------------------------------------------------------------------
+tl_status build_refs(tl_ctx* c, const tl_equation* eq, const Analysis& a, GenericPlan* p) {
+    p->n_refs = eq->n_refs;
+    p->virt_pos_var = a.vars.empty() ? -1 : 0;
+    for (int r = 0; r < eq->n_refs; ++r) {
+        const tl_ref* ref = &eq->refs[r];
+        RefPlan& rp = p->refs[r];
+        memset(&rp, 0, sizeof rp);
+        Tensor* t = find_defined(c, ref->tensor);
+        tl_status st;
+        if (t && t->shard == TL_SHARD_ROWS && c->world > 1)
+            return fail(c, TL_ERR_UNSUPPORTED, "%s: row-sharded tensor in a generic equation", ref->tensor);
+        rp.ptr = read_ptr(c, t, &st);
+        TL_TRY(st);
+        rp.total = t ? t->total : 0;
+        int nidx = t ? std::min(ref->rank, t->rank) : 0;
+        rp.nidx = nidx;
+        for (int k = 0; k < nidx; ++k) {
+            const tl_index* ix = &ref->idx[k];
+            rp.kind[k] = ix->kind;
+            rp.val[k] = ix->value;
+            rp.stride[k] = t->strides[k];
+            rp.var[k] = -1;
+            switch (ix->kind) {
+            case TL_IX_NAME: case TL_IX_ADD: case TL_IX_SUB: case TL_IX_DIV:
+                rp.var[k] = var_index(a.vars, ix->name);
+                if (ix->kind == TL_IX_DIV && ix->value <= 0) return fail(c, TL_ERR_INVALID, "division index by 0");
+                break;
+            case TL_IX_PRIMED: rp.var[k] = var_index(a.vars, primed(ix->name)); break;
+            case TL_IX_VIRTUAL: {
+                Tensor* vt = find_defined(c, ix->name);
+                rp.virt[k] = read_ptr(c, vt, &st);
+                TL_TRY(st);
+                rp.virt_total[k] = vt ? vt->total : 0;
+                break;
+            }
+            default: break;
+            }
+        }
+    }
+    p->n_code = eq->n_code;
+    for (int i = 0; i < eq->n_code; ++i) {
+        p->code[i].op = eq->code[i].op;
+        p->code[i].arg = eq->code[i].arg;
+        p->code[i].arg2 = eq->code[i].arg2;
+        p->code[i].value = eq->code[i].value;
+    }
+    return TL_OK;
+}
+
+tl_status validate_code(tl_ctx* c, const tl_equation* eq) {
+    if (eq->n_refs < 0 || eq->n_refs > TL_MAX_REFS || eq->n_code < 0 || eq->n_code > TL_MAX_CODE ||
+        eq->lhs.rank < 0 || eq->lhs.rank > TL_MAX_RANK)
+        return fail(c, TL_ERR_INVALID, "malformed equation descriptor");
+    int sp = 0;
+    for (int i = 0; i < eq->n_code; ++i) {
+        const tl_instr* in = &eq->code[i];
+        switch (in->op) {
+        case TL_OP_REF:
+            if (in->arg < 0 || in->arg >= eq->n_refs) return fail(c, TL_ERR_INVALID, "bad ref operand");
+            sp++; break;
+        case TL_OP_LIT: sp++; break;
+        case TL_OP_PROD:
+            if (in->arg < 1 || in->arg > sp) return fail(c, TL_ERR_INVALID, "bad product arity");
+            sp -= in->arg - 1; break;
+        case TL_OP_NEG: case TL_OP_NOT: case TL_OP_NL:
+            if (sp < 1) return fail(c, TL_ERR_INVALID, "stack underflow");
+            break;
+        default:
+            if (in->op < TL_OP_ADD || in->op > TL_OP_OR) return fail(c, TL_ERR_INVALID, "bad opcode %d", in->op);
+            if (sp < 2) return fail(c, TL_ERR_INVALID, "stack underflow");
+            sp--;
+        }
+        if (sp > 16) return fail(c, TL_ERR_UNSUPPORTED, "expression deeper than 16");
+    }
+    if (eq->n_code > 0 && sp != 1) return fail(c, TL_ERR_INVALID, "expression leaves %d values", sp);
+    for (int r = 0; r < eq->n_refs; ++r)
+        if (eq->refs[r].rank < 0 || eq->refs[r].rank > TL_MAX_RANK) return fail(c, TL_ERR_INVALID, "bad ref rank");
+    return TL_OK;
+}
+
+bool root_is_boolean(const tl_equation* eq) {
+    if (eq->n_code == 0) return false;
+    const tl_instr* r = &eq->code[eq->n_code - 1];
+    if (r->op == TL_OP_NL && r->arg == TL_NL_STEP) return true;
+    if (r->op >= TL_OP_GT && r->op <= TL_OP_NE) return true;
+    if (r->op == TL_OP_NOT) return true;
+    if (r->op == TL_OP_LIT) return r->value == 0.0 || r->value == 1.0;
+    return false;
+}
+
+// ----------------------------------------------------------------------------
+// Pattern: C[m,n] (+)= [relu] (A[.,.] B[.,.] [* or / literal])  → GEMM
+// ----------------------------------------------------------------------------
+struct GemmMatch {
+    int ref_a, ref_b;
+    float scale;
+    bool relu_term;
+};
+
+// Recognise REF a, REF b, [LIT s, MUL|DIV], PROD 2 [, NL relu] in any of the
+// forms the parser produces for `A B`, `A B / s`, `A (B * s)`, `relu(A B)`.
+bool match_product2(const tl_equation* eq, GemmMatch* m) {
+    const tl_instr* c = eq->code;
+    int n = eq->n_code;
+    m->relu_term = false;
+    m->scale = 1.0f;
+    if (n >= 1 && c[n - 1].op == TL_OP_NL && c[n - 1].arg == TL_NL_RELU) { m->relu_term = true; n--; }
+    if (eq->n_refs != 2) return false;
+    // REF a REF b PROD
+    if (n == 3 && c[0].op == TL_OP_REF && c[1].op == TL_OP_REF && c[2].op == TL_OP_PROD && c[2].arg == 2) {
+        m->ref_a = c[0].arg; m->ref_b = c[1].arg; return true;
+    }
+    // REF a REF b LIT s (MUL|DIV) PROD     — A (B op s)
+    if (n == 5 && c[0].op == TL_OP_REF && c[1].op == TL_OP_REF && c[2].op == TL_OP_LIT &&
+        (c[3].op == TL_OP_MUL || c[3].op == TL_OP_DIV) && c[4].op == TL_OP_PROD && c[4].arg == 2) {
+        if (c[3].op == TL_OP_DIV && c[2].value == 0.0) return false;
+        m->ref_a = c[0].arg; m->ref_b = c[1].arg;
+        m->scale = (float)(c[3].op == TL_OP_MUL ? c[2].value : 1.0 / c[2].value);
+        // (B / s) with s a power of two is exact in fp32, else rounding differs ≤ 1 ulp
+        return true;
+    }
+    // REF a LIT s (MUL|DIV) REF b PROD    — (A op s) B
+    if (n == 5 && c[0].op == TL_OP_REF && c[1].op == TL_OP_LIT && (c[2].op == TL_OP_MUL || c[2].op == TL_OP_DIV) &&
+        c[3].op == TL_OP_REF && c[4].op == TL_OP_PROD && c[4].arg == 2) {
+        if (c[2].op == TL_OP_DIV && c[1].value == 0.0) return false;
+        m->ref_a = c[0].arg; m->ref_b = c[3].arg;
+        m->scale = (float)(c[2].op == TL_OP_MUL ? c[1].value : 1.0 / c[1].value);
+        return true;
+    }
+    return false;
+}
+
+int ref_var(const tl_ref* r, int k, const Analysis& a) {
+    if (k >= r->rank || r->idx[k].kind != TL_IX_NAME) return -2;
+    return var_index(a.vars, r->idx[k].name);
+}
+
+// Tensor-shaped check: every index a plain name whose var size equals the dim.
+bool plain_2d(const tl_ref* r, const Tensor* t, const Analysis& a) {
+    if (!t || r->rank != 2 || t->rank != 2) return false;
+    for (int k = 0; k < 2; ++k) {
+        int v = ref_var(r, k, a);
+        if (v < 0 || a.vars[v].size != t->dims[k]) return false;
+    }
+    return true;
+}
+
+tl_status try_gemm(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* lhs, bool* done) {
+    *done = false;
+    if (eq->accum != TL_ACC_ASSIGN && eq->accum != TL_ACC_ADD) return TL_OK;
+    if (a.n_free != 2 || (int)a.vars.size() != 3 || !a.has_contraction) return TL_OK;
+    GemmMatch m;
+    if (!match_product2(eq, &m)) return TL_OK;
+    const tl_ref* ra = &eq->refs[m.ref_a];
+    const tl_ref* rb = &eq->refs[m.ref_b];
+    Tensor* ta = find_defined(c, ra->tensor);
+    Tensor* tb = find_defined(c, rb->tensor);
+    if (!lhs_bijective(a, lhs)) return TL_OK;
+    if (!plain_2d(ra, ta, a) || !plain_2d(rb, tb, a) || !plain_2d(&eq->lhs, lhs, a)) {
+        // an operand that was never defined reads 0.0: the product adds nothing
+        if ((!ta || !tb) && lhs_bijective(a, lhs)) {
+            // `=`/`+=` of zero terms leave the LHS as it was
+            *done = true;
+        }
+        return TL_OK;
+    }
+    for (Tensor* t : {ta, tb, lhs})
+        if (t->shard == TL_SHARD_ROWS && c->world > 1) return TL_OK;
+    const int vm = a.lhs_var[0], vn = a.lhs_var[1], vk = a.n_free;  // contracted var is last
+    // orient operands: A holds (m,k), B holds (k,n)
+    auto holds = [&](const tl_ref* r, int v1, int v2) {
+        int x = ref_var(r, 0, a), y = ref_var(r, 1, a);
+        return (x == v1 && y == v2) || (x == v2 && y == v1);
+    };
+    const tl_ref *rA = ra, *rB = rb;
+    Tensor *tA = ta, *tB = tb;
+    if (!(holds(rA, vm, vk) && holds(rB, vk, vn))) {
+        if (holds(rb, vm, vk) && holds(ra, vk, vn)) { std::swap(rA, rB); std::swap(tA, tB); }
+        else return TL_OK;
+    }
+    GemmPlan g;
+    memset(&g, 0, sizeof g);
+    g.M = a.vars[vm].size; g.N = a.vars[vn].size; g.K = a.vars[vk].size;
+    tl_status st;
+    g.A = read_ptr(c, tA, &st); TL_TRY(st);
+    g.B = read_ptr(c, tB, &st); TL_TRY(st);
+    if (!g.A || !g.B) { *done = true; return TL_OK; }  // a zero operand adds 0.0 terms
+    int am = ref_var(rA, 0, a) == vm ? 0 : 1;
+    g.sam = tA->strides[am]; g.sak = tA->strides[1 - am];
+    int bk = ref_var(rB, 0, a) == vk ? 0 : 1;
+    g.sbk = tB->strides[bk]; g.sbn = tB->strides[1 - bk];
+    g.scale = m.scale;
+    g.relu_term = m.relu_term ? 1 : 0;
+    g.beta = lhs->zero ? 0 : 1;
+    if (g.beta) TL_TRY(ensure_dense(c, lhs));
+    else TL_TRY(alloc_dense_public(c, lhs));
+    g.C = lhs->dense;
+    // LHS [m,n] or [n,m]
+    g.scm = lhs->strides[0]; g.scn = lhs->strides[1];
+    if (a.lhs_var[0] != vm) std::swap(g.scm, g.scn);
+    TL_TRY(launch_gemm(c, g));
+    mark_written_dense(lhs);
+    lhs->boolean = false;
+    *done = true;
+    return TL_OK;
+}
+
+// ----------------------------------------------------------------------------
+// Pattern: H[v,f] (+)= [relu] (S[v,u] X[u,g] W[g,f]) with S sparse, S >= 0
+//   → P = [relu-per-term] X·W  (dense GEMM), then H (+)= S · P  (CSR SpMM).
+// relu(s·x·w) = s·relu(x·w) for s >= 0, so the per-term relu moves inside P.
+// ----------------------------------------------------------------------------
+tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* lhs, bool* done) {
+    *done = false;
+    if (eq->accum != TL_ACC_ASSIGN && eq->accum != TL_ACC_ADD) return TL_OK;
+    if (eq->n_refs != 3 || a.n_free != 2 || (int)a.vars.size() != 4) return TL_OK;
+    const tl_instr* k = eq->code;
+    int n = eq->n_code;
+    bool relu = false;
+    if (n >= 1 && k[n - 1].op == TL_OP_NL && k[n - 1].arg == TL_NL_RELU) { relu = true; n--; }
+    if (!(n == 5 && k[0].op == TL_OP_REF && k[1].op == TL_OP_REF && k[2].op == TL_OP_PROD && k[2].arg == 2 &&
+          k[3].op == TL_OP_REF && k[4].op == TL_OP_PROD && k[4].arg == 2))
+        return TL_OK;
+    const tl_ref* rs = &eq->refs[k[0].arg];
+    const tl_ref* rx = &eq->refs[k[1].arg];
+    const tl_ref* rw = &eq->refs[k[3].arg];
+    Tensor* S = find_defined(c, rs->tensor);
+    Tensor* X = find_defined(c, rx->tensor);
+    Tensor* W = find_defined(c, rw->tensor);
+    if (!S || !X || !W || !S->csr_valid || !S->csr_nonneg) return TL_OK;
+    if (!lhs_bijective(a, lhs) || S->rank != 2 || X->rank != 2 || W->rank != 2 || lhs->rank != 2) return TL_OK;
+    int vv = a.lhs_var[0], vf = a.lhs_var[1];
+    // S[v,u], X[u,g], W[g,f] as plain names with matching sizes
+    int s0 = ref_var(rs, 0, a), s1 = ref_var(rs, 1, a);
+    int x0 = ref_var(rx, 0, a), x1 = ref_var(rx, 1, a);
+    int w0 = ref_var(rw, 0, a), w1 = ref_var(rw, 1, a);
+    if (s0 != vv || x0 != s1 || w0 != x1 || w1 != vf) return TL_OK;
+    if (s1 < a.n_free || x1 < a.n_free) return TL_OK;
+    if (S->dims[0] != a.vars[vv].size || S->dims[1] != a.vars[s1].size || X->dims[0] != a.vars[s1].size ||
+        X->dims[1] != a.vars[x1].size || W->dims[0] != a.vars[x1].size || W->dims[1] != a.vars[vf].size)
+        return TL_OK;
+    if (W->shard == TL_SHARD_ROWS && c->world > 1) return TL_OK;
+    bool sharded = c->world > 1 && X->shard == TL_SHARD_ROWS;
+    if (c->world > 1 && (S->shard == TL_SHARD_ROWS) != (lhs->shard == TL_SHARD_ROWS)) return TL_OK;
+    if (c->world > 1 && S->shard != TL_SHARD_ROWS && sharded) return TL_OK;
+    const int64_t nu = X->dims[0], g = X->dims[1], f = W->dims[1];
+    tl_status st;
+    const float* xp = read_ptr(c, X, &st); TL_TRY(st);
+    const float* wp = read_ptr(c, W, &st); TL_TRY(st);
+    int64_t lrows_x = X->local_rows(c->rank, c->world);
+    // P rows for the local u rows (all rows when X is replicated)
+    int64_t p_rows = sharded ? lrows_x : nu;
+    int64_t gathered_rows_per_rank = sharded ? (nu + c->world - 1) / c->world : 0;
+    size_t p_bytes = (size_t)p_rows * f * 4;
+    size_t pg_bytes = sharded ? (size_t)gathered_rows_per_rank * c->world * f * 4 : 0;
+    void* ws = nullptr;
+    TL_TRY(workspace(c, p_bytes + pg_bytes + (sharded ? (size_t)gathered_rows_per_rank * f * 4 : 0) + 256, &ws));
+    float* P = (float*)ws;
+    if (!xp || !wp) {
+        TL_CK(c, cudaMemsetAsync(P, 0, p_bytes, c->stream));
+    } else {
+        GemmPlan gp;
+        memset(&gp, 0, sizeof gp);
+        gp.M = p_rows; gp.N = f; gp.K = g;
+        gp.A = xp; gp.sam = g; gp.sak = 1;
+        gp.B = wp; gp.sbk = f; gp.sbn = 1;
+        gp.C = P; gp.scm = f; gp.scn = 1;
+        gp.scale = 1.0f; gp.beta = 0; gp.relu_term = relu ? 1 : 0;
+        if (p_rows > 0) TL_TRY(launch_gemm(c, gp));
+    }
+    const float* Pfull = P;
+    int col_world = 1;
+    int64_t col_local = 0;
+    if (sharded) {
+        // pad the local block to the per-rank row count, then all-gather
+        float* Ppad = (float*)((char*)ws + p_bytes);
+        float* Pg = Ppad + gathered_rows_per_rank * f;
+        if (p_rows > 0)
+            TL_CK(c, cudaMemcpyAsync(Ppad, P, p_bytes, cudaMemcpyDeviceToDevice, c->stream));
+        TL_TRY(comm_allgather(c, Ppad, Pg, (size_t)gathered_rows_per_rank * f * 4));
+        Pfull = Pg;
+        col_world = c->world;
+        col_local = gathered_rows_per_rank;
+    }
+    int beta = lhs->zero ? 0 : 1;
+    if (beta) TL_TRY(ensure_dense(c, lhs));
+    else TL_TRY(alloc_dense_public(c, lhs));
+    int64_t out_rows = lhs->local_rows(c->rank, c->world);
+    TL_TRY(launch_spmm(c, out_rows, S->rowptr, S->colidx, S->vals, Pfull, f, f, lhs->dense, f, beta, 0,
+                       col_world, col_local));
+    mark_written_dense(lhs);
+    lhs->boolean = false;
+    *done = true;
+    return TL_OK;
+}
+
+// ----------------------------------------------------------------------------
+// Pattern: R[x,y] = step(E[x,y]) with E sparse → bit rows of R
+// ----------------------------------------------------------------------------
+tl_status try_step_bits(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* lhs, bool* done) {
+    *done = false;
+    if (eq->accum != TL_ACC_ASSIGN || a.has_contraction || eq->n_refs != 1 || eq->n_code != 2) return TL_OK;
+    if (!(eq->code[0].op == TL_OP_REF && eq->code[1].op == TL_OP_NL && eq->code[1].arg == TL_NL_STEP)) return TL_OK;
+    Tensor* E = find_defined(c, eq->refs[0].tensor);
+    if (!E || !E->csr_valid || lhs->rank != 2 || E->rank != 2) return TL_OK;
+    if (!lhs_bijective(a, lhs) || !plain_2d(&eq->refs[0], E, a)) return TL_OK;
+    if (ref_var(&eq->refs[0], 0, a) != a.lhs_var[0] || ref_var(&eq->refs[0], 1, a) != a.lhs_var[1]) return TL_OK;
+    if (E->dims[0] != lhs->dims[0] || E->dims[1] != lhs->dims[1]) return TL_OK;
+    // a sharded source needs a sharded destination; a replicated one feeds either
+    if (c->world > 1 && E->shard == TL_SHARD_ROWS && lhs->shard != TL_SHARD_ROWS) return TL_OK;
+    TL_TRY(launch_csr_to_bits(c, E, lhs));
+    mark_written_bits(lhs);
+    *done = true;
+    return TL_OK;
+}
+
+// ----------------------------------------------------------------------------
+// Row-wise softmax / lnorm (softmax.zig:19-229, layernorm.zig:25-310)
+// ----------------------------------------------------------------------------
+tl_status run_rowwise(tl_ctx* c, const tl_equation* eq, bool lnorm) {
+    if (eq->n_code != 2 || eq->code[0].op != TL_OP_REF) return TL_OK;  // F3: comment and return
+    int norm_axis = -1;
+    for (int k = 0; k < eq->lhs.rank; ++k)
+        if (eq->lhs.idx[k].kind == TL_IX_NORMALIZE) { norm_axis = k; break; }
+    if (norm_axis < 0 && eq->lhs.rank > 0) norm_axis = eq->lhs.rank - 1;
+    Tensor* out = find_defined(c, eq->lhs.tensor);
+    if (!out) TL_TRY(allocate_tensor(c, eq->lhs.tensor, eq->lhs.idx, eq->lhs.rank, &out));
+    Tensor* in = find_defined(c, eq->refs[0].tensor);
+    if (!in) return TL_OK;
+    if ((in->shard == TL_SHARD_ROWS || out->shard == TL_SHARD_ROWS) && c->world > 1)
+        return fail(c, TL_ERR_UNSUPPORTED, "row-wise op on a sharded tensor");
+    RowPlan p;
+    memset(&p, 0, sizeof p);
+    std::vector<std::string> outer_names;
+    int64_t norm_size = 1;
+    for (int k = 0; k < eq->lhs.rank; ++k) {
+        const tl_index* ix = &eq->lhs.idx[k];
+        if (ix->kind != TL_IX_NAME && ix->kind != TL_IX_NORMALIZE) continue;
+        int64_t s = domain_size(c, ix->name);
+        if (k == norm_axis) norm_size = s;
+        else {
+            // repeated outer names share one loop variable
+            if (std::find(outer_names.begin(), outer_names.end(), std::string(ix->name)) != outer_names.end()) continue;
+            outer_names.push_back(ix->name);
+            p.outer_size[p.n_outer++] = s;
+        }
+    }
+    for (int k = 0; k < eq->lhs.rank; ++k) {
+        const tl_index* ix = &eq->lhs.idx[k];
+        if (ix->kind != TL_IX_NAME && ix->kind != TL_IX_NORMALIZE) continue;
+        int64_t si = k < in->rank ? in->strides[k] : 0;
+        int64_t so = k < out->rank ? out->strides[k] : 0;
+        if (k == norm_axis) { p.in_sn += si; p.out_sn += so; continue; }
+        int o = (int)(std::find(outer_names.begin(), outer_names.end(), std::string(ix->name)) - outer_names.begin());
+        p.outer_in_stride[o] += si;
+        p.outer_out_stride[o] += so;
+    }
+    p.rows = 1;
+    for (int o = 0; o < p.n_outer; ++o) p.rows *= p.outer_size[o];
+    p.len = norm_size;
+    tl_status st;
+    (void)st;
+    TL_TRY(ensure_dense(c, in));
+    p.in = in->dense;
+    // every output element is written exactly once when the row set tiles it
+    TL_TRY(ensure_dense(c, out));
+    p.out = out->dense;
+    p.in_total = in->total;
+    p.out_total = out->total;
+    p.lnorm = lnorm ? 1 : 0;
+    if (p.rows > 0 && p.len > 0) TL_TRY(launch_rowwise(c, p));
+    mark_written_dense(out);
+    out->boolean = false;
+    return TL_OK;
+}
+
+}  // namespace
+
+namespace tl {
+static tl_status alloc_dense_impl(tl_ctx* c, Tensor* t);
+tl_status alloc_dense_public(tl_ctx* c, Tensor* t) { return alloc_dense_impl(c, t); }
+static tl_status alloc_dense_impl(tl_ctx* c, Tensor* t) {
+    // dense storage without defining its contents (the caller writes all of it)
+    int64_t need = t->local_rows(c->rank, c->world) * (t->rank >= 1 && t->dims[0] > 0 ? t->total / t->dims[0] : 1);
+    if (t->shard != TL_SHARD_ROWS || c->world <= 1) need = t->total;
+    if (t->dense && t->dense_elems >= need) return TL_OK;
+    cudaFree(t->dense);
+    t->dense = nullptr;
+    TL_CK(c, cudaMalloc(&t->dense, std::max<int64_t>(need, 1) * sizeof(float)));
+    t->dense_elems = need;
+    return TL_OK;
+}
+}  // namespace tl
+
+// ============================================================================
+// genEquation (llvm.zig:357-459)
+// ============================================================================
+static tl_status run_equation(tl_ctx* c, const tl_equation* eq) {
+    TL_TRY(validate_code(c, eq));
+    if (eq->n_code > 0 && eq->code[eq->n_code - 1].op == TL_OP_NL) {
+        int f = eq->code[eq->n_code - 1].arg;
+        if (f == TL_NL_SOFTMAX) return run_rowwise(c, eq, false);
+        if (f == TL_NL_LNORM) return run_rowwise(c, eq, true);
+        if (f == TL_NL_CONCAT) return fail(c, TL_ERR_UNSUPPORTED, "concat is not lowered");
+    }
+    Tensor* lhs = find_defined(c, eq->lhs.tensor);
+    if (!lhs) TL_TRY(allocate_tensor(c, eq->lhs.tensor, eq->lhs.idx, eq->lhs.rank, &lhs));
+    Analysis a;
+    TL_TRY(analyze(c, eq, false, &a));
+
+    GenericPlan* p = new GenericPlan();
+    std::unique_ptr<GenericPlan> hold(p);
+    memset(p, 0, sizeof *p);
+    if (a.scalar) {
+        // genScalarAssign (einsum.zig:257-278): constant indices only
+        if (lhs->shard == TL_SHARD_ROWS && c->world > 1) return fail(c, TL_ERR_UNSUPPORTED, "scalar store into a sharded tensor");
+        int64_t off = 0;
+        for (int k = 0; k < eq->lhs.rank && k < lhs->rank; ++k)
+            off += (eq->lhs.idx[k].kind == TL_IX_CONST ? eq->lhs.idx[k].value : 0) * lhs->strides[k];
+        TL_TRY(build_refs(c, eq, a, p));
+        TL_TRY(ensure_dense(c, lhs));
+        bool was_bool = lhs->boolean;
+        if (off >= 0 && off < lhs->total) TL_TRY(launch_set1(c, lhs->dense, off, *p));
+        mark_written_dense(lhs);
+        lhs->boolean = was_bool && root_is_boolean(eq);
+        return TL_OK;
+    }
+    if (lhs->shard == TL_SHARD_ROWS && c->world > 1) {
+        bool done = false;
+        TL_TRY(try_sparse_chain(c, eq, a, lhs, &done));
+        if (!done) TL_TRY(try_step_bits(c, eq, a, lhs, &done));
+        if (!done) {
+            // fill of a sharded input before its load: `X[u,g] = 0`
+            if (eq->n_code == 1 && eq->code[0].op == TL_OP_LIT && eq->code[0].value == 0.0 && !a.has_contraction &&
+                eq->accum == TL_ACC_ASSIGN) {
+                lhs->zero = true;
+                lhs->dense_valid = lhs->bits_valid = lhs->csr_valid = false;
+                return TL_OK;
+            }
+            return fail(c, TL_ERR_UNSUPPORTED, "%s: equation on a row-sharded tensor is not lowered", eq->lhs.tensor);
+        }
+        return TL_OK;
+    }
+    // constant fill of the whole tensor: `X[b,i] = 0` (kept lazy when zero)
+    if (eq->n_code == 1 && eq->code[0].op == TL_OP_LIT && !a.has_contraction && eq->accum == TL_ACC_ASSIGN &&
+        lhs_bijective(a, lhs)) {
+        double v = eq->code[0].value;
+        if (v == 0.0) {
+            lhs->zero = true;
+            lhs->boolean = true;
+            lhs->dense_valid = lhs->bits_valid = lhs->csr_valid = lhs->csc_valid = false;
+            return TL_OK;
+        }
+        TL_TRY(alloc_dense_public(c, lhs));
+        TL_TRY(launch_fill(c, lhs->dense, lhs->total, (float)v));
+        mark_written_dense(lhs);
+        lhs->boolean = v == 1.0;
+        return TL_OK;
+    }
+    bool done = false;
+    TL_TRY(try_gemm(c, eq, a, lhs, &done));
+    if (!done) TL_TRY(try_sparse_chain(c, eq, a, lhs, &done));
+    if (!done) TL_TRY(try_step_bits(c, eq, a, lhs, &done));
+    if (done) return TL_OK;
+
+    // generic loop nest
+    TL_TRY(build_refs(c, eq, a, p));
+    p->n_vars = (int)a.vars.size();
+    p->n_free = a.n_free;
+    p->n_out = 1;
+    p->n_inner = 1;
+    for (int i = 0; i < p->n_vars; ++i) {
+        p->sizes[i] = a.vars[i].size;
+        if (i < a.n_free) p->n_out *= a.vars[i].size;
+        else p->n_inner *= a.vars[i].size;
+    }
+    bool bij = lhs_bijective(a, lhs);
+    bool inj = lhs_injective(a, lhs);
+    bool was_zero = lhs->zero;
+    bool was_bool = lhs->boolean;
+    if (bij && was_zero) {
+        TL_TRY(alloc_dense_public(c, lhs));
+        p->old_zero = 1;
+    } else {
+        TL_TRY(ensure_dense(c, lhs));
+        p->old_zero = 0;
+    }
+    p->lhs = lhs->dense;
+    p->lhs_total = lhs->total;
+    p->n_lhs_terms = std::min(a.n_lhs_terms, lhs->rank);
+    for (int t = 0; t < p->n_lhs_terms; ++t) {
+        p->lhs_var[t] = a.lhs_var[t];
+        p->lhs_div[t] = a.lhs_div[t];
+        p->lhs_stride[t] = lhs->strides[t];
+    }
+    p->accum = eq->accum;
+    p->has_contraction = a.has_contraction ? 1 : 0;
+    p->atomic = inj ? 0 : 1;
+    p->recursive = 0;
+    if (p->n_out > 0 && p->n_inner > 0) TL_TRY(launch_generic(c, *p, nullptr));
+    // avg= divides the whole LHS by the product of its divisors (einsum.zig:151-195)
+    if (eq->accum == TL_ACC_AVG && a.avg_div > 1) {
+        GenericPlan* d = new GenericPlan();
+        std::unique_ptr<GenericPlan> hd(d);
+        memset(d, 0, sizeof *d);
+        d->n_vars = 1; d->n_free = 1; d->sizes[0] = lhs->total; d->n_out = lhs->total; d->n_inner = 1;
+        d->n_refs = 1;
+        d->refs[0].ptr = lhs->dense; d->refs[0].total = lhs->total; d->refs[0].nidx = 1;
+        d->refs[0].kind[0] = TL_IX_NAME; d->refs[0].var[0] = 0; d->refs[0].stride[0] = 1;
+        d->n_code = 3;
+        d->code[0] = {TL_OP_REF, 0, 0, 0, 0.0};
+        d->code[1] = {TL_OP_LIT, 0, 0, 0, (double)a.avg_div};
+        d->code[2] = {TL_OP_DIV, 0, 0, 0, 0.0};
+        d->lhs = lhs->dense; d->lhs_total = lhs->total; d->n_lhs_terms = 1;
+        d->lhs_var[0] = 0; d->lhs_div[0] = 1; d->lhs_stride[0] = 1;
+        d->accum = TL_ACC_ASSIGN;
+        if (lhs->total > 0) TL_TRY(launch_generic(c, *d, nullptr));
+    }
+    mark_written_dense(lhs);
+    bool b = root_is_boolean(eq);
+    if (eq->accum == TL_ACC_MAX || eq->accum == TL_ACC_MIN) b = b && (was_bool || was_zero);
+    else if (eq->accum != TL_ACC_ASSIGN || a.has_contraction) b = false;
+    else if (!bij) b = b && was_bool;
+    lhs->boolean = b;
+    return TL_OK;
+}
+
+extern "C" tl_status tl_equation_run(tl_ctx* c, const tl_equation* eq) {
+    if (!c || !eq) return TL_ERR_INVALID;
+    TL_CK(c, cudaSetDevice(c->device));
+    return run_equation(c, eq);
+}
+
+// ============================================================================
+// Fixpoint (fixpoint.zig:46-297)
+// ============================================================================
+static bool is_recursive(const tl_equation* eq) {
+    for (int r = 0; r < eq->n_refs; ++r)
+        if (strcmp(eq->refs[r].tensor, eq->lhs.tensor) == 0) return true;
+    return false;
+}
+
+enum ClosureForm { NOT_CLOSURE = 0, CLOSURE_RIGHT, CLOSURE_LEFT };
+
+// R[x,z] max= step(R[x,y] E[y,z])   → right form (rows of R are independent)
+// R[x,y] max= step(E[x,z] R[z,y])   → left form  (row x reads rows z of R)
+static ClosureForm match_closure(tl_ctx* c, const tl_equation* eq, Tensor** Rout, Tensor** Eout) {
+    if (eq->accum != TL_ACC_MAX || eq->n_refs != 2 || eq->n_code != 4) return NOT_CLOSURE;
+    const tl_instr* k = eq->code;
+    if (!(k[0].op == TL_OP_REF && k[1].op == TL_OP_REF && k[2].op == TL_OP_PROD && k[2].arg == 2 &&
+          k[3].op == TL_OP_NL && k[3].arg == TL_NL_STEP))
+        return NOT_CLOSURE;
+    const tl_ref* r0 = &eq->refs[k[0].arg];
+    const tl_ref* r1 = &eq->refs[k[1].arg];
+    const tl_ref* L = &eq->lhs;
+    if (L->rank != 2 || r0->rank != 2 || r1->rank != 2) return NOT_CLOSURE;
+    for (const tl_ref* r : {L, r0, r1})
+        for (int i = 0; i < 2; ++i) if (r->idx[i].kind != TL_IX_NAME) return NOT_CLOSURE;
+    auto nm = [](const tl_ref* r, int i) { return std::string(r->idx[i].name); };
+    std::string x = nm(L, 0), z = nm(L, 1);
+    if (x == z) return NOT_CLOSURE;
+    ClosureForm form = NOT_CLOSURE;
+    const tl_ref* er = nullptr;
+    // right: R[x,y] E[y,z]
+    if (!strcmp(r0->tensor, L->tensor) && strcmp(r1->tensor, L->tensor) && nm(r0, 0) == x && nm(r1, 1) == z &&
+        nm(r0, 1) == nm(r1, 0) && nm(r0, 1) != x && nm(r0, 1) != z) {
+        form = CLOSURE_RIGHT; er = r1;
+    }
+    // left: E[x,y] R[y,z]
+    if (!strcmp(r1->tensor, L->tensor) && strcmp(r0->tensor, L->tensor) && nm(r0, 0) == x && nm(r1, 1) == z &&
+        nm(r0, 1) == nm(r1, 0) && nm(r0, 1) != x && nm(r0, 1) != z) {
+        form = CLOSURE_LEFT; er = r0;
+    }
+    if (form == NOT_CLOSURE) return NOT_CLOSURE;
+    Tensor* R = find_defined(c, L->tensor);
+    Tensor* E = find_defined(c, er->tensor);
+    if (!R || !E || R->rank != 2 || E->rank != 2) return NOT_CLOSURE;
+    int64_t n = R->dims[0];
+    std::string y = nm(r0, 1);
+    if (R->dims[1] != n || E->dims[0] != n || E->dims[1] != n) return NOT_CLOSURE;
+    if (domain_size(c, x.c_str()) != n || domain_size(c, z.c_str()) != n || domain_size(c, y.c_str()) != n)
+        return NOT_CLOSURE;
+    if (!R->boolean) return NOT_CLOSURE;
+    // step(r * e) == (r > 0) && (e > 0) needs e >= 0 (r is 0/1)
+    if (!(E->csr_valid ? E->csr_nonneg : E->boolean)) return NOT_CLOSURE;
+    // the sweeps read successor lists of every row: the relation is replicated
+    if (E->csr_valid && E->csr_rows != n) return NOT_CLOSURE;
+    if (form == CLOSURE_LEFT && R->shard == TL_SHARD_ROWS && c->world > 1) return NOT_CLOSURE;
+    *Rout = R;
+    *Eout = E;
+    return form;
+}
+
+static tl_status generic_recursive(tl_ctx* c, const tl_equation* eq, int* d_changed) {
+    Tensor* lhs = find_defined(c, eq->lhs.tensor);
+    if (!lhs) TL_TRY(allocate_tensor(c, eq->lhs.tensor, eq->lhs.idx, eq->lhs.rank, &lhs));
+    if (lhs->shard == TL_SHARD_ROWS && c->world > 1)
+        return fail(c, TL_ERR_UNSUPPORTED, "%s: recursive equation on a sharded tensor", eq->lhs.tensor);
+    Analysis a;
+    TL_TRY(analyze(c, eq, true, &a));
+    if (a.scalar) return TL_OK;
+    GenericPlan* p = new GenericPlan();
+    std::unique_ptr<GenericPlan> hold(p);
+    memset(p, 0, sizeof *p);
+    TL_TRY(ensure_dense(c, lhs));
+    mark_written_dense(lhs);
+    TL_TRY(build_refs(c, eq, a, p));
+    p->n_vars = (int)a.vars.size();
+    p->n_free = a.n_free;
+    p->n_out = 1; p->n_inner = 1;
+    for (int i = 0; i < p->n_vars; ++i) {
+        p->sizes[i] = a.vars[i].size;
+        if (i < a.n_free) p->n_out *= a.vars[i].size; else p->n_inner *= a.vars[i].size;
+    }
+    p->lhs = lhs->dense;
+    p->lhs_total = lhs->total;
+    p->n_lhs_terms = std::min(a.n_lhs_terms, lhs->rank);
+    for (int t = 0; t < p->n_lhs_terms; ++t) {
+        p->lhs_var[t] = a.lhs_var[t]; p->lhs_div[t] = 1; p->lhs_stride[t] = lhs->strides[t];
+    }
+    p->accum = eq->accum;
+    p->has_contraction = a.has_contraction;
+    p->atomic = lhs_injective(a, lhs) ? 0 : 1;
+    p->recursive = 1;
+    bool was_bool = lhs->boolean;
+    if (p->n_out > 0 && p->n_inner > 0) TL_TRY(launch_generic(c, *p, d_changed));
+    lhs->boolean = was_bool && eq->accum == TL_ACC_MAX && root_is_boolean(eq);
+    return TL_OK;
+}
+
+static tl_status run_fixpoint(tl_ctx* c, const tl_equation* eqs, int n, int32_t* sweeps_out) {
+    for (int i = 0; i < n; ++i) TL_TRY(validate_code(c, &eqs[i]));
+    // allocate every recursive LHS first (genRecursiveEquation, fixpoint.zig:103-106)
+    for (int i = 0; i < n; ++i) {
+        Tensor* t = find_defined(c, eqs[i].lhs.tensor);
+        if (!t) TL_TRY(allocate_tensor(c, eqs[i].lhs.tensor, eqs[i].lhs.idx, eqs[i].lhs.rank, &t));
+    }
+    int max_sweeps = c->opts.max_sweeps > 0 ? c->opts.max_sweeps : 1000;
+    int* d_changed = c->d_flags;   // word 0: changed this sweep
+    int sweeps = 0;
+    bool changed = true;
+    // a single closure equation runs on bit rows
+    Tensor *R = nullptr, *E = nullptr;
+    ClosureForm form = n == 1 ? match_closure(c, &eqs[0], &R, &E) : NOT_CLOSURE;
+    // the bit-row sweeps read the relation's successor lists (CSR)
+    if (form != NOT_CLOSURE && !E->csr_valid) form = NOT_CLOSURE;
+    if (form != NOT_CLOSURE) TL_TRY(ensure_bits(c, R));
+    while (sweeps < max_sweeps && changed) {
+        TL_CK(c, cudaMemsetAsync(d_changed, 0, sizeof(int), c->stream));
+        if (form == CLOSURE_RIGHT) TL_TRY(launch_closure_right(c, R, E, d_changed));
+        else if (form == CLOSURE_LEFT) TL_TRY(launch_closure_left(c, R, E, d_changed));
+        else for (int i = 0; i < n; ++i) TL_TRY(generic_recursive(c, &eqs[i], d_changed));
+        if (c->world > 1) TL_TRY(comm_allreduce_max_int(c, d_changed, 1));
+        TL_CK(c, cudaMemcpyAsync(c->h_flags, d_changed, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+        TL_CK(c, cudaStreamSynchronize(c->stream));
+        changed = c->h_flags[0] != 0;
+        sweeps++;
+    }
+    if (form != NOT_CLOSURE) mark_written_bits(R);
+    c->last_sweeps = sweeps;
+    if (sweeps_out) *sweeps_out = sweeps;
+    if (changed) fail(c, TL_OK, "fixpoint stopped at the %d-sweep cap", sweeps);
+    return TL_OK;
+}
+
+extern "C" tl_status tl_fixpoint(tl_ctx* c, const tl_equation* eqs, int32_t n, int32_t* sweeps_out) {
+    if (!c || (n > 0 && !eqs)) return TL_ERR_INVALID;
+    TL_CK(c, cudaSetDevice(c->device));
+    return run_fixpoint(c, eqs, n, sweeps_out);
+}
+
+// ============================================================================
+// sparse declaration, save / load, program schedule
+// ============================================================================
+extern "C" tl_status tl_sparse_decl(tl_ctx* c, const tl_ref* decl) {
+    if (!c || !decl || decl->rank < 0 || decl->rank > TL_MAX_RANK) return TL_ERR_INVALID;
+    tl_index idx[TL_MAX_RANK];
+    for (int k = 0; k < decl->rank; ++k) {
+        memset(&idx[k], 0, sizeof idx[k]);
+        idx[k].kind = TL_IX_NAME;
+        snprintf(idx[k].name, TL_NAME_LEN, "%s", decl->idx[k].name);
+    }
+    Tensor* t;
+    TL_TRY(allocate_tensor(c, decl->tensor, idx, decl->rank, &t));
+    t->is_sparse = true;
+    return TL_OK;
+}
+
+static tl_status run_save(tl_ctx* c, const tl_statement* st) {
+    Tensor* t = find_defined(c, st->name);
+    if (!t) return TL_OK;   // the reference emits a comment
+    std::vector<double> v(std::max<int64_t>(t->total, 1));
+    TL_TRY(tl_tensor_download(static_cast<tl_tensor*>(t), v.data()));
+    FILE* f = fopen(st->path, "wb");
+    if (!f) return fail(c, TL_ERR_IO, "cannot open %s", st->path);
+    size_t w = fwrite(v.data(), 8, (size_t)t->total, f);
+    fclose(f);
+    return w == (size_t)t->total ? TL_OK : fail(c, TL_ERR_IO, "short write to %s", st->path);
+}
+
+static tl_status run_load(tl_ctx* c, const tl_statement* st) {
+    Tensor* t = find_defined(c, st->name);
+    if (!t) return TL_OK;
+    if (st->host_data) return tl_tensor_upload(static_cast<tl_tensor*>(t), st->host_data);
+    if (st->path[0] == 0) {
+        // resident input: the device storage already holds this run's values
+        if (!t->dense) return fail(c, TL_ERR_INVALID, "%s: resident load without device data", st->name);
+        t->zero = false;
+        t->dense_valid = true;
+        t->bits_valid = t->csr_valid = t->csc_valid = false;
+        return TL_OK;
+    }
+    std::vector<double> v(std::max<int64_t>(t->total, 1), 0.0);
+    FILE* f = fopen(st->path, "rb");
+    if (!f) return fail(c, TL_ERR_IO, "cannot open %s", st->path);
+    size_t r = fread(v.data(), 8, (size_t)t->total, f);
+    fclose(f);
+    (void)r;
+    return tl_tensor_upload(static_cast<tl_tensor*>(t), v.data());
+}
+
+static tl_status run_sparse_load(tl_ctx* c, const tl_statement* st) {
+    Tensor* t = find_defined(c, st->name);
+    if (!t) return fail(c, TL_ERR_NOT_FOUND, "sparse tensor %s not declared", st->name);
+    if (!st->coo_rows) {
+        // resident: keep the CSR uploaded earlier
+        if (!t->rowptr) return fail(c, TL_ERR_INVALID, "%s: resident sparse load without device data", st->name);
+        t->zero = false;
+        t->csr_valid = true;
+        t->boolean = t->csr_ones;
+        t->dense_valid = t->bits_valid = false;
+        t->csc_valid = t->colptr != nullptr;
+        return TL_OK;
+    }
+    return tl_sparse_upload(static_cast<tl_tensor*>(t), st->size, st->coo_rows, st->coo_cols, st->host_data);
+}
+
+extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n) {
+    if (!c || (n > 0 && !s)) return TL_ERR_INVALID;
+    TL_CK(c, cudaSetDevice(c->device));
+    c->err.clear();
+    c->query_out.clear();
+    // a fresh run: every tensor is absent until its first definition
+    for (auto& kv : c->tensors) kv.second->defined = false;
+    c->maxdims.clear();
+    for (int i = 0; i < n; ++i)
+        if (s[i].kind == TL_STMT_DOMAIN) TL_TRY(tl_domain(c, s[i].name, s[i].size));
+    std::vector<tl_equation> eqs, rec;
+    for (int i = 0; i < n; ++i)
+        if (s[i].kind == TL_STMT_EQUATION) eqs.push_back(s[i].eq);
+    TL_TRY(tl_declare_dims(c, eqs.data(), (int)eqs.size()));
+    for (int i = 0; i < n; ++i) {
+        const tl_statement* st = &s[i];
+        switch (st->kind) {
+        case TL_STMT_DOMAIN: case TL_STMT_QUERY: break;
+        case TL_STMT_EQUATION:
+            if (is_recursive(&st->eq)) rec.push_back(st->eq);
+            else TL_TRY(run_equation(c, &st->eq));
+            break;
+        case TL_STMT_SPARSE: TL_TRY(tl_sparse_decl(c, &st->sparse)); break;
+        case TL_STMT_SPARSE_LOAD: TL_TRY(run_sparse_load(c, st)); break;
+        case TL_STMT_BACKWARD:
+            TL_TRY(run_backward(c, st->name, st->params, st->n_params, eqs.data(), (int)eqs.size()));
+            break;
+        case TL_STMT_SAVE: TL_TRY(run_save(c, st)); break;
+        case TL_STMT_LOAD: TL_TRY(run_load(c, st)); break;
+        default: return fail(c, TL_ERR_INVALID, "unknown statement kind %d", st->kind);
+        }
+    }
+    c->last_sweeps = 0;
+    if (!rec.empty()) TL_TRY(run_fixpoint(c, rec.data(), (int)rec.size(), nullptr));
+    for (int i = 0; i < n; ++i) {
+        if (s[i].kind != TL_STMT_QUERY) continue;
+        Tensor* t = find_defined(c, s[i].name);
+        if (!t) continue;
+        std::vector<char> buf(64 + 20 * 32 + strlen(s[i].name));
+        TL_TRY(tl_query_format(static_cast<tl_tensor*>(t), buf.data(), (int64_t)buf.size()));
+        c->query_out += buf.data();
+        if (c->opts.verbose) fputs(buf.data(), stdout);
+    }
+    return TL_OK;
+}

@@ -1,0 +1,267 @@
+// Internal declarations of libtl_cuda (not part of the ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/tl_cuda.h"
+
+namespace tl {
+
+constexpr int kMaxVars = 12;
+
+// ----------------------------------------------------------------------------
+// Device tensor with several interchangeable storages.
+// ----------------------------------------------------------------------------
+struct Tensor {
+    std::string name;
+    void* owner = nullptr;  // tl_ctx that created the tensor
+    int rank = 0;
+    int64_t dims[TL_MAX_RANK] = {0};
+    int64_t strides[TL_MAX_RANK] = {0};
+    int64_t total = 0;
+
+    // Reference state: present in the codegen's tensor map (defined) and
+    // holding calloc zeros that have not been written yet (zero).
+    bool defined = false;
+    bool zero = true;
+    bool boolean = false;   // every value is 0 or 1
+    bool is_sparse = false; // declared `sparse`
+    int shard = TL_SHARD_NONE;
+
+    // fp32 dense row-major (local rows only when sharded)
+    float* dense = nullptr;
+    int64_t dense_elems = 0;
+    bool dense_valid = false;
+
+    // bit rows of a rank-2 0/1 tensor (local rows only when sharded)
+    uint32_t* bits = nullptr;
+    int64_t bits_words = 0;   // words per row
+    int64_t bits_rows = 0;
+    bool bits_valid = false;
+
+    // CSR of a rank-2 tensor (local rows only when sharded)
+    int64_t* rowptr = nullptr;
+    int32_t* colidx = nullptr;
+    float* vals = nullptr;
+    int64_t nnz = 0, csr_cap = 0, csr_rows = 0;
+    bool csr_valid = false;
+    bool csr_nonneg = false;  // every stored value >= 0
+    bool csr_ones = false;    // every stored value == 1
+
+    // CSC (predecessor lists) of a rank-2 tensor, global
+    int64_t* colptr = nullptr;
+    int32_t* rowidx = nullptr;
+    int64_t csc_cap = 0;
+    bool csc_valid = false;
+
+    int64_t local_rows(int rank_, int world) const {
+        if (shard != TL_SHARD_ROWS || world <= 1 || this->rank < 1) return this->rank >= 1 ? dims[0] : 1;
+        return dims[0] > rank_ ? (dims[0] - rank_ + world - 1) / world : 0;
+    }
+};
+
+struct KStat {
+    int64_t launches = 0;
+    double total_ms = 0, bytes = 0, flops = 0;
+};
+
+struct PendingEvent {
+    std::string name;
+    cudaEvent_t a, b;
+    double bytes, flops;
+};
+
+}  // namespace tl
+
+struct tl_tensor : tl::Tensor {};
+
+struct tl_ctx {
+    tl_init_opts opts{};
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    std::unordered_map<std::string, int64_t> domains;
+    std::unordered_map<std::string, std::vector<int64_t>> maxdims;
+    std::map<std::string, std::unique_ptr<tl_tensor>> tensors;
+    std::string err;
+    std::string query_out;
+    int32_t last_sweeps = 0;
+    int64_t launches = 0;
+    int rank = 0, world = 1;
+    void* comm = nullptr;  // ncclComm_t
+
+    // device scratch
+    void* ws = nullptr;
+    size_t ws_cap = 0;
+    int* d_flags = nullptr;     // [0..63] changed / error words
+    int* h_flags = nullptr;     // pinned mirror
+
+    // profiling
+    bool prof = false;
+    std::vector<tl::PendingEvent> pending;
+    std::vector<cudaEvent_t> event_pool;
+    std::map<std::string, tl::KStat> stats;
+};
+
+namespace tl {
+
+// error helpers --------------------------------------------------------------
+tl_status fail(tl_ctx* c, tl_status code, const char* fmt, ...)
+    __attribute__((format(printf, 3, 4)));
+tl_status cuda_fail(tl_ctx* c, cudaError_t e, const char* what);
+
+#define TL_CK(ctx, call)                                                         \
+    do {                                                                         \
+        cudaError_t _e = (call);                                                 \
+        if (_e != cudaSuccess) return ::tl::cuda_fail((ctx), _e, #call);         \
+    } while (0)
+#define TL_TRY(expr)                                                             \
+    do {                                                                         \
+        tl_status _s = (expr);                                                   \
+        if (_s != TL_OK) return _s;                                              \
+    } while (0)
+
+// launch accounting: every kernel launch of the runtime goes through these
+void launch_begin(tl_ctx* c, const char* name, double bytes, double flops, cudaEvent_t* ev);
+tl_status launch_end(tl_ctx* c, cudaEvent_t* ev);
+struct LaunchScope {
+    tl_ctx* c;
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    LaunchScope(tl_ctx* c_, const char* name, double bytes = 0, double flops = 0) : c(c_) {
+        launch_begin(c, name, bytes, flops, ev);
+    }
+    tl_status done() { return launch_end(c, ev); }
+};
+
+// scratch workspace (grown on demand, never shrunk)
+tl_status workspace(tl_ctx* c, size_t bytes, void** out);
+tl_status ensure_dense(tl_ctx* c, Tensor* t);
+tl_status ensure_bits(tl_ctx* c, Tensor* t);
+tl_status ensure_csr(tl_ctx* c, Tensor* t);
+tl_status alloc_bits_public(tl_ctx* c, Tensor* t);
+tl_status alloc_dense_public(tl_ctx* c, Tensor* t);
+void mark_written_dense(Tensor* t);
+void mark_written_bits(Tensor* t);
+const float* read_ptr(tl_ctx* c, Tensor* t, tl_status* st);
+
+// ----------------------------------------------------------------------------
+// Kernel entry points (k_*.cu)
+// ----------------------------------------------------------------------------
+struct RefPlan {
+    const float* ptr;     // nullptr → every element reads 0.0
+    int64_t total;
+    int32_t nidx;         // indices applied (min(rank, #indices))
+    int32_t kind[TL_MAX_RANK];
+    int32_t var[TL_MAX_RANK];
+    int64_t val[TL_MAX_RANK];
+    int64_t stride[TL_MAX_RANK];
+    const float* virt[TL_MAX_RANK];
+    int64_t virt_total[TL_MAX_RANK];
+};
+
+struct CodeOp {
+    int32_t op, arg, arg2, _pad;
+    double value;
+};
+
+struct GenericPlan {
+    int32_t n_vars, n_free;
+    int64_t sizes[kMaxVars];
+    int64_t n_out;               // product of free sizes
+    int64_t n_inner;             // product of contracted sizes
+    int32_t n_refs, n_code;
+    RefPlan refs[TL_MAX_REFS];
+    CodeOp code[TL_MAX_CODE];
+    float* lhs;
+    int64_t lhs_total;
+    int32_t n_lhs_terms;
+    int32_t lhs_var[TL_MAX_RANK];
+    int64_t lhs_div[TL_MAX_RANK];
+    int64_t lhs_stride[TL_MAX_RANK];
+    int32_t accum;
+    int32_t has_contraction;
+    int32_t old_zero;            // LHS holds logical zeros: start from 0.0
+    int32_t atomic;              // several threads may hit one LHS element
+    int32_t recursive;           // fixpoint sweep: report increases in *changed
+    int32_t virt_pos_var;
+};
+
+tl_status launch_generic(tl_ctx* c, const GenericPlan& p, int* d_changed);
+
+// rowwise softmax / lnorm over a strided row set
+struct RowPlan {
+    const float* in;
+    float* out;
+    int64_t in_total, out_total;
+    int64_t rows, len;
+    int32_t n_outer;
+    int64_t outer_size[TL_MAX_RANK];
+    int64_t outer_in_stride[TL_MAX_RANK];
+    int64_t outer_out_stride[TL_MAX_RANK];
+    int64_t in_sn, out_sn;
+    int32_t lnorm;
+};
+tl_status launch_rowwise(tl_ctx* c, const RowPlan& p);
+
+// dense GEMM C[m,n] (+)= sum_k f(A[m,k] B[k,n] * scale), arbitrary strides
+struct GemmPlan {
+    int64_t M, N, K;
+    const float* A; int64_t sam, sak;
+    const float* B; int64_t sbk, sbn;
+    float* C; int64_t scm, scn;
+    float scale;
+    int32_t beta;        // 1: add into C, 0: overwrite
+    int32_t relu_term;   // per-term relu
+    int32_t epi_relu;    // additionally write relu(C) into D (fused next equation)
+    float* D; int64_t sdm, sdn;
+};
+tl_status launch_gemm(tl_ctx* c, const GemmPlan& p);
+bool tcgen05_available(tl_ctx* c);
+
+// CSR SpMM out[v, j] (+)= sum_e val[e] * P[col[e], j]
+tl_status launch_spmm(tl_ctx* c, int64_t rows, const int64_t* rowptr, const int32_t* colidx,
+                      const float* vals, const float* P, int64_t ldp, int64_t f, float* out,
+                      int64_t ldo, int beta, int relu_out, int col_shard_world, int64_t col_local_rows);
+
+// closure
+tl_status launch_csr_to_dense(tl_ctx* c, Tensor* t);
+tl_status launch_csr_to_bits(tl_ctx* c, Tensor* t, Tensor* out);
+tl_status launch_dense_to_bits(tl_ctx* c, Tensor* t);
+tl_status launch_bits_to_dense(tl_ctx* c, Tensor* t);
+tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed);
+tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed);
+
+// elementwise gradient rules
+tl_status launch_grad_elem(tl_ctx* c, int rule, float* out, int64_t out_total, const float* up,
+                           int64_t up_total, const float* x, int64_t x_total, const float* y,
+                           int64_t y_total);
+tl_status launch_grad_softmax(tl_ctx* c, float* out, int64_t out_total, const float* up,
+                              int64_t up_total, const float* y, int64_t y_total);
+tl_status launch_fill(tl_ctx* c, float* p, int64_t n, float v);
+tl_status launch_set1(tl_ctx* c, float* p, int64_t off, const GenericPlan& plan);
+
+// communication (comm.cpp)
+tl_status comm_init(tl_ctx* c);
+tl_status comm_destroy(tl_ctx* c);
+tl_status comm_allreduce_max_int(tl_ctx* c, int* d_buf, int count);
+tl_status comm_allgather(tl_ctx* c, const void* d_send, void* d_recv, size_t bytes_per_rank);
+
+// autodiff (autodiff.cpp)
+tl_status run_backward(tl_ctx* c, const char* loss, const char (*params)[TL_NAME_LEN], int np,
+                       const tl_equation* eqs, int n_eqs);
+
+// equation lowering (runtime.cpp)
+Tensor* find(tl_ctx* c, const std::string& name);
+Tensor* find_defined(tl_ctx* c, const std::string& name);
+tl_status allocate_tensor(tl_ctx* c, const char* name, const tl_index* idx, int n, Tensor** out);
+tl_status new_tensor(tl_ctx* c, const std::string& name, int rank, const int64_t* dims, Tensor** out);
+int64_t domain_size(tl_ctx* c, const char* name);
+
+}  // namespace tl

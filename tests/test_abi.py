@@ -1,0 +1,73 @@
+"""The C-ABI library: it loads, exports every symbol the header declares, and
+its structs have the layout the Python mirror uses.  No compute (CPU only)."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+from tensor_logic_lang_b200 import abi
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "tl_cuda.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tl_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from tensor_logic_lang_b200 import build
+    build.build()
+    return abi.load_library()
+
+
+def test_exports_match_header(lib):
+    declared = header_functions()
+    assert sorted(abi.EXPORTS) == declared
+    out = subprocess.run(["nm", "-D", "--defined-only", abi.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (tl_[a-z0-9_]+)", out))
+    missing = [f for f in declared if f not in exported]
+    assert not missing, missing
+    for f in declared:
+        assert getattr(lib, f) is not None
+
+
+def test_struct_layout_matches_c(tmp_path):
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "tl_cuda.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(tl_index), sizeof(tl_ref),'
+                   ' sizeof(tl_instr), sizeof(tl_equation), sizeof(tl_statement), sizeof(tl_init_opts),'
+                   ' sizeof(tl_kernel_stats), offsetof(tl_statement, eq)); return 0;}\n')
+    exe = tmp_path / "sz"
+    subprocess.run(["gcc", "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    want = [C.sizeof(abi.Index), C.sizeof(abi.Ref), C.sizeof(abi.Instr), C.sizeof(abi.Equation),
+            C.sizeof(abi.Statement), C.sizeof(abi.InitOpts), C.sizeof(abi.KernelStats), abi.Statement.eq.offset]
+    assert got == want
+
+
+def test_default_opts(lib):
+    o = abi.InitOpts()
+    lib.tl_default_opts(C.byref(o))
+    assert o.device == -1 and o.world_size == 1 and o.max_sweeps == 1000 and o.precision == abi.PREC_TF32
+
+
+def test_null_arguments_are_rejected(lib):
+    # argument checks happen before any device call
+    assert lib.tl_init(None, None) == abi.TL_ERR_INVALID
+    assert lib.tl_shutdown(None) == abi.TL_OK
+    assert lib.tl_sync(None) == abi.TL_ERR_INVALID
+    assert lib.tl_last_error(None) == b"no context"
+    assert lib.tl_tensor_rank(None) == -1
+
+
+def test_library_has_no_oracle_dependency():
+    out = subprocess.run(["ldd", abi.LIB_PATH], capture_output=True, text=True).stdout
+    assert "oracle" not in out
+    syms = subprocess.run(["nm", "-D", abi.LIB_PATH], capture_output=True, text=True).stdout
+    assert "or_program_run" not in syms

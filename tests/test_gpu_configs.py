@@ -1,0 +1,153 @@
+"""The benchmark configurations on the CUDA backend against the f64 oracle.
+
+Small sizes run the oracle's literal loop nests; full sizes (marked slow) use
+the oracle's full-size restatements (reference-order f64 GEMM, the
+P-reordered message passing, row-wise Gauss-Seidel closure), each pinned to
+the literal loops in tests/test_oracle.py.
+"""
+import numpy as np
+import pytest
+
+from tensor_logic_lang_b200 import configs
+from tensor_logic_lang_b200 import inputs as gen
+
+from gpu_helpers import TOL_TF32, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx(gpu_ctx_factory):
+    c = gpu_ctx_factory()
+    yield c
+    c.close()
+
+
+def test_c0_mlp_forward_full(ctx, oracle_lib):
+    p, data, _, _ = configs.program(configs.mlp_forward)
+    ctx.run(p)
+    ref = oracle_lib.OracleRun(p)
+    for n in ("H", "Z2", "Y"):
+        assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
+
+
+def test_c1_attention_reduced(ctx, oracle_lib):
+    p, data, _, _ = configs.program(configs.attention, s=512, d=64)
+    ctx.run(p)
+    ref = oracle_lib.OracleRun(p)
+    for n in ("Scores", "Attn", "Out"):
+        assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
+
+
+def _attention_f64(d):
+    S = oracle_gemm_like(d["Q"], d["K"].T) / 8.0
+    A = np.exp(S) / np.exp(S).sum(axis=1, keepdims=True)
+    return S, A, A @ d["V"]
+
+
+def oracle_gemm_like(a, b):
+    return a @ b
+
+
+@pytest.mark.slow
+def test_c1_attention_full(ctx, oracle_lib):
+    p, d, _, _ = configs.program(configs.attention)
+    ctx.run(p)
+    Q, K, V = d["Q"], d["K"], d["V"]
+    S = oracle_lib.gemm(Q, K.T, scale=0.125)
+    A = np.exp(S) / np.exp(S).sum(axis=1, keepdims=True)
+    O = oracle_lib.gemm(A, V)
+    assert_close(ctx.tensor("Scores"), S, TOL_TF32, "Scores")
+    assert_close(ctx.tensor("Attn"), A, TOL_TF32, "Attn")
+    assert_close(ctx.tensor("Out"), O, TOL_TF32, "Out")
+
+
+def test_c2_train_reduced(ctx, oracle_lib):
+    p, d, _, _ = configs.program(configs.mlp_train, b=256, i=784, h=512, o=10)
+    ctx.run(p)
+    ref = oracle_lib.OracleRun(p)
+    for n in ("Z1", "H", "Y", "L", "dL_dW2", "dL_dW1"):
+        assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
+
+
+def c2_reference(oracle_lib, d):
+    """Full-size C2 through the reference-order f64 GEMM restatement (autodiff.zig rules)."""
+    X, W1, W2, T = d["X"], d["W1"], d["W2"], d["Target"]
+    Z1 = oracle_lib.gemm(X, W1)
+    H = np.maximum(Z1, 0.0)
+    Z2 = oracle_lib.gemm(H, W2)
+    Y = np.exp(Z2) / np.exp(Z2).sum(axis=1, keepdims=True)
+    D = Y - T
+    dY = 2.0 * D
+    dZ2 = Y * (dY - (dY * Y).sum())
+    dW2 = oracle_lib.gemm(H.T, dZ2)
+    dH = oracle_lib.gemm(dZ2, W2.T)
+    dZ1 = dH * (Z1 > 0)
+    dW1 = oracle_lib.gemm(X.T, dZ1)
+    return dict(Z1=Z1, H=H, Y=Y, L=np.array([(D * D).sum()]), dL_dW2=dW2, dL_dW1=dW1)
+
+
+@pytest.mark.slow
+def test_c2_train_full(ctx, oracle_lib):
+    p, d, _, _ = configs.program(configs.mlp_train)
+    ctx.run(p)
+    ref = c2_reference(oracle_lib, d)
+    for n, want in ref.items():
+        assert_close(ctx.tensor(n).reshape(want.shape), want, TOL_TF32, n)
+
+
+@pytest.mark.parametrize("n,f", [(512, 32), (4096, 128)])
+def test_c3_gnn_reduced(ctx, oracle_lib, n, f):
+    p, d, sp, _ = configs.program(configs.gnn, n=n, f=f)
+    ctx.run(p)
+    rows, cols, _ = sp["Adj"]
+    rowptr, colidx = gen.csr_from_coo(n, rows, cols)
+    h1 = oracle_lib.gnn_layer(rowptr, colidx, d["H0"], d["W1"])
+    h2 = oracle_lib.gnn_layer(rowptr, colidx, h1, d["W2"])
+    assert_close(ctx.tensor("H1"), h1, TOL_TF32, "H1")
+    assert_close(ctx.tensor("H2"), h2, TOL_TF32, "H2")
+
+
+@pytest.mark.slow
+def test_c3_gnn_full(ctx, oracle_lib):
+    p, d, sp, _ = configs.program(configs.gnn)
+    ctx.run(p)
+    n = 16384
+    rows, cols, _ = sp["Adj"]
+    rowptr, colidx = gen.csr_from_coo(n, rows, cols)
+    h1 = oracle_lib.gnn_layer(rowptr, colidx, d["H0"], d["W1"])
+    h2 = oracle_lib.gnn_layer(rowptr, colidx, h1, d["W2"])
+    assert_close(ctx.tensor("H1"), h1, TOL_TF32, "H1")
+    assert_close(ctx.tensor("H2"), h2, TOL_TF32, "H2")
+
+
+def closure_reference(oracle_lib, n, rows, cols):
+    colptr, rowidx = gen.csr_from_coo(n, cols, rows)
+    W = (n + 31) // 32
+    R = np.zeros((n, W), dtype=np.uint32)
+    np.bitwise_or.at(R, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
+    sweeps = oracle_lib.closure_right(n, colptr, rowidx, R)
+    return R, sweeps
+
+
+@pytest.mark.slow
+def test_c4_closure_full(ctx, oracle_lib):
+    p, _, sp, _ = configs.program(configs.closure)
+    ctx.run(p)
+    n = 32768
+    rows, cols, _ = sp["Edge"]
+    R, sweeps = closure_reference(oracle_lib, n, rows, cols)
+    np.testing.assert_array_equal(ctx.bits("Reach"), R)
+    assert ctx.sweeps == sweeps == 2
+    # size-independent property: the closure is transitive and contains Edge
+    got = ctx.bits("Reach")
+    assert int(np.unpackbits(got.view(np.uint8)).sum()) >= len(rows)
+
+
+def test_c4_closure_reduced(ctx, oracle_lib):
+    p, _, sp, _ = configs.program(configs.closure, n=4096)
+    ctx.run(p)
+    rows, cols, _ = sp["Edge"]
+    R, sweeps = closure_reference(oracle_lib, 4096, rows, cols)
+    np.testing.assert_array_equal(ctx.bits("Reach"), R)
+    assert ctx.sweeps == sweeps

@@ -1,0 +1,179 @@
+"""Each kernel family against the f64 oracle on seeded inputs, incl. tails and odd shapes."""
+import numpy as np
+import pytest
+
+from tensor_logic_lang_b200 import inputs as gen
+from tensor_logic_lang_b200 import lang
+
+from gpu_helpers import TOL_FP32, TOL_TF32, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx(gpu_ctx_factory):
+    c = gpu_ctx_factory()
+    yield c
+    c.close()
+
+
+def both(ctx, oracle_lib, src, data=None, sparse=None):
+    p = lang.Program(src, inputs=data, sparse_inputs=sparse)
+    ctx.run(p)
+    return oracle_lib.OracleRun(p)
+
+
+def decl(**dom):
+    return "".join(f"domain {k}: {v}\n" for k, v in dom.items())
+
+
+def inputs_src(names):
+    return "".join(f"{n}[{','.join(ix)}] = 0\nload {n} \"{n}.bin\"\n" for n, ix in names)
+
+
+# ----------------------------------------------------------------------------- GEMM
+GEMM_CASES = [
+    # (M, N, K, A index order, B index order, LHS order, extra)
+    (300, 200, 100, "mk", "kn", "mn", ""),          # SIMT, tails
+    (1024, 512, 784, "mk", "kn", "mn", ""),         # tcgen05: A K-major, B MN-major
+    (1024, 512, 784, "mk", "nk", "mn", ""),         # tcgen05: both K-major
+    (784, 1024, 512, "km", "kn", "mn", ""),         # tcgen05: both MN-major (dW-style)
+    (512, 1024, 256, "km", "nk", "nm", ""),         # transposed output
+    (1000, 600, 300, "mk", "kn", "mn", ""),         # tails in M, N, K
+    (1024, 768, 200, "mk", "kn", "mn", "relu"),     # per-term relu: sign split
+    (512, 512, 128, "mk", "kn", "mn", "scale"),     # literal scale
+    (512, 512, 130, "mk", "kn", "mn", "accum"),     # += into existing values, K not /4
+    (2048, 64, 2048, "mk", "kn", "mn", ""),         # N = 64 tile, long K
+    (1024, 10, 4096, "mk", "kn", "mn", ""),         # skinny N: SIMT split-K
+]
+
+
+@pytest.mark.parametrize("case", GEMM_CASES, ids=[f"{c[0]}x{c[1]}x{c[2]}-{c[3]}{c[4]}{c[5]}-{c[6]}" for c in GEMM_CASES])
+def test_gemm(ctx, oracle_lib, case):
+    M, N, K, ao, bo, lo, extra = case
+    size = dict(m=M, n=N, k=K)
+    A = gen.normal(1, "A", tuple(size[c] for c in ao))
+    B = gen.normal(1, "B", tuple(size[c] for c in bo))
+    a = f"A[{ao[0]},{ao[1]}]"
+    b = f"B[{bo[0]},{bo[1]}]"
+    rhs = f"{a} {b}"
+    if extra == "relu":
+        rhs = f"relu({a} {b})"
+    if extra == "scale":
+        rhs = f"{a} {b} / 8.0"
+    src = decl(m=M, n=N, k=K) + inputs_src([("A", ao), ("B", bo)])
+    if extra == "accum":
+        C0 = gen.normal(2, "C0", (M, N))
+        src += inputs_src([("C", "mn")]) + f"C[m,n] += {rhs}\n"
+        data = dict(A=A, B=B, C=C0)
+        out = "C"
+    else:
+        src += f"C[{lo[0]},{lo[1]}] = {rhs}\n"
+        data = dict(A=A, B=B)
+        out = "C"
+    p = lang.Program(src, inputs=data)
+    ctx.run(p)
+    got = ctx.tensor(out)
+    # reference values from the oracle's reference-order f64 loop
+    Am = A if ao == "mk" else A.T
+    Bm = B if bo == "kn" else B.T
+    want = oracle_lib.gemm(Am, Bm, C_init=data.get("C"), relu_per_term=(extra == "relu"),
+                           scale=0.125 if extra == "scale" else 1.0)
+    if lo == "nm":
+        want = want.T
+    tol = TOL_TF32 if M * N * K >= (1 << 25) else TOL_FP32
+    assert_close(got, want, tol, "C")
+
+
+# ----------------------------------------------------------------------------- row-wise
+ROW_CASES = [(3, 10), (2048, 2048), (64, 1000), (5, 5000), (1024, 10), (7, 129)]
+
+
+@pytest.mark.parametrize("rows,cols", ROW_CASES)
+@pytest.mark.parametrize("op", ["softmax", "lnorm"])
+def test_rowwise(ctx, oracle_lib, rows, cols, op):
+    X = gen.normal(3, "X", (rows, cols), 2.0)
+    src = decl(r=rows, c=cols) + inputs_src([("X", "rc")]) + f"Y[r,c.] = {op}(X[r,c])\nYt[r.,c] = {op}(X[r,c])\n"
+    ref = both(ctx, oracle_lib, src, dict(X=X))
+    assert_close(ctx.tensor("Y"), ref.tensor("Y"), TOL_FP32 * 10, "Y")
+    assert_close(ctx.tensor("Yt"), ref.tensor("Yt"), TOL_FP32 * 10, "Yt")
+
+
+# ----------------------------------------------------------------------------- generic
+GENERIC = [
+    ("S[i] = A[i,j] B[j]", "sum"),
+    ("S[i] += exp(A[i,j] B[j])", "exp per term"),
+    ("S[i] max= A[i,j] B[j]", "max"),
+    ("S[i] min= A[i,j] - B[j]", "min"),
+    ("S[i] *= sigmoid(A[i,j])", "mul"),
+    ("S[i] = tanh(A[i,j] B[j]) + abs(B[j])", "tanh+abs"),
+    ("S[i] = step(A[i,j]) B[j]", "step factor"),
+    ("S[i] = sqrt(abs(A[i,j])) * cos(B[j]) - sin(A[i,j])", "mixed"),
+    ("S[i] = A[i,3] + A[i+1,0] - A[i-1,2]", "const and offset"),
+    ("S[i] = A[i,j] > B[j]", "comparison"),
+    ("S[i] = log(abs(A[i,j]) + 1.0) ^ 2", "log pow"),
+    ("S[i] = -A[i,j]", "negate"),
+]
+
+
+@pytest.mark.parametrize("eq,what", GENERIC, ids=[g[1] for g in GENERIC])
+def test_generic_einsum(ctx, oracle_lib, eq, what):
+    A = gen.normal(4, "A", (37, 23))
+    B = gen.normal(4, "B", (23,))
+    src = decl(i=37, j=23) + inputs_src([("A", "ij"), ("B", "j")]) + "S[i] = 0\n" + eq + "\n"
+    ref = both(ctx, oracle_lib, src, dict(A=A, B=B))
+    assert_close(ctx.tensor("S"), ref.tensor("S"), TOL_FP32, what)
+
+
+def test_avg_pool_and_scalar_assign(ctx, oracle_lib):
+    X = gen.normal(5, "X", (32, 6))
+    src = decl(i=32, j=6) + inputs_src([("X", "ij")]) + \
+        "P[i/4, j] avg= X[i,j]\nX[3,2] = 7.5\nQ[i,j] = X[i,j] * 2.0\nT = X[i,j]\n"
+    ref = both(ctx, oracle_lib, src, dict(X=X))
+    for n in ("P", "Q", "T"):
+        assert_close(ctx.tensor(n), ref.tensor(n), TOL_FP32, n)
+
+
+# ----------------------------------------------------------------------------- fixpoint
+@pytest.mark.parametrize("n,deg,seed", [(100, 3, 1), (1000, 4, 2), (4096, 4, 3), (2000, 1, 4)])
+def test_closure_bits(ctx, oracle_lib, n, deg, seed):
+    rows, cols = gen.random_dag(n, deg, seed)
+    src = decl(x=n, y=n, z=n) + "sparse Edge[x, y]\nReach[x,y] = step(Edge[x,y])\n" \
+                                "Reach[x,z] max= step(Reach[x,y] Edge[y,z])\n"
+    p = lang.Program(src, sparse_inputs={"Edge": (rows, cols, None)})
+    ctx.run(p)
+    got = ctx.bits("Reach")
+    colptr, rowidx = gen.csr_from_coo(n, cols, rows)
+    W = (n + 31) // 32
+    R = np.zeros((n, W), dtype=np.uint32)
+    np.bitwise_or.at(R, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
+    sweeps = oracle_lib.closure_right(n, colptr, rowidx, R)
+    np.testing.assert_array_equal(got, R)
+    assert ctx.sweeps == sweeps == 2
+
+
+def test_closure_with_cycles(ctx, oracle_lib):
+    n = 300
+    rng = np.random.default_rng(9)
+    pairs = np.unique(rng.integers(0, n, size=(900, 2)), axis=0)
+    pairs = pairs[pairs[:, 0] != pairs[:, 1]]
+    rows, cols = pairs[:, 0], pairs[:, 1]
+    src = decl(x=n, y=n, z=n) + "sparse Edge[x, y]\nReach[x,y] = step(Edge[x,y])\n" \
+                                "Reach[x,z] max= step(Reach[x,y] Edge[y,z])\n"
+    ref = both(ctx, oracle_lib, src, sparse={"Edge": (rows, cols, None)})
+    np.testing.assert_array_equal(ctx.tensor("Reach"), ref.tensor("Reach"))
+
+
+def test_generic_recursive_dense(ctx, oracle_lib):
+    # a dense relation takes the generic recursive kernel: same fixpoint
+    n = 40
+    E = np.zeros((n, n))
+    rng = np.random.default_rng(5)
+    for u in range(n):
+        for v in rng.choice(n, 2, replace=False):
+            if u < v:
+                E[u, v] = 1.0
+    src = decl(x=n, y=n, z=n) + inputs_src([("E", "xy")]) + \
+        "R[x,y] = step(E[x,y])\nR[x,z] max= step(R[x,y] E[y,z])\n"
+    ref = both(ctx, oracle_lib, src, dict(E=E))
+    np.testing.assert_array_equal(ctx.tensor("R"), ref.tensor("R"))
