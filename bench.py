@@ -169,13 +169,16 @@ def l2_flush(buf):
     buf.add_(1)   # writes 256 MiB (> 126 MB L2) on torch's stream
 
 
-def time_steps(ctx, step, steps, warmup, dist, flush):
+def time_steps(ctx, step, steps, warmup, dist, flush, profile=True):
     import torch
     timer = StreamTimer(ctx)
     for _ in range(warmup):
         step()
     ctx.sync()
     torch.cuda.synchronize()
+    if profile:
+        ctx.profile(True)
+        ctx.profile_reset()
     dist.barrier()
     total = 0.0
     launches0 = ctx.launches
@@ -227,8 +230,6 @@ def run_closure(args, dist, peaks):
 
     clocks = ClockSampler(dist.local)
     clocks.start()
-    ctx.profile(True)
-    ctx.profile_reset()
     ms, launches = time_steps(ctx, lambda: ctx.run(resident), args.steps, args.warmup, dist, flush)
     prof = ctx.profile_read()
     ctx.profile(False)
@@ -305,8 +306,6 @@ def run_einsum_configs(args, peaks):
             if s.kind == 7:
                 s.coo_rows = None
                 s.coo_cols = None
-        ctx.profile(True)
-        ctx.profile_reset()
         ms, launches = time_steps(ctx, lambda: ctx.run(p_res), args.steps, args.warmup, One(), flush)
         prof = ctx.profile_read()
         ctx.profile(False)
@@ -315,7 +314,8 @@ def run_einsum_configs(args, peaks):
         tc = prof.get("gemm_tcgen05_tf32")
         entry = {"tflops": round(flops / (per / 1e3) / 1e12, 3), "ms_per_step": round(per, 4),
                  "algo_flops": flops, "gpu_launches_per_step": launches / args.steps,
-                 "top_kernel": top[0], "top_kernel_share": round(top[1].get("total_ms", 0) / max(ms, 1e-9), 3)}
+                 "top_kernel": top[0], "top_kernel_share": round(top[1].get("total_ms", 0) / max(ms, 1e-9), 3),
+                 "kernels_ms_per_step": {k: round(v["total_ms"] / args.steps, 4) for k, v in prof.items()}}
         if tc and tc["launches"]:
             tflops = tc["flops"] / (tc["total_ms"] / 1e3) / 1e12
             # TF32 issues at half the bf16 rate on the same tensor cores

@@ -168,14 +168,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
-// UMMA shared-memory descriptor, 128-byte swizzle (layout type 2), sm_100 version 1.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// UMMA shared-memory descriptor (sm_100 version 1).  Layout type 2 is the
+// 128-byte swizzle of K-major tiles; type 1 is the 128-byte swizzle with a
+// 32-byte atom, the one shared-memory layout MN-major tf32 operands have.
+constexpr uint64_t kLayoutSW128 = 2, kLayoutSW128Base32B = 1;
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint64_t layout) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFF);
     d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
     d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
     d |= (uint64_t)1 << 46;                 // descriptor version (Blackwell)
-    d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+    d |= layout << 61;
     return d;
 }
 
@@ -293,10 +297,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < TC_BK / 8; ++kk) {
-                    // K-major: advance 32 bytes inside the swizzled row; SBO = 8 rows.
-                    // MN-major: advance one 8-row K group (1 KB); LBO = next 32-wide MN chunk.
-                    const uint64_t ad = A_MN ? umma_desc(sa + kk * 1024, 4096, 1024) : umma_desc(sa + kk * 32, 16, 1024);
-                    const uint64_t bd = B_MN ? umma_desc(sb + kk * 1024, 4096, 1024) : umma_desc(sb + kk * 32, 16, 1024);
+                    // K-major: advance 32 bytes inside the swizzled 128-byte row; SBO = 8 rows.
+                    // MN-major: 8 K rows of 128 bytes per MMA (two 4-row 32B-atom groups,
+                    // SBO = 512 bytes); LBO = the next 32-wide MN chunk (one 4 KB box).
+                    const uint64_t ad = A_MN ? umma_desc(sa + kk * 1024, 4096, 512, kLayoutSW128Base32B)
+                                             : umma_desc(sa + kk * 32, 16, 1024, kLayoutSW128);
+                    const uint64_t bd = B_MN ? umma_desc(sb + kk * 1024, 4096, 512, kLayoutSW128Base32B)
+                                             : umma_desc(sb + kk * 32, 16, 1024, kLayoutSW128);
                     umma_tf32(tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(&empty[s]);
@@ -356,6 +363,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+// Round an fp32 value to TF32 (10-bit mantissa), nearest with ties away from
+// zero.  The tensor cores would otherwise drop the low 13 bits (truncation),
+// which biases sums of same-sign terms such as the sign-split products.
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
 // relu sign split into K-major copies: Ap[m, 0:K] = max(A,0), Ap[m, K:2K] = max(-A,0);
 // Bp[n, 0:K] = max(sB,0), Bp[n, K:2K] = max(-sB,0) with s the sign of the scale.
 __global__ void k_split_a(const float* __restrict__ A, int64_t sam, int64_t sak, int64_t M, int64_t K, int64_t ldp,
@@ -365,10 +381,10 @@ __global__ void k_split_a(const float* __restrict__ A, int64_t sam, int64_t sak,
         const int64_t m = i / K, k = i % K;
         const float a = A[m * sam + k * sak];
         if (split) {
-            Ap[m * ldp + k] = fmaxf(a, 0.f);
-            Ap[m * ldp + K + k] = fmaxf(-a, 0.f);
+            Ap[m * ldp + k] = tf32_rna(fmaxf(a, 0.f));
+            Ap[m * ldp + K + k] = tf32_rna(fmaxf(-a, 0.f));
         } else {
-            Ap[m * ldp + k] = a;
+            Ap[m * ldp + k] = tf32_rna(a);
         }
     }
 }
@@ -389,10 +405,10 @@ __global__ void k_transpose_split(const float* __restrict__ S, int64_t s_r, int6
         if (cc < Cn && r < R) {
             const float v = tile[threadIdx.x][i];
             if (split) {
-                D[cc * ld + r] = fmaxf(v, 0.f);
-                D[cc * ld + R + r] = fmaxf(-v, 0.f);
+                D[cc * ld + r] = tf32_rna(fmaxf(v, 0.f));
+                D[cc * ld + R + r] = tf32_rna(fmaxf(-v, 0.f));
             } else {
-                D[cc * ld + r] = v;
+                D[cc * ld + r] = tf32_rna(v);
             }
         }
     }
@@ -417,8 +433,10 @@ EncodeTiledFn get_encode() {
 }
 
 // 2-D fp32 map: inner (contiguous) extent x, outer extent y, row stride in
-// elements; box 32 x box_y with 128-byte swizzle.
-bool make_map(CUtensorMap* map, const float* base, int64_t x, int64_t y, int64_t row_stride, int box_y) {
+// elements; box 32 x box_y.  K-major tiles use the 128-byte swizzle;
+// MN-major tiles (mn = true) the 128-byte swizzle with 32-byte atoms that
+// the MN-major tf32 UMMA layout expects.
+bool make_map(CUtensorMap* map, const float* base, int64_t x, int64_t y, int64_t row_stride, int box_y, bool mn) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return false;
     cuuint64_t dims[2] = {(cuuint64_t)x, (cuuint64_t)y};
@@ -426,8 +444,9 @@ bool make_map(CUtensorMap* map, const float* base, int64_t x, int64_t y, int64_t
     cuuint32_t box[2] = {32, (cuuint32_t)box_y};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -527,7 +546,9 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
 
     // Operand layouts.  A[m,k]: K-major when sak == 1, MN-major when sam == 1.
     // B[k,n] as the UMMA "B" (N x K): K-major when sbk == 1, MN-major when sbn == 1.
-    const bool no_mn = env_flag("TL_GEMM_NO_MN");
+    // MN-major operand descriptors are opt-in (TL_GEMM_MN=1) until validated;
+    // by default MN-major operands go through a K-major transposing copy.
+    const bool no_mn = !env_flag("TL_GEMM_MN");
     const bool split = p.relu_term != 0;
     const float sgn = p.scale < 0.f ? -1.f : 1.f;
     const int64_t Ke = split ? 2 * p.K : p.K;
@@ -581,11 +602,11 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     const int64_t Ka = a_ok ? p.K : Kpad, Kb = b_ok ? p.K : Kpad;
     const int64_t Kx = Ka > Kb ? Ka : Kb;
     CUtensorMap ma, mb;
-    bool ok = A.mn_major ? make_map(&ma, A.ptr, p.M, Ka, A.rows_stride, 32)
-                         : make_map(&ma, A.ptr, Ka, p.M, A.rows_stride, TC_BM);
+    bool ok = A.mn_major ? make_map(&ma, A.ptr, p.M, Ka, A.rows_stride, 32, true)
+                         : make_map(&ma, A.ptr, Ka, p.M, A.rows_stride, TC_BM, false);
     const int BN = p.N >= 256 && (p.N % 256 == 0 || p.N >= 1024) ? 256 : (p.N >= 128 ? 128 : 64);
-    ok = ok && (B.mn_major ? make_map(&mb, B.ptr, p.N, Kb, B.rows_stride, 32)
-                           : make_map(&mb, B.ptr, Kb, p.N, B.rows_stride, BN));
+    ok = ok && (B.mn_major ? make_map(&mb, B.ptr, p.N, Kb, B.rows_stride, 32, true)
+                           : make_map(&mb, B.ptr, Kb, p.N, B.rows_stride, BN, false));
     if (!ok) return launch_simt(c, p);
     TcEpi e;
     e.C = p.C; e.scm = p.scm; e.scn = p.scn;

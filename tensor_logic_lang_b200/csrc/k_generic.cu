@@ -190,6 +190,113 @@ __global__ void k_generic(const __grid_constant__ GenericPlan p, int* changed, i
     }
 }
 
+// Small outputs with long contractions: one block per LHS element, the
+// contracted range split across the block's threads and combined with a
+// tree reduction in f64.  The operator must be associative (sum, max, min,
+// product); the order of the partial folds differs from the reference's
+// sequential loop only in f64 rounding of sums.
+__global__ void __launch_bounds__(256) k_generic_reduce(const __grid_constant__ GenericPlan p) {
+    __shared__ double sh[256];
+    const bool is_max = p.accum == TL_ACC_MAX, is_min = p.accum == TL_ACC_MIN, is_mul = p.accum == TL_ACC_MUL;
+    const double ident = is_max ? -INFINITY : is_min ? INFINITY : is_mul ? 1.0 : 0.0;
+    for (int64_t o = blockIdx.x; o < p.n_out; o += gridDim.x) {
+        int64_t iv[kMaxVars];
+        int64_t rem = o;
+        for (int v = p.n_free - 1; v >= 0; --v) {
+            iv[v] = rem % p.sizes[v];
+            rem /= p.sizes[v];
+        }
+        double acc = ident;
+        for (int64_t j = threadIdx.x; j < p.n_inner; j += blockDim.x) {
+            int64_t r = j;
+            for (int v = p.n_vars - 1; v >= p.n_free; --v) {
+                iv[v] = r % p.sizes[v];
+                r /= p.sizes[v];
+            }
+            const double t = eval(p, iv);
+            acc = is_max ? (t > acc ? t : acc) : is_min ? (t < acc ? t : acc) : is_mul ? acc * t : acc + t;
+        }
+        sh[threadIdx.x] = acc;
+        __syncthreads();
+        for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+            if (threadIdx.x < s) {
+                const double a = sh[threadIdx.x], b = sh[threadIdx.x + s];
+                sh[threadIdx.x] = is_max ? (b > a ? b : a) : is_min ? (b < a ? b : a) : is_mul ? a * b : a + b;
+            }
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) {
+            int64_t off = 0;
+            for (int k = 0; k < p.n_lhs_terms; ++k) off += (iv[p.lhs_var[k]] / p.lhs_div[k]) * p.lhs_stride[k];
+            if (off >= 0 && off < p.lhs_total) {
+                const double old = p.old_zero ? 0.0 : (double)p.lhs[off];
+                const double part = sh[0];
+                const double nv = is_max ? (part > old ? part : old) : is_min ? (part < old ? part : old)
+                                : is_mul ? old * part : old + part;
+                p.lhs[off] = (float)nv;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Element-wise equations whose operands share the LHS's shape and index
+// order: the flat index addresses every operand, no index decoding.
+__global__ void k_generic_aligned(const __grid_constant__ GenericPlan p) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < p.n_out; t += (int64_t)gridDim.x * blockDim.x) {
+        double st[16];
+        int sp = 0;
+        for (int i = 0; i < p.n_code; ++i) {
+            const CodeOp& in = p.code[i];
+            switch (in.op) {
+            case TL_OP_REF: { const float* q = p.refs[in.arg].ptr; st[sp++] = q ? (double)q[t] : 0.0; break; }
+            case TL_OP_LIT: st[sp++] = in.value; break;
+            case TL_OP_PROD: {
+                const int n = in.arg;
+                double a = st[sp - n];
+                for (int k = 1; k < n; ++k) a = a * st[sp - n + k];
+                sp -= n;
+                st[sp++] = a;
+                break;
+            }
+            case TL_OP_NEG: st[sp - 1] = -st[sp - 1]; break;
+            case TL_OP_NOT: st[sp - 1] = st[sp - 1] == 0.0 ? 1.0 : 0.0; break;
+            case TL_OP_NL: st[sp - 1] = nonlin(in.arg, st[sp - 1], in.arg2, in.value); break;
+            default: {
+                const double b = st[--sp], a = st[sp - 1];
+                double r;
+                switch (in.op) {
+                case TL_OP_ADD: r = a + b; break;
+                case TL_OP_SUB: r = a - b; break;
+                case TL_OP_MUL: r = a * b; break;
+                case TL_OP_DIV: r = a / b; break;
+                case TL_OP_POW: r = pow(a, b); break;
+                case TL_OP_GT: r = a > b; break;
+                case TL_OP_LT: r = a < b; break;
+                case TL_OP_GE: r = a >= b; break;
+                case TL_OP_LE: r = a <= b; break;
+                case TL_OP_EQ: r = a == b; break;
+                case TL_OP_NE: r = (a < b) || (a > b); break;
+                default: r = a + b; break;
+                }
+                st[sp - 1] = r;
+            }
+            }
+        }
+        const double rhs = sp > 0 ? st[sp - 1] : 0.0;
+        const double old = p.old_zero ? 0.0 : (double)p.lhs[t];
+        double nv;
+        switch (p.accum) {
+        case TL_ACC_ASSIGN: nv = rhs; break;
+        case TL_ACC_ADD: case TL_ACC_AVG: nv = old + rhs; break;
+        case TL_ACC_MAX: nv = rhs > old ? rhs : old; break;
+        case TL_ACC_MIN: nv = rhs < old ? rhs : old; break;
+        default: nv = old * rhs; break;
+        }
+        p.lhs[t] = (float)nv;
+    }
+}
+
 __global__ void k_set1(const __grid_constant__ GenericPlan p, float* dst, int64_t off) {
     if (threadIdx.x == 0 && blockIdx.x == 0) dst[off] = (float)eval(p, nullptr);
 }
@@ -203,10 +310,28 @@ __global__ void k_fill(float* p, int64_t n, float v) {
 
 tl_status launch_generic(tl_ctx* c, const GenericPlan& p, int* d_changed) {
     const bool serial = p.atomic && p.accum == TL_ACC_ASSIGN && !p.has_contraction;
+    const double terms = (double)p.n_out * (double)p.n_inner;
+    if (p.aligned && !p.recursive && !p.has_contraction) {
+        int64_t blocks = (p.n_out + 255) / 256;
+        const int64_t cap = (int64_t)c->sm_count * 16;
+        if (blocks > cap) blocks = cap;
+        LaunchScope L(c, "elementwise", (double)p.n_out * 4.0 * (p.n_refs + 1), (double)p.n_out);
+        k_generic_aligned<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, c->stream>>>(p);
+        return L.done();
+    }
+    // few outputs, long contraction, associative operator: split the contraction
+    const bool assoc = p.has_contraction && (p.accum == TL_ACC_ASSIGN || p.accum == TL_ACC_ADD ||
+                                             p.accum == TL_ACC_AVG || p.accum == TL_ACC_MAX ||
+                                             p.accum == TL_ACC_MIN || p.accum == TL_ACC_MUL);
+    if (assoc && !p.recursive && !p.atomic && p.n_inner >= 512 && p.n_out < (int64_t)c->sm_count * 64) {
+        int64_t blocks = p.n_out < (int64_t)c->sm_count * 8 ? p.n_out : (int64_t)c->sm_count * 8;
+        LaunchScope L(c, "generic_reduce", terms * 4.0 * p.n_refs, terms * 2.0);
+        k_generic_reduce<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, c->stream>>>(p);
+        return L.done();
+    }
     const int threads = 128;
     int64_t blocks = serial ? 1 : (p.n_out + threads - 1) / threads;
     blocks = blocks < 1 ? 1 : (blocks > 65535LL * 8 ? 65535LL * 8 : blocks);
-    const double terms = (double)p.n_out * (double)p.n_inner;
     LaunchScope L(c, "generic_einsum", terms * 4.0 * (p.n_refs + 0.0) / (p.n_inner > 0 ? p.n_inner : 1) + p.n_out * 4.0,
                   terms * 2.0);
     k_generic<<<(unsigned)blocks, serial ? 1 : threads, 0, c->stream>>>(p, d_changed, serial ? 1 : 0);

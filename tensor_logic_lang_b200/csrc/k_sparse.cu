@@ -20,6 +20,8 @@
 // same two sweeps the reference takes; on any edge set the fixpoint reached
 // is the least one above the start, bit for bit.  A device-side changed word
 // records whether any row gained a bit.
+#include <vector>
+
 #include "tl_internal.h"
 
 namespace tl {
@@ -71,53 +73,87 @@ __global__ void k_bits_to_dense(const uint32_t* bits, int64_t rows, int64_t cols
     }
 }
 
-// Right-form sweep.  One warp per local row; `row_of(i)` maps a local row to
-// its global index (rows are dealt cyclically across ranks).
-__global__ void __launch_bounds__(128) k_closure_right(uint32_t* R, int64_t local_rows, int64_t words, int64_t n,
-                                                       const int64_t* __restrict__ rowptr,
-                                                       const int32_t* __restrict__ colidx, int* changed) {
-    extern __shared__ uint32_t srow_all[];
+// Right-form sweep.  A warp takes rows from a shared counter (the rows with
+// the largest reach sets, low indices on a u < v DAG, start first), holds the
+// row in shared memory, and walks it in windows of 1024 bits.  The set,
+// not yet expanded bits of a window are compacted into a work list that all
+// 32 lanes expand together; the window is re-read until no new bit appears
+// in it.  pending[r] is the lowest word that may hold a bit not expanded in
+// an earlier sweep: a successor that lands below the current window (a back
+// edge) is left for the next sweep, as in the reference's in-place order,
+// and a row with nothing pending is already closed, so its sweep changes
+// nothing and is skipped without loading the row.
+constexpr int kClosureWarps = 4;
+constexpr int kWindowWords = 32;
+
+__global__ void __launch_bounds__(32 * kClosureWarps)
+    k_closure_right(uint32_t* R, int64_t local_rows, int64_t words, const int64_t* __restrict__ rowptr,
+                    const int32_t* __restrict__ colidx, int64_t e_rows, int* changed, unsigned long long* next_row,
+                    int32_t* pending) {
+    extern __shared__ uint32_t smem_u[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    uint32_t* row = srow_all + (int64_t)wib * words;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + wib; r < local_rows; r += warps) {
-        uint32_t* grow = R + r * words;
+    uint32_t* row = smem_u + (int64_t)wib * (words + kWindowWords * 32 / 2);
+    uint16_t* wl = reinterpret_cast<uint16_t*>(row + words);
+    for (;;) {
+        unsigned long long r = 0;
+        if (lane == 0) r = atomicAdd(next_row, 1ull);
+        r = __shfl_sync(0xffffffffu, r, 0);
+        if ((int64_t)r >= local_rows) break;
+        const int64_t start_w = pending[r];
+        if (start_w >= words) continue;                  // closed row: nothing to expand
+        uint32_t* grow = R + (int64_t)r * words;
         for (int64_t w = lane; w < words; w += 32) row[w] = grow[w];
         __syncwarp();
         bool grew = false;
-        for (int64_t c0 = 0; c0 < words; c0 += 32) {
+        int32_t low = INT32_MAX;
+        for (int64_t c0 = (start_w / kWindowWords) * kWindowWords; c0 < words; c0 += kWindowWords) {
             const int64_t w = c0 + lane;
             uint32_t done = 0;
             for (;;) {
                 const uint32_t cur = w < words ? row[w] : 0u;
-                uint32_t pend = cur & ~done;
-                if (__ballot_sync(0xffffffffu, pend != 0) == 0) break;
+                const uint32_t pend = cur & ~done;
+                const int cnt = __popc(pend);
+                int pre = cnt;                          // inclusive prefix over lanes
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int v = __shfl_up_sync(0xffffffffu, pre, o);
+                    if (lane >= o) pre += v;
+                }
+                const int total = __shfl_sync(0xffffffffu, pre, 31);
+                if (total == 0) break;
+                int at = pre - cnt;
+                for (uint32_t m = pend; m; m &= m - 1) wl[at++] = (uint16_t)(lane * 32 + __ffs(m) - 1);
                 done |= pend;
-                while (pend) {
-                    const int b = __ffs(pend) - 1;
-                    pend &= pend - 1;
-                    const int64_t y = w * 32 + b;
-                    for (int64_t e = rowptr[y]; e < rowptr[y + 1]; ++e) {
+                __syncwarp();
+                for (int i = lane; i < total; i += 32) {
+                    const int64_t y = c0 * 32 + wl[i];
+                    if (y >= e_rows) continue;
+                    const int64_t e1 = rowptr[y + 1];
+                    for (int64_t e = rowptr[y]; e < e1; ++e) {
                         const int32_t z = colidx[e];
                         const uint32_t bit = 1u << (z & 31);
                         if (!(row[z >> 5] & bit)) {
                             const uint32_t old = atomicOr(&row[z >> 5], bit);
-                            grew = grew || !(old & bit);
+                            if (!(old & bit)) {
+                                grew = true;
+                                if ((z >> 5) < c0) low = min(low, (int32_t)(z >> 5));
+                            }
                         }
                     }
                 }
                 __syncwarp();
             }
         }
-        __syncwarp();
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) low = min(low, __shfl_xor_sync(0xffffffffu, low, o));
         const bool any = __any_sync(0xffffffffu, grew);
+        if (lane == 0) pending[r] = low;
         if (any) {
             for (int64_t w = lane; w < words; w += 32) grow[w] = row[w];
             if (lane == 0) *changed = 1;
         }
         __syncwarp();
     }
-    (void)n;
 }
 
 // Left-form sweep Rnew[x] = R[x] | OR_{z in succ(x)} R[z] from the previous
@@ -126,7 +162,8 @@ __global__ void __launch_bounds__(128) k_closure_right(uint32_t* R, int64_t loca
 // so its sweep is exactly this Jacobi step and the sweep counts agree.
 __global__ void __launch_bounds__(256) k_closure_left(const uint32_t* __restrict__ R, uint32_t* __restrict__ Rnew,
                                                       int64_t n, int64_t words, const int64_t* __restrict__ rowptr,
-                                                      const int32_t* __restrict__ colidx, int* changed) {
+                                                      const int32_t* __restrict__ colidx, int64_t e_rows,
+                                                      int* changed) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t x = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); x < n; x += warps) {
@@ -134,7 +171,8 @@ __global__ void __launch_bounds__(256) k_closure_left(const uint32_t* __restrict
         for (int64_t w = lane; w < words; w += 32) {
             const uint32_t cur = R[x * words + w];
             uint32_t acc = cur;
-            for (int64_t e = rowptr[x]; e < rowptr[x + 1]; ++e) acc |= R[(int64_t)colidx[e] * words + w];
+            if (x < e_rows)
+                for (int64_t e = rowptr[x]; e < rowptr[x + 1]; ++e) acc |= R[(int64_t)colidx[e] * words + w];
             Rnew[x * words + w] = acc;
             grew = grew || (acc != cur);
         }
@@ -179,6 +217,46 @@ __global__ void __launch_bounds__(256) k_spmm(int64_t rows, const int64_t* __res
                 float* op = out + v * ldo + j;
                 *op = beta ? *op + acc : acc;
             }
+        }
+    }
+}
+
+// Dense → CSR, pass 1: nonzeros per row, and flags for negative / non-unit values.
+__global__ void k_dense_count(const float* in, int64_t rows, int64_t cols, int64_t* counts, int* flags) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+         r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+        int64_t cnt = 0;
+        bool neg = false, nonunit = false;
+        for (int64_t cc = lane; cc < cols; cc += 32) {
+            const float v = in[r * cols + cc];
+            if (v != 0.f) { cnt++; nonunit = nonunit || v != 1.f; }
+            neg = neg || v < 0.f;
+        }
+        for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+        if (__any_sync(0xffffffffu, neg) && lane == 0) atomicExch(&flags[0], 1);
+        if (__any_sync(0xffffffffu, nonunit) && lane == 0) atomicExch(&flags[1], 1);
+        if (lane == 0) counts[r] = cnt;
+    }
+}
+
+// Dense → CSR, pass 2: columns in ascending order per row (warp ballot compaction).
+__global__ void k_dense_fill(const float* in, int64_t rows, int64_t cols, const int64_t* rowptr, int32_t* colidx,
+                             float* vals) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+         r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+        int64_t pos = rowptr[r];
+        for (int64_t c0 = 0; c0 < cols; c0 += 32) {
+            const int64_t cc = c0 + lane;
+            const float v = cc < cols ? in[r * cols + cc] : 0.f;
+            const unsigned m = __ballot_sync(0xffffffffu, v != 0.f);
+            if (v != 0.f) {
+                const int64_t at = pos + __popc(m & ((1u << lane) - 1u));
+                colidx[at] = (int32_t)cc;
+                vals[at] = v;
+            }
+            pos += __popc(m);
         }
     }
 }
@@ -239,26 +317,87 @@ tl_status launch_bits_to_dense(tl_ctx* c, Tensor* t) {
     return L.done();
 }
 
-tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed) {
+tl_status launch_dense_to_csr(tl_ctx* c, Tensor* t) {
+    if (t->rank != 2) return fail(c, TL_ERR_UNSUPPORTED, "sparse storage needs rank 2");
+    if (t->shard == TL_SHARD_ROWS && c->world > 1) return fail(c, TL_ERR_UNSUPPORTED, "CSR of a sharded dense tensor");
+    TL_TRY(ensure_dense(c, t));
+    const int64_t rows = t->dims[0], cols = t->dims[1];
+    void* ws = nullptr;
+    TL_TRY(workspace(c, (size_t)(rows + 1) * 8 + 64, &ws));
+    int64_t* counts = (int64_t*)ws;
+    int* flags = (int*)(counts + rows + 1);
+    TL_CK(c, cudaMemsetAsync(flags, 0, 2 * sizeof(int), c->stream));
+    {
+        LaunchScope L(c, "dense_to_csr_count", (double)rows * cols * 4.0);
+        k_dense_count<<<grid_for(c, rows, 8), 256, 0, c->stream>>>(t->dense, rows, cols, counts, flags);
+        TL_TRY(L.done());
+    }
+    std::vector<int64_t> h(rows + 1, 0);
+    int hf[2];
+    TL_CK(c, cudaMemcpyAsync(h.data() + 1, counts, rows * 8, cudaMemcpyDeviceToHost, c->stream));
+    TL_CK(c, cudaMemcpyAsync(hf, flags, 2 * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    TL_CK(c, cudaStreamSynchronize(c->stream));
+    for (int64_t r = 0; r < rows; ++r) h[r + 1] += h[r];
+    const int64_t nnz = h[rows];
+    if (nnz > t->csr_cap || !t->rowptr || t->csr_rows != rows) {
+        cudaFree(t->rowptr); cudaFree(t->colidx); cudaFree(t->vals);
+        t->rowptr = nullptr; t->colidx = nullptr; t->vals = nullptr;
+        const int64_t cap = nnz > 0 ? nnz : 1;
+        TL_CK(c, cudaMalloc(&t->rowptr, (rows + 1) * 8));
+        TL_CK(c, cudaMalloc(&t->colidx, cap * 4));
+        TL_CK(c, cudaMalloc(&t->vals, cap * 4));
+        t->csr_cap = cap;
+    }
+    TL_CK(c, cudaMemcpyAsync(t->rowptr, h.data(), (rows + 1) * 8, cudaMemcpyHostToDevice, c->stream));
+    {
+        LaunchScope L(c, "dense_to_csr_fill", (double)rows * cols * 4.0);
+        k_dense_fill<<<grid_for(c, rows, 8), 256, 0, c->stream>>>(t->dense, rows, cols, t->rowptr, t->colidx, t->vals);
+        TL_TRY(L.done());
+    }
+    TL_CK(c, cudaStreamSynchronize(c->stream));   // h dies here
+    t->nnz = nnz;
+    t->csr_rows = rows;
+    t->csr_valid = true;
+    t->csr_nonneg = hf[0] == 0;
+    t->csr_ones = hf[1] == 0;
+    return TL_OK;
+}
+
+tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, int sweep) {
     const int64_t words = R->bits_words;
-    const int warps_per_block = 4;
-    const size_t smem = (size_t)warps_per_block * words * 4;
-    if (smem > 200 * 1024) return fail(c, TL_ERR_UNSUPPORTED, "closure rows of %lld bits exceed shared memory", (long long)R->dims[1]);
+    const size_t smem = (size_t)kClosureWarps * (words + kWindowWords * 16) * 4;
+    if (smem > 200 * 1024)
+        return fail(c, TL_ERR_UNSUPPORTED, "closure rows of %lld bits exceed shared memory", (long long)R->dims[1]);
     static size_t attr = 0;
     if (smem > 48 * 1024 && smem > attr) {
         TL_CK(c, cudaFuncSetAttribute(k_closure_right, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr = smem;
     }
     const int64_t rows = R->bits_rows;
-    // per sweep: read and write the local bit rows once, plus the CSR
+    // fixpoint-long state: the per-row pending word (0 = expand everything)
+    if ((size_t)rows * 4 > c->aux_cap) {
+        TL_CK(c, cudaStreamSynchronize(c->stream));
+        cudaFree(c->aux);
+        c->aux = nullptr;
+        c->aux_cap = 0;
+        TL_CK(c, cudaMalloc(&c->aux, std::max<size_t>((size_t)rows * 4, 4096)));
+        c->aux_cap = std::max<size_t>((size_t)rows * 4, 4096);
+    }
+    int32_t* pending = (int32_t*)c->aux;
+    if (sweep == 0 && rows > 0) TL_CK(c, cudaMemsetAsync(pending, 0, (size_t)rows * 4, c->stream));
+    unsigned long long* counter = reinterpret_cast<unsigned long long*>(c->d_flags + 16);
+    TL_CK(c, cudaMemsetAsync(counter, 0, sizeof(unsigned long long), c->stream));
+    // algorithmic bytes of one sweep: read and write the local bit rows, read the CSR
     const double bytes = (double)rows * words * 4.0 * 2.0 + (double)(E->csr_rows + 1) * 8.0 + (double)E->nnz * 4.0;
     LaunchScope L(c, "closure_sweep", bytes, 0);
-    const int blocks_per_sm = (int)std::max<size_t>(1, std::min<size_t>(16, (200 * 1024) / std::max<size_t>(smem, 1)));
-    unsigned grid = (unsigned)std::min<int64_t>((rows + warps_per_block - 1) / warps_per_block,
-                                                (int64_t)c->sm_count * blocks_per_sm);
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_closure_right, 32 * kClosureWarps, smem);
+    if (per_sm < 1) per_sm = 1;
+    int64_t grid = std::min<int64_t>((rows + kClosureWarps - 1) / kClosureWarps, (int64_t)c->sm_count * per_sm);
     if (grid < 1) grid = 1;
-    k_closure_right<<<grid, 32 * warps_per_block, smem, c->stream>>>(R->bits, rows, words, R->dims[1], E->rowptr,
-                                                                     E->colidx, d_changed);
+    k_closure_right<<<(unsigned)grid, 32 * kClosureWarps, smem, c->stream>>>(R->bits, rows, words, E->rowptr,
+                                                                            E->colidx, E->csr_rows, d_changed,
+                                                                            counter, pending);
     return L.done();
 }
 
@@ -270,7 +409,7 @@ tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed) {
     {
         LaunchScope L(c, "closure_left_sweep", (double)E->nnz * words * 4.0 + (double)n * words * 8.0, 0);
         k_closure_left<<<grid_for(c, n, 8), 256, 0, c->stream>>>(R->bits, (uint32_t*)ws, n, words, E->rowptr,
-                                                                 E->colidx, d_changed);
+                                                                 E->colidx, E->csr_rows, d_changed);
         TL_TRY(L.done());
     }
     TL_CK(c, cudaMemcpyAsync(R->bits, ws, bytes, cudaMemcpyDeviceToDevice, c->stream));

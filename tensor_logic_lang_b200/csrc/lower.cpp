@@ -666,6 +666,20 @@ static tl_status run_equation(tl_ctx* c, const tl_equation* eq) {
     p->has_contraction = a.has_contraction ? 1 : 0;
     p->atomic = inj ? 0 : 1;
     p->recursive = 0;
+    // element-wise with every operand indexed exactly like the LHS
+    p->aligned = (!a.has_contraction && bij) ? 1 : 0;
+    for (int r = 0; r < eq->n_refs && p->aligned; ++r) {
+        const tl_ref* ref = &eq->refs[r];
+        Tensor* t = find_defined(c, ref->tensor);
+        if (ref->rank != lhs->rank || (t && t->rank != lhs->rank)) { p->aligned = 0; break; }
+        for (int k = 0; k < ref->rank; ++k) {
+            if (ref->idx[k].kind != TL_IX_NAME || var_index(a.vars, ref->idx[k].name) != a.lhs_var[k] ||
+                (t && t->dims[k] != lhs->dims[k])) {
+                p->aligned = 0;
+                break;
+            }
+        }
+    }
     if (p->n_out > 0 && p->n_inner > 0) TL_TRY(launch_generic(c, *p, nullptr));
     // avg= divides the whole LHS by the product of its divisors (einsum.zig:151-195)
     if (eq->accum == TL_ACC_AVG && a.avg_div > 1) {
@@ -746,14 +760,16 @@ static ClosureForm match_closure(tl_ctx* c, const tl_equation* eq, Tensor** Rout
     if (!R || !E || R->rank != 2 || E->rank != 2) return NOT_CLOSURE;
     int64_t n = R->dims[0];
     std::string y = nm(r0, 1);
-    if (R->dims[1] != n || E->dims[0] != n || E->dims[1] != n) return NOT_CLOSURE;
+    // E may have fewer rows than n (its max dims come from constant-index
+    // assignments); the missing rows read as 0.0, i.e. have no successors
+    if (R->dims[1] != n || E->dims[0] > n || E->dims[1] != n) return NOT_CLOSURE;
     if (domain_size(c, x.c_str()) != n || domain_size(c, z.c_str()) != n || domain_size(c, y.c_str()) != n)
         return NOT_CLOSURE;
     if (!R->boolean) return NOT_CLOSURE;
     // step(r * e) == (r > 0) && (e > 0) needs e >= 0 (r is 0/1)
     if (!(E->csr_valid ? E->csr_nonneg : E->boolean)) return NOT_CLOSURE;
     // the sweeps read successor lists of every row: the relation is replicated
-    if (E->csr_valid && E->csr_rows != n) return NOT_CLOSURE;
+    if (E->csr_valid && E->csr_rows != E->dims[0]) return NOT_CLOSURE;
     if (form == CLOSURE_LEFT && R->shard == TL_SHARD_ROWS && c->world > 1) return NOT_CLOSURE;
     *Rout = R;
     *Eout = E;
@@ -812,11 +828,18 @@ static tl_status run_fixpoint(tl_ctx* c, const tl_equation* eqs, int n, int32_t*
     Tensor *R = nullptr, *E = nullptr;
     ClosureForm form = n == 1 ? match_closure(c, &eqs[0], &R, &E) : NOT_CLOSURE;
     // the bit-row sweeps read the relation's successor lists (CSR)
-    if (form != NOT_CLOSURE && !E->csr_valid) form = NOT_CLOSURE;
+    if (form != NOT_CLOSURE && !E->csr_valid) {
+        // a dense 0/1 relation (element assignments): build its successor lists
+        if (E->shard == TL_SHARD_ROWS && c->world > 1) form = NOT_CLOSURE;
+        else {
+            TL_TRY(launch_dense_to_csr(c, E));
+            if (!E->csr_nonneg) form = NOT_CLOSURE;
+        }
+    }
     if (form != NOT_CLOSURE) TL_TRY(ensure_bits(c, R));
     while (sweeps < max_sweeps && changed) {
         TL_CK(c, cudaMemsetAsync(d_changed, 0, sizeof(int), c->stream));
-        if (form == CLOSURE_RIGHT) TL_TRY(launch_closure_right(c, R, E, d_changed));
+        if (form == CLOSURE_RIGHT) TL_TRY(launch_closure_right(c, R, E, d_changed, sweeps));
         else if (form == CLOSURE_LEFT) TL_TRY(launch_closure_left(c, R, E, d_changed));
         else for (int i = 0; i < n; ++i) TL_TRY(generic_recursive(c, &eqs[i], d_changed));
         if (c->world > 1) TL_TRY(comm_allreduce_max_int(c, d_changed, 1));
@@ -909,6 +932,7 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
     TL_CK(c, cudaSetDevice(c->device));
     c->err.clear();
     c->query_out.clear();
+    c->domains.clear();   // a program's domains are its own (llvm.zig:133-140)
     // a fresh run: every tensor is absent until its first definition
     for (auto& kv : c->tensors) kv.second->defined = false;
     c->maxdims.clear();
@@ -947,5 +971,5 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
         c->query_out += buf.data();
         if (c->opts.verbose) fputs(buf.data(), stdout);
     }
-    return TL_OK;
+    return check_device_flags(c);
 }

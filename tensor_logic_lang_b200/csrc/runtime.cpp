@@ -310,6 +310,7 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     for (auto e : c->event_pool) cudaEventDestroy(e);
     if (c->comm) comm_destroy(c);
     cudaFree(c->ws);
+    cudaFree(c->aux);
     cudaFree(c->d_flags);
     cudaFreeHost(c->h_flags);
     cudaStreamDestroy(c->stream);
@@ -319,11 +320,25 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
 
 extern "C" const char* tl_last_error(const tl_ctx* c) { return c ? c->err.c_str() : "no context"; }
 
+namespace tl {
+// Device-side error words: [8] a tensor-core pipeline wait gave up.
+tl_status check_device_flags(tl_ctx* c) {
+    TL_CK(c, cudaMemcpyAsync(c->h_flags + 8, c->d_flags + 8, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    TL_CK(c, cudaStreamSynchronize(c->stream));
+    if (c->h_flags[8] != 0) {
+        c->h_flags[8] = 0;
+        TL_CK(c, cudaMemsetAsync(c->d_flags + 8, 0, sizeof(int), c->stream));
+        return fail(c, TL_ERR_CUDA, "a tensor-core pipeline wait timed out; results are invalid");
+    }
+    return TL_OK;
+}
+}  // namespace tl
+
 extern "C" tl_status tl_sync(tl_ctx* c) {
     if (!c) return TL_ERR_INVALID;
     TL_CK(c, cudaStreamSynchronize(c->stream));
     TL_CK(c, cudaGetLastError());
-    return TL_OK;
+    return check_device_flags(c);
 }
 
 extern "C" int32_t tl_last_sweeps(const tl_ctx* c) { return c ? c->last_sweeps : 0; }

@@ -101,6 +101,8 @@ struct tl_ctx {
     void* ws = nullptr;
     size_t ws_cap = 0;
     int* d_flags = nullptr;     // [0..63] changed / error words
+    void* aux = nullptr;        // state kept across the sweeps of one fixpoint
+    size_t aux_cap = 0;
     int* h_flags = nullptr;     // pinned mirror
 
     // profiling
@@ -139,6 +141,9 @@ struct LaunchScope {
     }
     tl_status done() { return launch_end(c, ev); }
 };
+
+// device-side error words (pipeline timeouts); syncs the stream
+tl_status check_device_flags(tl_ctx* c);
 
 // scratch workspace (grown on demand, never shrunk)
 tl_status workspace(tl_ctx* c, size_t bytes, void** out);
@@ -191,6 +196,7 @@ struct GenericPlan {
     int32_t atomic;              // several threads may hit one LHS element
     int32_t recursive;           // fixpoint sweep: report increases in *changed
     int32_t virt_pos_var;
+    int32_t aligned;             // element-wise, every operand shaped and indexed like the LHS
 };
 
 tl_status launch_generic(tl_ctx* c, const GenericPlan& p, int* d_changed);
@@ -235,7 +241,8 @@ tl_status launch_csr_to_dense(tl_ctx* c, Tensor* t);
 tl_status launch_csr_to_bits(tl_ctx* c, Tensor* t, Tensor* out);
 tl_status launch_dense_to_bits(tl_ctx* c, Tensor* t);
 tl_status launch_bits_to_dense(tl_ctx* c, Tensor* t);
-tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed);
+tl_status launch_dense_to_csr(tl_ctx* c, Tensor* t);
+tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, int sweep);
 tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed);
 
 // elementwise gradient rules

@@ -85,6 +85,17 @@ def test_gemm(ctx, oracle_lib, case):
     assert_close(got, want, tol, "C")
 
 
+MN_CASES = [c for c in GEMM_CASES if "km" in (c[3],) or c[4] == "kn"]
+
+
+@pytest.mark.parametrize("case", MN_CASES, ids=[f"{c[0]}x{c[1]}x{c[2]}-{c[3]}{c[4]}{c[5]}-{c[6]}" for c in MN_CASES])
+def test_gemm_mn_major_descriptors(ctx, oracle_lib, case, monkeypatch):
+    """The same GEMMs with MN-major operands read by the tensor cores directly
+    (128-byte swizzle with 32-byte atoms) instead of through a transposing copy."""
+    monkeypatch.setenv("TL_GEMM_MN", "1")
+    test_gemm(ctx, oracle_lib, case)
+
+
 # ----------------------------------------------------------------------------- row-wise
 ROW_CASES = [(3, 10), (2048, 2048), (64, 1000), (5, 5000), (1024, 10), (7, 129)]
 
