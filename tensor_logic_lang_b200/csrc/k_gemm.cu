@@ -224,7 +224,7 @@ struct TcCfg {
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const __grid_constant__ TcEpi epi, int num_kb) {
+              const __grid_constant__ TcEpi epi, int num_kb, int kb_per_split) {
     using Cfg = TcCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -235,6 +235,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * BN;
+    // this CTA's K range: k-blocks [kb_first, kb_first + n_kb) of num_kb
+    const int kb_first = blockIdx.z * kb_per_split;
+    const int n_kb = min(kb_per_split, num_kb - kb_first);
+    const bool split_k = gridDim.z > 1;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -256,14 +260,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            for (int kb = 0; kb < num_kb; ++kb) {
+            for (int kb = 0; kb < n_kb; ++kb) {
                 const int s = kb % Cfg::STAGES;
                 const uint32_t ph = (kb / Cfg::STAGES) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, epi.err)) break;
                 uint8_t* sa = smem + s * Cfg::STAGE;
                 uint8_t* sb = sa + Cfg::A_BYTES;
                 mbar_expect_tx(&full[s], Cfg::STAGE);
-                const int k0 = kb * TC_BK;
+                const int k0 = (kb_first + kb) * TC_BK;
                 if (!A_MN) {
                     tma_load_2d(sa, &tmA, &full[s], k0, m0);
                 } else {
@@ -286,7 +290,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                    | ((uint32_t)(BN >> 3) << 17)     // N
                                    | ((uint32_t)(TC_BM >> 4) << 24); // M
         bool ok = true;
-        for (int kb = 0; kb < num_kb && ok; ++kb) {
+        for (int kb = 0; kb < n_kb && ok; ++kb) {
             const int s = kb % Cfg::STAGES;
             const uint32_t ph = (kb / Cfg::STAGES) & 1;
             ok = mbar_wait(&full[s], ph, epi.err);
@@ -318,7 +322,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const bool ok = mbar_wait(accum_full, 0, epi.err);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int64_t row = (int64_t)m0 + q * 32 + lane;
-        if (ok) {
+        if (ok && n_kb > 0 && split_k) {
+            // partial tile of a split K range: add into C
+#pragma unroll 1
+            for (int ch = 0; ch < BN / 16; ++ch) {
+                float v[16];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + ch * 16, v);
+                if (row >= epi.M) continue;
+                const int64_t col0 = (int64_t)n0 + ch * 16;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (col0 + j < epi.N) atomicAdd(epi.C + row * epi.scm + (col0 + j) * epi.scn, v[j] * epi.mag);
+            }
+        } else if (ok && !split_k) {
 #pragma unroll 1
             for (int ch = 0; ch < BN / 16; ++ch) {
                 float v[16];
@@ -372,44 +388,63 @@ __device__ __forceinline__ float tf32_rna(float x) {
     return __uint_as_float(r);
 }
 
-// relu sign split into K-major copies: Ap[m, 0:K] = max(A,0), Ap[m, K:2K] = max(-A,0);
-// Bp[n, 0:K] = max(sB,0), Bp[n, K:2K] = max(-sB,0) with s the sign of the scale.
-__global__ void k_split_a(const float* __restrict__ A, int64_t sam, int64_t sak, int64_t M, int64_t K, int64_t ldp,
-                          float* __restrict__ Ap, int split) {
-    const int64_t total = M * K;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t m = i / K, k = i % K;
-        const float a = A[m * sam + k * sak];
-        if (split) {
-            Ap[m * ldp + k] = tf32_rna(fmaxf(a, 0.f));
-            Ap[m * ldp + K + k] = tf32_rna(fmaxf(-a, 0.f));
-        } else {
-            Ap[m * ldp + k] = tf32_rna(a);
-        }
+// Tensor-core operand copies.  An operand is viewed as R rows (M or N) by K;
+// the copy holds nseg segments of K values each, segment s transformed by
+// op s (4 bits each in `ops`), applied to x = sgn * source:
+//   OP_RN   round(x)                      plain TF32 operand
+//   OP_LO   round(x - round(x))           low part (3xTF32: hi*hi + hi*lo + lo*hi)
+//   OP_POS  round(max(x, 0))              relu sign split: a+ b+ + a- b-
+//   OP_NEG  round(max(-x, 0))
+enum { OP_RN = 0, OP_LO = 1, OP_POS = 2, OP_NEG = 3 };
+
+__device__ __forceinline__ float seg_op(int op, float x) {
+    switch (op) {
+    case OP_LO: { const float h = tf32_rna(x); return tf32_rna(x - h); }
+    case OP_POS: return tf32_rna(fmaxf(x, 0.f));
+    case OP_NEG: return tf32_rna(fmaxf(-x, 0.f));
+    default: return tf32_rna(x);
     }
 }
 
-// Transposing copy through shared memory (coalesced both ways) of a [R x C]
-// view with arbitrary strides into a row-major [C x ld] block, optional split.
-__global__ void k_transpose_split(const float* __restrict__ S, int64_t s_r, int64_t s_c, int64_t R, int64_t Cn,
-                                  float* __restrict__ D, int64_t ld, float sgn, int split) {
+// K-major copy dst[r * ld + s * K + k], k fastest (coalesced for K-contiguous sources).
+__global__ void k_prep_kmajor(const float* __restrict__ S, int64_t s_r, int64_t s_k, int64_t R, int64_t K, int nseg,
+                              unsigned ops, float sgn, float* __restrict__ D, int64_t ld) {
+    const int64_t total = R * K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / K, k = i % K;
+        const float x = S[r * s_r + k * s_k] * sgn;
+        for (int s = 0; s < nseg; ++s) D[r * ld + s * K + k] = seg_op((ops >> (4 * s)) & 15, x);
+    }
+}
+
+// MN-major copy dst[(s * K + k) * ld + r], r fastest (coalesced for R-contiguous sources).
+__global__ void k_prep_mnmajor(const float* __restrict__ S, int64_t s_r, int64_t s_k, int64_t R, int64_t K, int nseg,
+                               unsigned ops, float sgn, float* __restrict__ D, int64_t ld) {
+    const int64_t total = R * K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t k = i / R, r = i % R;
+        const float x = S[r * s_r + k * s_k] * sgn;
+        for (int s = 0; s < nseg; ++s) D[(s * K + k) * ld + r] = seg_op((ops >> (4 * s)) & 15, x);
+    }
+}
+
+// K-major copy of a source with any strides, through 32 x 33 shared-memory
+// tiles so both the reads (along the source's fastest dim) and the writes
+// (along k) coalesce.
+__global__ void k_prep_transpose(const float* __restrict__ S, int64_t s_r, int64_t s_k, int64_t R, int64_t K,
+                                 int nseg, unsigned ops, float sgn, float* __restrict__ D, int64_t ld) {
     __shared__ float tile[32][33];
-    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+    const int64_t r0 = (int64_t)blockIdx.x * 32, k0 = (int64_t)blockIdx.y * 32;
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int64_t r = r0 + i, cc = c0 + threadIdx.x;
-        tile[i][threadIdx.x] = (r < R && cc < Cn) ? S[r * s_r + cc * s_c] * sgn : 0.f;
+        const int64_t k = k0 + i, r = r0 + threadIdx.x;   // read along r
+        tile[i][threadIdx.x] = (r < R && k < K) ? S[r * s_r + k * s_k] * sgn : 0.f;
     }
     __syncthreads();
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int64_t cc = c0 + i, r = r0 + threadIdx.x;
-        if (cc < Cn && r < R) {
-            const float v = tile[threadIdx.x][i];
-            if (split) {
-                D[cc * ld + r] = tf32_rna(fmaxf(v, 0.f));
-                D[cc * ld + R + r] = tf32_rna(fmaxf(-v, 0.f));
-            } else {
-                D[cc * ld + r] = tf32_rna(v);
-            }
+        const int64_t r = r0 + i, k = k0 + threadIdx.x;   // write along k
+        if (r < R && k < K) {
+            const float x = tile[threadIdx.x][i];
+            for (int s = 0; s < nseg; ++s) D[r * ld + s * K + k] = seg_op((ops >> (4 * s)) & 15, x);
         }
     }
 }
@@ -450,15 +485,9 @@ bool make_map(CUtensorMap* map, const float* base, int64_t x, int64_t y, int64_t
     return r == CUDA_SUCCESS;
 }
 
-struct Operand {
-    const float* ptr;
-    int64_t rows_stride;   // stride of the non-contiguous dim (elements)
-    bool mn_major;         // contiguous along M (or N)
-};
-
 template <int BN, bool AM, bool BM>
 tl_status launch_tc_inst(tl_ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const TcEpi& e, int64_t M, int64_t N,
-                         int num_kb) {
+                         int num_kb, int kb_per_split, int splits) {
     using Cfg = TcCfg<BN>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -467,18 +496,18 @@ tl_status launch_tc_inst(tl_ctx* c, const CUtensorMap& ma, const CUtensorMap& mb
             return fail(c, TL_ERR_CUDA, "cannot reserve %d bytes of shared memory", Cfg::SMEM);
         attr_set = true;
     }
-    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + TC_BM - 1) / TC_BM));
-    k_gemm_tc<BN, AM, BM><<<grid, TC_THREADS, Cfg::SMEM, c->stream>>>(ma, mb, e, num_kb);
+    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + TC_BM - 1) / TC_BM), (unsigned)splits);
+    k_gemm_tc<BN, AM, BM><<<grid, TC_THREADS, Cfg::SMEM, c->stream>>>(ma, mb, e, num_kb, kb_per_split);
     return TL_OK;
 }
 
 template <int BN>
 tl_status launch_tc_bn(tl_ctx* c, bool am, bool bm, const CUtensorMap& ma, const CUtensorMap& mb, const TcEpi& e,
-                       int64_t M, int64_t N, int num_kb) {
-    if (!am && !bm) return launch_tc_inst<BN, false, false>(c, ma, mb, e, M, N, num_kb);
-    if (am && !bm) return launch_tc_inst<BN, true, false>(c, ma, mb, e, M, N, num_kb);
-    if (!am && bm) return launch_tc_inst<BN, false, true>(c, ma, mb, e, M, N, num_kb);
-    return launch_tc_inst<BN, true, true>(c, ma, mb, e, M, N, num_kb);
+                       int64_t M, int64_t N, int num_kb, int kb_per_split, int splits) {
+    if (!am && !bm) return launch_tc_inst<BN, false, false>(c, ma, mb, e, M, N, num_kb, kb_per_split, splits);
+    if (am && !bm) return launch_tc_inst<BN, true, false>(c, ma, mb, e, M, N, num_kb, kb_per_split, splits);
+    if (!am && bm) return launch_tc_inst<BN, false, true>(c, ma, mb, e, M, N, num_kb, kb_per_split, splits);
+    return launch_tc_inst<BN, true, true>(c, ma, mb, e, M, N, num_kb, kb_per_split, splits);
 }
 
 bool env_flag(const char* name) {
@@ -544,70 +573,74 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
               macs >= (double)(1 << 25);
     if (!tc) return launch_simt(c, p);
 
-    // Operand layouts.  A[m,k]: K-major when sak == 1, MN-major when sam == 1.
-    // B[k,n] as the UMMA "B" (N x K): K-major when sbk == 1, MN-major when sbn == 1.
-    // MN-major operand descriptors are opt-in (TL_GEMM_MN=1) until validated;
-    // by default MN-major operands go through a K-major transposing copy.
-    const bool no_mn = !env_flag("TL_GEMM_MN");
+    // Every tensor-core operand is copied once into the workspace, rounded to
+    // TF32 (nearest; the hardware would truncate), with the K segments of the
+    // chosen precision: plain, relu sign split (2K), or 3xTF32 (3K, fp32-class
+    // accuracy for tensors whose sign a later step / relu gradient tests).
+    // A copy keeps its source's orientation when that is K- or MN-contiguous
+    // (a streaming copy; MN-major tiles feed the tensor cores directly) and
+    // becomes K-major through shared-memory tiles otherwise.
+    const bool use_mn = !env_flag("TL_GEMM_NO_MN");
     const bool split = p.relu_term != 0;
+    const bool precise = !split && p.precise != 0;
     const float sgn = p.scale < 0.f ? -1.f : 1.f;
-    const int64_t Ke = split ? 2 * p.K : p.K;
-    const int64_t Kpad = (Ke + 3) & ~int64_t(3);   // 16-byte row strides for TMA
-    Operand A{p.A, 0, false}, B{p.B, 0, false};
-    bool a_ok = false, b_ok = false;
-    if (!split && p.sak == 1 && (p.sam % 4) == 0 && ((uintptr_t)p.A % 16) == 0) { A.rows_stride = p.sam; a_ok = true; }
-    else if (!split && !no_mn && p.sam == 1 && (p.sak % 4) == 0 && ((uintptr_t)p.A % 16) == 0) {
-        A.rows_stride = p.sak; A.mn_major = true; a_ok = true;
-    }
-    if (!split && p.sbk == 1 && (p.sbn % 4) == 0 && ((uintptr_t)p.B % 16) == 0) { B.rows_stride = p.sbn; b_ok = true; }
-    else if (!split && !no_mn && p.sbn == 1 && (p.sbk % 4) == 0 && ((uintptr_t)p.B % 16) == 0) {
-        B.rows_stride = p.sbk; B.mn_major = true; b_ok = true;
-    }
-    // prep copies (sign split, transposes) live in the workspace
+    const int nseg = split ? 2 : precise ? 3 : 1;
+    const unsigned ops_a = split ? (OP_POS | OP_NEG << 4) : precise ? (OP_RN | OP_RN << 4 | OP_LO << 8) : OP_RN;
+    const unsigned ops_b = split ? (OP_POS | OP_NEG << 4) : precise ? (OP_RN | OP_LO << 4 | OP_RN << 8) : OP_RN;
+    const int64_t Ke = nseg * p.K;
+    struct Prep { int64_t R, s_r, s_k; unsigned ops; float sgn; bool mn; int64_t ld; float* dst; const char* name; };
+    Prep pa{p.M, p.sam, p.sak, ops_a, 1.f, use_mn && p.sak != 1 && p.sam == 1, 0, nullptr, "gemm_prep_a"};
+    Prep pb{p.N, p.sbn, p.sbk, ops_b, split ? sgn : 1.f, use_mn && p.sbk != 1 && p.sbn == 1, 0, nullptr,
+            "gemm_prep_b"};
     size_t need = 0;
-    if (!a_ok) need += (size_t)p.M * Kpad * 4 + 256;
-    if (!b_ok) need += (size_t)p.N * Kpad * 4 + 256;
+    for (Prep* q : {&pa, &pb}) {
+        q->ld = q->mn ? ((q->R + 3) & ~int64_t(3)) : ((Ke + 3) & ~int64_t(3));   // 16-byte row strides
+        need += (((size_t)(q->mn ? Ke : q->R) * q->ld * 4) + 255) & ~size_t(255);
+    }
     void* ws = nullptr;
-    if (need) TL_TRY(workspace(c, need, &ws));
+    TL_TRY(workspace(c, need, &ws));
     uint8_t* wp = (uint8_t*)ws;
-    if (!a_ok) {
-        float* Ap = (float*)wp;
-        wp += ((size_t)p.M * Kpad * 4 + 255) & ~size_t(255);
-        if (Kpad != Ke) TL_CK(c, cudaMemsetAsync(Ap, 0, (size_t)p.M * Kpad * 4, c->stream));
-        LaunchScope L(c, "gemm_prep_a", (double)p.M * p.K * 4.0 + (double)p.M * Ke * 4.0);
-        if (p.sak == 1 || p.sam != 1) {
-            int64_t blocks = (p.M * p.K + 255) / 256;
-            if (blocks > (int64_t)c->sm_count * 32) blocks = (int64_t)c->sm_count * 32;
-            k_split_a<<<(unsigned)blocks, 256, 0, c->stream>>>(p.A, p.sam, p.sak, p.M, p.K, Kpad, Ap, split ? 1 : 0);
+    for (Prep* q : {&pa, &pb}) {
+        q->dst = (float*)wp;
+        wp += (((size_t)(q->mn ? Ke : q->R) * q->ld * 4) + 255) & ~size_t(255);
+        const float* src = q == &pa ? p.A : p.B;
+        LaunchScope L(c, q->name, (double)q->R * p.K * 4.0 * (1 + nseg));
+        int64_t blocks = (q->R * p.K + 255) / 256;
+        if (blocks > (int64_t)c->sm_count * 32) blocks = (int64_t)c->sm_count * 32;
+        if (q->mn) {
+            k_prep_mnmajor<<<(unsigned)blocks, 256, 0, c->stream>>>(src, q->s_r, q->s_k, q->R, p.K, nseg, q->ops,
+                                                                   q->sgn, q->dst, q->ld);
+        } else if (q->s_k == 1) {
+            k_prep_kmajor<<<(unsigned)blocks, 256, 0, c->stream>>>(src, q->s_r, q->s_k, q->R, p.K, nseg, q->ops,
+                                                                  q->sgn, q->dst, q->ld);
         } else {
-            // A is M-contiguous: view it as [K x M] and transpose
-            dim3 g((unsigned)((p.M + 31) / 32), (unsigned)((p.K + 31) / 32));
-            k_transpose_split<<<g, dim3(32, 8), 0, c->stream>>>(p.A, p.sak, p.sam, p.K, p.M, Ap, Kpad, 1.f, split ? 1 : 0);
+            dim3 g((unsigned)((q->R + 31) / 32), (unsigned)((p.K + 31) / 32));
+            k_prep_transpose<<<g, dim3(32, 8), 0, c->stream>>>(src, q->s_r, q->s_k, q->R, p.K, nseg, q->ops, q->sgn,
+                                                              q->dst, q->ld);
         }
         TL_TRY(L.done());
-        A = {Ap, Kpad, false};
     }
-    if (!b_ok) {
-        float* Bp = (float*)wp;
-        if (Kpad != Ke) TL_CK(c, cudaMemsetAsync(Bp, 0, (size_t)p.N * Kpad * 4, c->stream));
-        LaunchScope L(c, "gemm_prep_b", (double)p.N * p.K * 4.0 + (double)p.N * Ke * 4.0);
-        // B[k,n] → Bp[n, k] (K-major), times the scale's sign, optional split
-        dim3 g((unsigned)((p.N + 31) / 32), (unsigned)((p.K + 31) / 32));
-        k_transpose_split<<<g, dim3(32, 8), 0, c->stream>>>(p.B, p.sbk, p.sbn, p.K, p.N, Bp, Kpad, split ? sgn : 1.f,
-                                                            split ? 1 : 0);
-        TL_TRY(L.done());
-        B = {Bp, Kpad, false};
-    }
-    // each map spans only its own operand's K extent; TMA reads zeros past it
-    const int64_t Ka = a_ok ? p.K : Kpad, Kb = b_ok ? p.K : Kpad;
-    const int64_t Kx = Ka > Kb ? Ka : Kb;
+    // the maps span Ke; TMA reads zeros past it (the K tail of the last block)
     CUtensorMap ma, mb;
-    bool ok = A.mn_major ? make_map(&ma, A.ptr, p.M, Ka, A.rows_stride, 32, true)
-                         : make_map(&ma, A.ptr, Ka, p.M, A.rows_stride, TC_BM, false);
     const int BN = p.N >= 256 && (p.N % 256 == 0 || p.N >= 1024) ? 256 : (p.N >= 128 ? 128 : 64);
-    ok = ok && (B.mn_major ? make_map(&mb, B.ptr, p.N, Kb, B.rows_stride, 32, true)
-                           : make_map(&mb, B.ptr, Kb, p.N, B.rows_stride, BN, false));
+    bool ok = pa.mn ? make_map(&ma, pa.dst, p.M, Ke, pa.ld, 32, true) : make_map(&ma, pa.dst, Ke, p.M, pa.ld, TC_BM, false);
+    ok = ok && (pb.mn ? make_map(&mb, pb.dst, p.N, Ke, pb.ld, 32, true) : make_map(&mb, pb.dst, Ke, p.N, pb.ld, BN, false));
     if (!ok) return launch_simt(c, p);
+    const int num_kb = (int)((Ke + TC_BK - 1) / TC_BK);
+    // split K when the output tiles cannot fill the SMs (each split >= 4 k-blocks)
+    const int64_t tiles = ((p.N + BN - 1) / BN) * ((p.M + TC_BM - 1) / TC_BM);
+    int splits = 1;
+    if (!p.epi_relu && tiles < c->sm_count && num_kb >= 8) {
+        splits = (int)std::min<int64_t>((c->sm_count + tiles - 1) / tiles, num_kb / 4);
+        if (splits < 1) splits = 1;
+    }
+    const int kb_per_split = (num_kb + splits - 1) / splits;
+    splits = (num_kb + kb_per_split - 1) / kb_per_split;
+    if (splits > 1 && !p.beta) {
+        GemmPlan z = p;   // zero C (a K = 0 pass honours its strides), then add partial tiles
+        z.K = 0;
+        TL_TRY(launch_simt(c, z));
+    }
     TcEpi e;
     e.C = p.C; e.scm = p.scm; e.scn = p.scn;
     e.D = p.D; e.sdm = p.sdm; e.sdn = p.sdn;
@@ -615,12 +648,11 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     e.mag = split ? fabsf(p.scale) : p.scale;
     e.beta = p.beta; e.epi_relu = p.epi_relu;
     e.err = c->d_flags + 8;
-    const int num_kb = (int)((Kx + TC_BK - 1) / TC_BK);
     LaunchScope L(c, "gemm_tcgen05_tf32", (double)(p.M * p.K + p.K * p.N + p.M * p.N * (1 + p.beta)) * 4.0,
                   2.0 * p.M * p.N * p.K);
-    if (BN == 256) TL_TRY(launch_tc_bn<256>(c, A.mn_major, B.mn_major, ma, mb, e, p.M, p.N, num_kb));
-    else if (BN == 128) TL_TRY(launch_tc_bn<128>(c, A.mn_major, B.mn_major, ma, mb, e, p.M, p.N, num_kb));
-    else TL_TRY(launch_tc_bn<64>(c, A.mn_major, B.mn_major, ma, mb, e, p.M, p.N, num_kb));
+    if (BN == 256) TL_TRY(launch_tc_bn<256>(c, pa.mn, pb.mn, ma, mb, e, p.M, p.N, num_kb, kb_per_split, splits));
+    else if (BN == 128) TL_TRY(launch_tc_bn<128>(c, pa.mn, pb.mn, ma, mb, e, p.M, p.N, num_kb, kb_per_split, splits));
+    else TL_TRY(launch_tc_bn<64>(c, pa.mn, pb.mn, ma, mb, e, p.M, p.N, num_kb, kb_per_split, splits));
     return L.done();
 }
 

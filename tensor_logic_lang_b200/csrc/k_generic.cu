@@ -190,53 +190,70 @@ __global__ void k_generic(const __grid_constant__ GenericPlan p, int* changed, i
     }
 }
 
-// Small outputs with long contractions: one block per LHS element, the
-// contracted range split across the block's threads and combined with a
-// tree reduction in f64.  The operator must be associative (sum, max, min,
-// product); the order of the partial folds differs from the reference's
-// sequential loop only in f64 rounding of sums.
-__global__ void __launch_bounds__(256) k_generic_reduce(const __grid_constant__ GenericPlan p) {
+// Small outputs with long contractions: block (o, s) folds slice s of LHS
+// element o's contracted range with its 256 threads and a tree in f64, and
+// a second pass folds the slices in order and merges the LHS's old value.
+// The operator must be associative (sum, max, min, product); the order of
+// the partial folds differs from the reference's sequential loop only in
+// f64 rounding of sums.
+__device__ __forceinline__ double fold_op(int accum, double a, double b) {
+    switch (accum) {
+    case TL_ACC_MAX: return b > a ? b : a;
+    case TL_ACC_MIN: return b < a ? b : a;
+    case TL_ACC_MUL: return a * b;
+    default: return a + b;
+    }
+}
+
+__device__ __forceinline__ double fold_ident(int accum) {
+    return accum == TL_ACC_MAX ? -INFINITY : accum == TL_ACC_MIN ? INFINITY : accum == TL_ACC_MUL ? 1.0 : 0.0;
+}
+
+__global__ void __launch_bounds__(256) k_generic_reduce(const __grid_constant__ GenericPlan p, double* partial,
+                                                        int64_t chunk) {
     __shared__ double sh[256];
-    const bool is_max = p.accum == TL_ACC_MAX, is_min = p.accum == TL_ACC_MIN, is_mul = p.accum == TL_ACC_MUL;
-    const double ident = is_max ? -INFINITY : is_min ? INFINITY : is_mul ? 1.0 : 0.0;
-    for (int64_t o = blockIdx.x; o < p.n_out; o += gridDim.x) {
+    const int64_t o = blockIdx.x, s = blockIdx.y;
+    int64_t iv[kMaxVars];
+    int64_t rem = o;
+    for (int v = p.n_free - 1; v >= 0; --v) {
+        iv[v] = rem % p.sizes[v];
+        rem /= p.sizes[v];
+    }
+    double acc = fold_ident(p.accum);
+    const int64_t j1 = (s + 1) * chunk < p.n_inner ? (s + 1) * chunk : p.n_inner;
+    for (int64_t j = s * chunk + threadIdx.x; j < j1; j += blockDim.x) {
+        int64_t r = j;
+        for (int v = p.n_vars - 1; v >= p.n_free; --v) {
+            iv[v] = r % p.sizes[v];
+            r /= p.sizes[v];
+        }
+        acc = fold_op(p.accum, acc, eval(p, iv));
+    }
+    sh[threadIdx.x] = acc;
+    __syncthreads();
+    for (int h = blockDim.x / 2; h > 0; h >>= 1) {
+        if (threadIdx.x < h) sh[threadIdx.x] = fold_op(p.accum, sh[threadIdx.x], sh[threadIdx.x + h]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) partial[o * gridDim.y + s] = sh[0];
+}
+
+__global__ void k_generic_reduce_finish(const __grid_constant__ GenericPlan p, const double* partial, int nsplit) {
+    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < p.n_out; o += (int64_t)gridDim.x * blockDim.x) {
         int64_t iv[kMaxVars];
         int64_t rem = o;
         for (int v = p.n_free - 1; v >= 0; --v) {
             iv[v] = rem % p.sizes[v];
             rem /= p.sizes[v];
         }
-        double acc = ident;
-        for (int64_t j = threadIdx.x; j < p.n_inner; j += blockDim.x) {
-            int64_t r = j;
-            for (int v = p.n_vars - 1; v >= p.n_free; --v) {
-                iv[v] = r % p.sizes[v];
-                r /= p.sizes[v];
-            }
-            const double t = eval(p, iv);
-            acc = is_max ? (t > acc ? t : acc) : is_min ? (t < acc ? t : acc) : is_mul ? acc * t : acc + t;
+        double part = fold_ident(p.accum);
+        for (int s = 0; s < nsplit; ++s) part = fold_op(p.accum, part, partial[o * nsplit + s]);
+        int64_t off = 0;
+        for (int k = 0; k < p.n_lhs_terms; ++k) off += (iv[p.lhs_var[k]] / p.lhs_div[k]) * p.lhs_stride[k];
+        if (off >= 0 && off < p.lhs_total) {
+            const double old = p.old_zero ? 0.0 : (double)p.lhs[off];
+            p.lhs[off] = (float)fold_op(p.accum, old, part);
         }
-        sh[threadIdx.x] = acc;
-        __syncthreads();
-        for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-            if (threadIdx.x < s) {
-                const double a = sh[threadIdx.x], b = sh[threadIdx.x + s];
-                sh[threadIdx.x] = is_max ? (b > a ? b : a) : is_min ? (b < a ? b : a) : is_mul ? a * b : a + b;
-            }
-            __syncthreads();
-        }
-        if (threadIdx.x == 0) {
-            int64_t off = 0;
-            for (int k = 0; k < p.n_lhs_terms; ++k) off += (iv[p.lhs_var[k]] / p.lhs_div[k]) * p.lhs_stride[k];
-            if (off >= 0 && off < p.lhs_total) {
-                const double old = p.old_zero ? 0.0 : (double)p.lhs[off];
-                const double part = sh[0];
-                const double nv = is_max ? (part > old ? part : old) : is_min ? (part < old ? part : old)
-                                : is_mul ? old * part : old + part;
-                p.lhs[off] = (float)nv;
-            }
-        }
-        __syncthreads();
     }
 }
 
@@ -324,9 +341,23 @@ tl_status launch_generic(tl_ctx* c, const GenericPlan& p, int* d_changed) {
                                              p.accum == TL_ACC_AVG || p.accum == TL_ACC_MAX ||
                                              p.accum == TL_ACC_MIN || p.accum == TL_ACC_MUL);
     if (assoc && !p.recursive && !p.atomic && p.n_inner >= 512 && p.n_out < (int64_t)c->sm_count * 64) {
-        int64_t blocks = p.n_out < (int64_t)c->sm_count * 8 ? p.n_out : (int64_t)c->sm_count * 8;
-        LaunchScope L(c, "generic_reduce", terms * 4.0 * p.n_refs, terms * 2.0);
-        k_generic_reduce<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, c->stream>>>(p);
+        // slices of >= 1024 terms, enough blocks to cover the SMs four times
+        int64_t nsplit = ((int64_t)c->sm_count * 4 + p.n_out - 1) / p.n_out;
+        const int64_t max_split = (p.n_inner + 1023) / 1024;
+        if (nsplit > max_split) nsplit = max_split;
+        if (nsplit > 65535) nsplit = 65535;
+        if (nsplit < 1) nsplit = 1;
+        const int64_t chunk = (p.n_inner + nsplit - 1) / nsplit;
+        void* ws = nullptr;
+        TL_TRY(workspace(c, (size_t)p.n_out * nsplit * sizeof(double) + 64, &ws));
+        {
+            LaunchScope L(c, "generic_reduce", terms * 4.0 * p.n_refs, terms * 2.0);
+            k_generic_reduce<<<dim3((unsigned)p.n_out, (unsigned)nsplit), 256, 0, c->stream>>>(p, (double*)ws, chunk);
+            TL_TRY(L.done());
+        }
+        LaunchScope L(c, "generic_reduce_finish", (double)p.n_out * nsplit * 8.0, 0);
+        k_generic_reduce_finish<<<(unsigned)((p.n_out + 127) / 128), 128, 0, c->stream>>>(p, (const double*)ws,
+                                                                                          (int)nsplit);
         return L.done();
     }
     const int threads = 128;

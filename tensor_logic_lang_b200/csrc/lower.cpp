@@ -360,6 +360,7 @@ tl_status try_gemm(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* 
     g.sbk = tB->strides[bk]; g.sbn = tB->strides[1 - bk];
     g.scale = m.scale;
     g.relu_term = m.relu_term ? 1 : 0;
+    g.precise = std::find(c->sign_sensitive.begin(), c->sign_sensitive.end(), lhs->name) != c->sign_sensitive.end();
     g.beta = lhs->zero ? 0 : 1;
     if (g.beta) TL_TRY(ensure_dense(c, lhs));
     else TL_TRY(alloc_dense_public(c, lhs));
@@ -942,6 +943,25 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
     for (int i = 0; i < n; ++i)
         if (s[i].kind == TL_STMT_EQUATION) eqs.push_back(s[i].eq);
     TL_TRY(tl_declare_dims(c, eqs.data(), (int)eqs.size()));
+    // sign-sensitive tensors: step / comparison arguments, and relu arguments
+    // when a backward pass will take relu's gradient step(x)
+    bool has_backward = false;
+    for (int i = 0; i < n; ++i) has_backward = has_backward || s[i].kind == TL_STMT_BACKWARD;
+    c->sign_sensitive.clear();
+    for (const tl_equation& e : eqs) {
+        for (int i = 1; i < e.n_code && i < TL_MAX_CODE; ++i) {
+            const tl_instr& in = e.code[i];
+            const bool tests_sign = (in.op == TL_OP_NL && (in.arg == TL_NL_STEP || (in.arg == TL_NL_RELU && has_backward))) ||
+                                    (in.op >= TL_OP_GT && in.op <= TL_OP_NE);
+            if (!tests_sign) continue;
+            for (int back = 1; back <= 2 && i - back >= 0; ++back) {
+                const tl_instr& prev = e.code[i - back];
+                if (prev.op == TL_OP_REF && prev.arg >= 0 && prev.arg < e.n_refs)
+                    c->sign_sensitive.push_back(e.refs[prev.arg].tensor);
+                if (in.op == TL_OP_NL) break;   // unary: only the direct operand
+            }
+        }
+    }
     for (int i = 0; i < n; ++i) {
         const tl_statement* st = &s[i];
         switch (st->kind) {

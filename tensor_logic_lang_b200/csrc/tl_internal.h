@@ -92,6 +92,9 @@ struct tl_ctx {
     std::map<std::string, std::unique_ptr<tl_tensor>> tensors;
     std::string err;
     std::string query_out;
+    // tensors whose sign a later step / comparison / relu gradient tests: their
+    // GEMMs run at fp32-class accuracy (3xTF32) so no sign flips against f64
+    std::vector<std::string> sign_sensitive;
     int32_t last_sweeps = 0;
     int64_t launches = 0;
     int rank = 0, world = 1;
@@ -226,6 +229,7 @@ struct GemmPlan {
     int32_t beta;        // 1: add into C, 0: overwrite
     int32_t relu_term;   // per-term relu
     int32_t epi_relu;    // additionally write relu(C) into D (fused next equation)
+    int32_t precise;     // fp32-class accuracy (3xTF32) on the tensor cores
     float* D; int64_t sdm, sdn;
 };
 tl_status launch_gemm(tl_ctx* c, const GemmPlan& p);
