@@ -256,17 +256,17 @@ def run_closure(args, dist, peaks):
     e2e_total = 0.0
     h2d = rows.nbytes + cols.nbytes
     d2h = local_rows * (n // 8)
-    out_bits = np.empty((local_rows, n // 32), dtype=np.uint32)
+    # pinned host buffer for the result (the step's device-to-host read)
+    out_bits = torch.empty((local_rows, n // 32), dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
     for i in range(args.warmup + args.steps):
         dist.barrier()
         t0 = time.perf_counter()
         ctx.run(full)
-        out = ctx.bits("Reach", rows=local_rows)
+        ctx.bits("Reach", rows=local_rows, out=out_bits)
         ctx.sync()
         t1 = time.perf_counter()
         if i >= args.warmup:
             e2e_total += t1 - t0
-        out_bits = out
     e2e_s = dist.max(e2e_total)
     e2e = {"value": total_sweeps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
            "d2h_bytes_per_step": int(d2h)}
@@ -291,8 +291,11 @@ def run_einsum_configs(args, peaks):
 
         def barrier(self):
             pass
-    for name, builder in [("mlp_forward", configs.mlp_forward), ("attention", configs.attention),
-                          ("mlp_train", configs.mlp_train), ("gnn", configs.gnn)]:
+    todo = [("mlp_forward", configs.mlp_forward), ("attention", configs.attention),
+            ("mlp_train", configs.mlp_train), ("gnn", configs.gnn)]
+    if args.workload not in ("all", "closure"):
+        todo = [t for t in todo if t[0] == args.workload]
+    for name, builder in todo:
         ctx = Context(device=0)
         p, data, sparse, flops = configs.program(builder)
         ctx.run(p)
@@ -380,6 +383,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-einsum", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
+    ap.add_argument("--workload", default="all",
+                    choices=["all", "closure", "mlp_forward", "attention", "mlp_train", "gnn"],
+                    help="all = closure headline + einsum configs at N=1; one name runs only that one "
+                         "(single-config profiling)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -390,12 +397,18 @@ def main():
     dist = Dist(world, rank, local)
     torch.cuda.set_device(local)
     peaks = load_peaks()
+    if args.workload not in ("all", "closure"):
+        einsum = run_einsum_configs(args, peaks)
+        if rank == 0:
+            print(json.dumps({"workload": args.workload, "einsum": einsum}))
+        dist.close()
+        return 0
     res = run_closure(args, dist, peaks)
     einsum = None
     cpu = None
-    if world == 1 and not args.no_einsum:
+    if world == 1 and not args.no_einsum and args.workload == "all":
         einsum = run_einsum_configs(args, peaks)
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu_sample_s > 0:
         sps, rows_done, secs = literal_sample(seconds=args.cpu_sample_s)
         cpu = {"value": sps, "unit": UNIT, "cores": 1, "kind": "port",
                "sample": f"literal x,z,y loop nest of one sweep (oracle/, -O2) on {rows_done} rows "

@@ -139,9 +139,9 @@ def gemm(A, B, C_init=None, relu_per_term=False, scale=1.0, threads=0):
     N = B.shape[1]
     out = np.zeros((M, N)) if C_init is None else np.array(C_init, dtype=np.float64, copy=True)
     A = np.ascontiguousarray(A)
-    B = np.ascontiguousarray(B)
+    Bt = np.ascontiguousarray(B.T)          # k contiguous for both operands in the inner loop
     D = C.POINTER(C.c_double)
-    lib().or_gemm(M, N, K, A.ctypes.data_as(D), K, 1, B.ctypes.data_as(D), N, 1,
+    lib().or_gemm(M, N, K, A.ctypes.data_as(D), K, 1, Bt.ctypes.data_as(D), 1, K,
                   out.ctypes.data_as(D), N, 1, int(relu_per_term), scale, threads)
     return out
 

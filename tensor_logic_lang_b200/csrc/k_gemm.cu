@@ -44,24 +44,44 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const __grid_constant__ GemmP
     const int64_t m0 = (int64_t)blockIdx.y * SB_M, n0 = (int64_t)blockIdx.x * BN;
     const int64_t kb = (int64_t)blockIdx.z * k_chunk;
     const int64_t ke = kb + k_chunk < p.K ? kb + k_chunk : p.K;
-    const bool a_kmajor = p.sak == 1;
-    float acc[4][TN] = {};
-    for (int64_t k0 = kb; k0 < ke; k0 += SB_K) {
-        for (int i = threadIdx.x; i < SB_M * SB_K; i += 256) {
+    const bool a_kmajor = p.sak == 1, b_nmajor = p.sbn == 1;
+    constexpr int A_PER = SB_M * SB_K / 256, B_PER = (BN * SB_K + 255) / 256;
+    // the next tile's loads are issued into registers before this tile's FMAs
+    float ra[A_PER], rb[B_PER];
+    auto load = [&](int64_t k0) {
+#pragma unroll
+        for (int t = 0; t < A_PER; ++t) {
+            const int i = threadIdx.x + t * 256;
             // walk the contiguous dimension of A across consecutive threads
             const int mm = a_kmajor ? i / SB_K : i % SB_M;
             const int kk = a_kmajor ? i % SB_K : i / SB_M;
             const int64_t gm = m0 + mm, gk = k0 + kk;
-            As[kk][mm] = (gm < p.M && gk < ke) ? p.A[gm * p.sam + gk * p.sak] : 0.f;
+            ra[t] = (gm < p.M && gk < ke) ? p.A[gm * p.sam + gk * p.sak] : 0.f;
         }
-        for (int i = threadIdx.x; i < BN * SB_K; i += 256) {
-            const bool b_nmajor = p.sbn == 1;
+#pragma unroll
+        for (int t = 0; t < B_PER; ++t) {
+            const int i = threadIdx.x + t * 256;
             const int nn = b_nmajor ? i % BN : i / SB_K;
             const int kk = b_nmajor ? i / BN : i % SB_K;
             const int64_t gn = n0 + nn, gk = k0 + kk;
-            Bs[kk][nn] = (gn < p.N && gk < ke) ? p.B[gk * p.sbk + gn * p.sbn] * sgn : 0.f;
+            rb[t] = (i < BN * SB_K && gn < p.N && gk < ke) ? p.B[gk * p.sbk + gn * p.sbn] * sgn : 0.f;
+        }
+    };
+    float acc[4][TN] = {};
+    if (kb < ke) load(kb);
+    for (int64_t k0 = kb; k0 < ke; k0 += SB_K) {
+#pragma unroll
+        for (int t = 0; t < A_PER; ++t) {
+            const int i = threadIdx.x + t * 256;
+            As[a_kmajor ? i % SB_K : i / SB_M][a_kmajor ? i / SB_K : i % SB_M] = ra[t];
+        }
+#pragma unroll
+        for (int t = 0; t < B_PER; ++t) {
+            const int i = threadIdx.x + t * 256;
+            if (i < BN * SB_K) Bs[b_nmajor ? i / BN : i % SB_K][b_nmajor ? i % BN : i / SB_K] = rb[t];
         }
         __syncthreads();
+        if (k0 + SB_K < ke) load(k0 + SB_K);
 #pragma unroll
         for (int kk = 0; kk < SB_K; ++kk) {
             float a[4], b[TN];
@@ -531,10 +551,11 @@ static tl_status launch_simt(tl_ctx* c, const GemmPlan& p) {
     const int64_t tiles = ((p.N + bn - 1) / bn) * ((p.M + SB_M - 1) / SB_M);
     // split K when the output has too few tiles to fill the GPU
     int64_t splits = 1;
-    if (!p.epi_relu && p.K >= 256) {
+    if (!p.epi_relu && p.K >= 64) {
+        // about two blocks per SM, each at least two 16-deep k-steps
         const int64_t want = (int64_t)c->sm_count * 2;
         if (tiles < want) splits = (want + tiles - 1) / tiles;
-        const int64_t max_splits = (p.K + 127) / 128;
+        const int64_t max_splits = (p.K + 31) / 32;
         if (splits > max_splits) splits = max_splits;
     }
     int64_t chunk = (p.K + splits - 1) / splits;
@@ -598,7 +619,7 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
         need += (((size_t)(q->mn ? Ke : q->R) * q->ld * 4) + 255) & ~size_t(255);
     }
     void* ws = nullptr;
-    TL_TRY(workspace(c, need, &ws));
+    TL_TRY(workspace(c, need, &ws, WS_GEMM));
     uint8_t* wp = (uint8_t*)ws;
     for (Prep* q : {&pa, &pb}) {
         q->dst = (float*)wp;

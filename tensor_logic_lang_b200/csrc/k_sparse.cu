@@ -405,7 +405,7 @@ tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed) {
     const int64_t n = R->dims[0], words = R->bits_words;
     const size_t bytes = (size_t)n * words * 4;
     void* ws = nullptr;
-    TL_TRY(workspace(c, bytes, &ws));
+    TL_TRY(workspace(c, bytes, &ws, WS_FIXPOINT));
     {
         LaunchScope L(c, "closure_left_sweep", (double)E->nnz * words * 4.0 + (double)n * words * 8.0, 0);
         k_closure_left<<<grid_for(c, n, 8), 256, 0, c->stream>>>(R->bits, (uint32_t*)ws, n, words, E->rowptr,

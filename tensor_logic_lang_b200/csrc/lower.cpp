@@ -314,8 +314,10 @@ bool plain_2d(const tl_ref* r, const Tensor* t, const Analysis& a) {
     return true;
 }
 
-tl_status try_gemm(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* lhs, bool* done) {
+tl_status try_gemm(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* lhs, bool* done,
+                   Tensor* fuse_relu = nullptr, bool* fused = nullptr) {
     *done = false;
+    if (fused) *fused = false;
     if (eq->accum != TL_ACC_ASSIGN && eq->accum != TL_ACC_ADD) return TL_OK;
     if (a.n_free != 2 || (int)a.vars.size() != 3 || !a.has_contraction) return TL_OK;
     GemmMatch m;
@@ -368,11 +370,46 @@ tl_status try_gemm(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* 
     // LHS [m,n] or [n,m]
     g.scm = lhs->strides[0]; g.scn = lhs->strides[1];
     if (a.lhs_var[0] != vm) std::swap(g.scm, g.scn);
+    // the next statement `H = relu(LHS)` (same shape, same index order) is
+    // written by this GEMM's epilogue; H must not be an operand being read
+    if (fuse_relu && fuse_relu != tA && fuse_relu != tB && fuse_relu != lhs) {
+        TL_TRY(alloc_dense_public(c, fuse_relu));
+        g.epi_relu = 1;
+        g.D = fuse_relu->dense;
+        g.sdm = g.scm;
+        g.sdn = g.scn;
+    }
     TL_TRY(launch_gemm(c, g));
     mark_written_dense(lhs);
     lhs->boolean = false;
+    if (g.epi_relu) {
+        mark_written_dense(fuse_relu);
+        fuse_relu->boolean = false;
+        if (fused) *fused = true;
+    }
     *done = true;
     return TL_OK;
+}
+
+// `next` is `H = relu(Z)` over the LHS Z of `eq`, element for element: same
+// shape and the same index order on both sides.  Returns H (allocated) or null.
+Tensor* relu_successor(tl_ctx* c, const tl_equation* eq, const tl_equation* next, Tensor* lhs) {
+    if (!next || next->accum != TL_ACC_ASSIGN || next->n_refs != 1 || next->n_code != 2) return nullptr;
+    if (!(next->code[0].op == TL_OP_REF && next->code[1].op == TL_OP_NL && next->code[1].arg == TL_NL_RELU)) return nullptr;
+    const tl_ref* r = &next->refs[0];
+    if (strcmp(r->tensor, eq->lhs.tensor) || !strcmp(next->lhs.tensor, eq->lhs.tensor)) return nullptr;
+    if (r->rank != 2 || next->lhs.rank != 2 || lhs->rank != 2) return nullptr;
+    for (int k = 0; k < 2; ++k) {
+        if (r->idx[k].kind != TL_IX_NAME || next->lhs.idx[k].kind != TL_IX_NAME) return nullptr;
+        if (strcmp(r->idx[k].name, next->lhs.idx[k].name)) return nullptr;
+        if (domain_size(c, r->idx[k].name) != lhs->dims[k]) return nullptr;
+    }
+    if (!strcmp(r->idx[0].name, r->idx[1].name)) return nullptr;
+    Tensor* h = find_defined(c, next->lhs.tensor);
+    if (!h && allocate_tensor(c, next->lhs.tensor, next->lhs.idx, next->lhs.rank, &h) != TL_OK) return nullptr;
+    if (h->rank != 2 || h->dims[0] != lhs->dims[0] || h->dims[1] != lhs->dims[1]) return nullptr;
+    if (h->shard == TL_SHARD_ROWS && c->world > 1) return nullptr;
+    return h;
 }
 
 // ----------------------------------------------------------------------------
@@ -424,7 +461,8 @@ tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, 
     size_t p_bytes = (size_t)p_rows * f * 4;
     size_t pg_bytes = sharded ? (size_t)gathered_rows_per_rank * c->world * f * 4 : 0;
     void* ws = nullptr;
-    TL_TRY(workspace(c, p_bytes + pg_bytes + (sharded ? (size_t)gathered_rows_per_rank * f * 4 : 0) + 256, &ws));
+    TL_TRY(workspace(c, p_bytes + pg_bytes + (sharded ? (size_t)gathered_rows_per_rank * f * 4 : 0) + 256, &ws,
+                     WS_CHAIN));
     float* P = (float*)ws;
     if (!xp || !wp) {
         TL_CK(c, cudaMemsetAsync(P, 0, p_bytes, c->stream));
@@ -565,7 +603,9 @@ static tl_status alloc_dense_impl(tl_ctx* c, Tensor* t) {
 // ============================================================================
 // genEquation (llvm.zig:357-459)
 // ============================================================================
-static tl_status run_equation(tl_ctx* c, const tl_equation* eq) {
+static tl_status run_equation(tl_ctx* c, const tl_equation* eq, const tl_equation* next = nullptr,
+                              bool* consumed_next = nullptr) {
+    if (consumed_next) *consumed_next = false;
     TL_TRY(validate_code(c, eq));
     if (eq->n_code > 0 && eq->code[eq->n_code - 1].op == TL_OP_NL) {
         int f = eq->code[eq->n_code - 1].arg;
@@ -628,7 +668,11 @@ static tl_status run_equation(tl_ctx* c, const tl_equation* eq) {
         return TL_OK;
     }
     bool done = false;
-    TL_TRY(try_gemm(c, eq, a, lhs, &done));
+    Tensor* fuse = nullptr;
+    if (next && consumed_next && validate_code(c, next) == TL_OK) fuse = relu_successor(c, eq, next, lhs);
+    bool fused = false;
+    TL_TRY(try_gemm(c, eq, a, lhs, &done, fuse, &fused));
+    if (done && fused && consumed_next) *consumed_next = true;
     if (!done) TL_TRY(try_sparse_chain(c, eq, a, lhs, &done));
     if (!done) TL_TRY(try_step_bits(c, eq, a, lhs, &done));
     if (done) return TL_OK;
@@ -968,7 +1012,14 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
         case TL_STMT_DOMAIN: case TL_STMT_QUERY: break;
         case TL_STMT_EQUATION:
             if (is_recursive(&st->eq)) rec.push_back(st->eq);
-            else TL_TRY(run_equation(c, &st->eq));
+            else {
+                // an element-wise relu right after a GEMM is written by its epilogue
+                const tl_equation* next = (i + 1 < n && s[i + 1].kind == TL_STMT_EQUATION &&
+                                           !is_recursive(&s[i + 1].eq)) ? &s[i + 1].eq : nullptr;
+                bool consumed = false;
+                TL_TRY(run_equation(c, &st->eq, next, &consumed));
+                if (consumed) ++i;
+            }
             break;
         case TL_STMT_SPARSE: TL_TRY(tl_sparse_decl(c, &st->sparse)); break;
         case TL_STMT_SPARSE_LOAD: TL_TRY(run_sparse_load(c, st)); break;

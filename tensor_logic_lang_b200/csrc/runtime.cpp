@@ -64,19 +64,20 @@ tl_status launch_end(tl_ctx* c, cudaEvent_t* ev) {
     return TL_OK;
 }
 
-tl_status workspace(tl_ctx* c, size_t bytes, void** out) {
-    if (bytes > c->ws_cap) {
-        if (c->ws) {
+tl_status workspace(tl_ctx* c, size_t bytes, void** out, int slot) {
+    if (slot < 0 || slot > 3) return fail(c, TL_ERR_INVALID, "bad workspace slot");
+    if (bytes > c->ws_cap[slot]) {
+        if (c->ws[slot]) {
             TL_CK(c, cudaStreamSynchronize(c->stream));
-            cudaFree(c->ws);
-            c->ws = nullptr;
-            c->ws_cap = 0;
+            cudaFree(c->ws[slot]);
+            c->ws[slot] = nullptr;
+            c->ws_cap[slot] = 0;
         }
-        size_t cap = std::max(bytes, (size_t)64 << 20);
-        TL_CK(c, cudaMalloc(&c->ws, cap));
-        c->ws_cap = cap;
+        size_t cap = std::max(bytes, (size_t)16 << 20);
+        TL_CK(c, cudaMalloc(&c->ws[slot], cap));
+        c->ws_cap[slot] = cap;
     }
-    *out = c->ws;
+    *out = c->ws[slot];
     return TL_OK;
 }
 
@@ -309,7 +310,7 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     for (auto& p : c->pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
     for (auto e : c->event_pool) cudaEventDestroy(e);
     if (c->comm) comm_destroy(c);
-    cudaFree(c->ws);
+    for (int i = 0; i < 4; ++i) cudaFree(c->ws[i]);
     cudaFree(c->aux);
     cudaFree(c->d_flags);
     cudaFreeHost(c->h_flags);

@@ -101,8 +101,8 @@ struct tl_ctx {
     void* comm = nullptr;  // ncclComm_t
 
     // device scratch
-    void* ws = nullptr;
-    size_t ws_cap = 0;
+    void* ws[4] = {nullptr, nullptr, nullptr, nullptr};   // one buffer per tl::WsSlot
+    size_t ws_cap[4] = {0, 0, 0, 0};
     int* d_flags = nullptr;     // [0..63] changed / error words
     void* aux = nullptr;        // state kept across the sweeps of one fixpoint
     size_t aux_cap = 0;
@@ -148,8 +148,11 @@ struct LaunchScope {
 // device-side error words (pipeline timeouts); syncs the stream
 tl_status check_device_flags(tl_ctx* c);
 
-// scratch workspace (grown on demand, never shrunk)
-tl_status workspace(tl_ctx* c, size_t bytes, void** out);
+// scratch workspaces (grown on demand, never shrunk); users that can be
+// nested (a message-passing step holding its transform while the GEMM that
+// produces it stages operand copies) take different slots
+enum WsSlot { WS_GENERAL = 0, WS_GEMM = 1, WS_CHAIN = 2, WS_FIXPOINT = 3 };
+tl_status workspace(tl_ctx* c, size_t bytes, void** out, int slot = WS_GENERAL);
 tl_status ensure_dense(tl_ctx* c, Tensor* t);
 tl_status ensure_bits(tl_ctx* c, Tensor* t);
 tl_status ensure_csr(tl_ctx* c, Tensor* t);

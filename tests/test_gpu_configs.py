@@ -62,16 +62,11 @@ def test_c1_attention_full(ctx, oracle_lib):
     assert_close(ctx.tensor("Out"), O, TOL_TF32, "Out")
 
 
-def test_c2_train_reduced(ctx, oracle_lib):
-    p, d, _, _ = configs.program(configs.mlp_train, b=256, i=784, h=512, o=10)
-    ctx.run(p)
-    ref = oracle_lib.OracleRun(p)
-    for n in ("Z1", "H", "Y", "L", "dL_dW2", "dL_dW1"):
-        assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
+def c2_reference(oracle_lib, d, relu_mask=None):
+    """C2 through the reference-order f64 GEMM restatement (autodiff.zig rules).
 
-
-def c2_reference(oracle_lib, d):
-    """Full-size C2 through the reference-order f64 GEMM restatement (autodiff.zig rules)."""
+    relu_mask, when given, replaces step(Z1) in the relu gradient (see
+    check_c2 for why)."""
     X, W1, W2, T = d["X"], d["W1"], d["W2"], d["Target"]
     Z1 = oracle_lib.gemm(X, W1)
     H = np.maximum(Z1, 0.0)
@@ -82,18 +77,44 @@ def c2_reference(oracle_lib, d):
     dZ2 = Y * (dY - (dY * Y).sum())
     dW2 = oracle_lib.gemm(H.T, dZ2)
     dH = oracle_lib.gemm(dZ2, W2.T)
-    dZ1 = dH * (Z1 > 0)
+    dZ1 = dH * ((Z1 > 0) if relu_mask is None else relu_mask)
     dW1 = oracle_lib.gemm(X.T, dZ1)
     return dict(Z1=Z1, H=H, Y=Y, L=np.array([(D * D).sum()]), dL_dW2=dW2, dL_dW1=dW1)
+
+
+def check_c2(ctx, oracle_lib, d):
+    """Forward tensors within tolerance; the relu gradient step(Z1) is
+    discontinuous, so an element whose f64 Z1 lies within rounding of 0 may
+    take the other branch on the device.  Such flips must sit at near-ties
+    (|Z1| <= 1e-4 max|Z1|); dW1 is then checked against the f64 chain taking
+    the device's branch at those ties, which isolates the arithmetic."""
+    ref = c2_reference(oracle_lib, d)
+    z1 = ctx.tensor("Z1")
+    for n in ("Z1", "H", "Y", "L", "dL_dW2"):
+        assert_close(ctx.tensor(n).reshape(ref[n].shape), ref[n], TOL_TF32, n)
+    mask = z1 > 0
+    flips = mask != (ref["Z1"] > 0)
+    tie = 1e-4 * np.max(np.abs(ref["Z1"]))
+    assert np.all(np.abs(ref["Z1"][flips]) <= tie), "relu branch differs away from a tie"
+    masked = c2_reference(oracle_lib, d, relu_mask=mask) if flips.any() else ref
+    assert_close(ctx.tensor("dL_dW1"), masked["dL_dW1"], TOL_TF32, "dL_dW1")
+    return int(flips.sum())
+
+
+def test_c2_train_reduced(ctx, oracle_lib):
+    p, d, _, _ = configs.program(configs.mlp_train, b=256, i=784, h=512, o=10)
+    ctx.run(p)
+    # the literal loop nests and the GEMM restatement agree (both f64)
+    ref = oracle_lib.OracleRun(p)
+    np.testing.assert_allclose(ref.tensor("dL_dW1"), c2_reference(oracle_lib, d)["dL_dW1"], rtol=1e-9, atol=1e-12)
+    check_c2(ctx, oracle_lib, d)
 
 
 @pytest.mark.slow
 def test_c2_train_full(ctx, oracle_lib):
     p, d, _, _ = configs.program(configs.mlp_train)
     ctx.run(p)
-    ref = c2_reference(oracle_lib, d)
-    for n, want in ref.items():
-        assert_close(ctx.tensor(n).reshape(want.shape), want, TOL_TF32, n)
+    check_c2(ctx, oracle_lib, d)
 
 
 @pytest.mark.parametrize("n,f", [(512, 32), (4096, 128)])
