@@ -54,6 +54,7 @@ typedef int32_t tl_status;
 #define TL_ERR_UNSUPPORTED    6  /* form the backend does not lower           */
 #define TL_ERR_NOT_FOUND      7  /* unknown tensor name                       */
 #define TL_ERR_IO             8  /* save/load file error                      */
+#define TL_ERR_TOO_LARGE      9  /* size above a fixed capacity (see below)   */
 
 /* ------------------------------------------------------------------------ */
 /* Index forms: src/frontend/ast.zig:17-59 (Index union)                     */
@@ -332,6 +333,44 @@ tl_status tl_profile_reset(tl_ctx* ctx);
 int64_t tl_launch_count(const tl_ctx* ctx);
 /* The context's CUDA stream (a cudaStream_t) for event timing by the caller. */
 void* tl_stream(const tl_ctx* ctx);
+
+/* ------------------------------------------------------------------------ */
+/* Allocation-free closure fixpoint.                                         */
+/*                                                                           */
+/* No counterpart in the reference.  For callers that must not allocate GPU */
+/* memory: a host application whose device memory belongs to its own pool   */
+/* or arena (a serving process under a fixed memory budget, a framework     */
+/* whose caching allocator owns the device), or a caller preparing work     */
+/* around stream capture, where cudaMalloc would synchronise the device or   */
+/* break the capture.  Such a caller cannot create a tl_ctx (tl_init         */
+/* allocates), so this entry point takes no context: every input and output */
+/* is caller-owned device memory, and the fixpoint's scratch (one word per   */
+/* row plus control words) lives in a fixed array inside the library, sized  */
+/* for at most TL_NOALLOC_MAX_ROWS rows (about 256 KiB, held by every GPU    */
+/* that loads the library until the process exits).                          */
+/*                                                                           */
+/* Computes Reach[x,z] max= step(Reach[x,y] Edge[y,z]) to its fixpoint, the  */
+/* same sweeps tl_fixpoint runs for this equation:                           */
+/*   n         rows and columns of Reach and Edge (0..TL_NOALLOC_MAX_ROWS;   */
+/*             a larger n returns TL_ERR_TOO_LARGE before touching the GPU)  */
+/*   d_rowptr  Edge as CSR on the device: n+1 int64 row offsets             */
+/*   d_colidx  column indices (int32, each in [0, n)); every stored entry    */
+/*             counts as a positive value                                    */
+/*   d_reach   in: the initial 0/1 relation, out: the fixpoint; n rows of    */
+/*             ceil(n/32) uint32 words, bit (z & 31) of word z >> 5 = [x,z]  */
+/*   max_sweeps  the sweep cap (0 = 1000, as fixpoint.zig:67-72)            */
+/*   stream    the cudaStream_t to run on (NULL = the default stream)        */
+/*   sweeps_out  receives the sweep count (may be NULL)                      */
+/* The first call on a device looks up the scratch array's device address    */
+/* (cudaGetSymbolAddress) and should happen before any stream capture.       */
+/* Every call shares the one array, so calls that overlap on the GPU (other  */
+/* streams, other host threads) race; serialise them.  The call returns      */
+/* after the fixpoint has converged (it reads the changed word each sweep).  */
+/* ------------------------------------------------------------------------ */
+#define TL_NOALLOC_MAX_ROWS 65536
+tl_status tl_closure_noalloc(int64_t n, const int64_t* d_rowptr, const int32_t* d_colidx,
+                             uint32_t* d_reach, int32_t max_sweeps, void* stream,
+                             int32_t* sweeps_out);
 
 #ifdef __cplusplus
 }

@@ -23,11 +23,13 @@ TL_ERR_NOT_CONVERGED = 5
 TL_ERR_UNSUPPORTED = 6
 TL_ERR_NOT_FOUND = 7
 TL_ERR_IO = 8
+TL_ERR_TOO_LARGE = 9
 STATUS_NAMES = {
     0: "TL_OK", 1: "TL_ERR_INVALID", 2: "TL_ERR_OOM", 3: "TL_ERR_CUDA",
     4: "TL_ERR_COMM", 5: "TL_ERR_NOT_CONVERGED", 6: "TL_ERR_UNSUPPORTED",
-    7: "TL_ERR_NOT_FOUND", 8: "TL_ERR_IO",
+    7: "TL_ERR_NOT_FOUND", 8: "TL_ERR_IO", 9: "TL_ERR_TOO_LARGE",
 }
+TL_NOALLOC_MAX_ROWS = 65536
 
 # index kinds
 IX_NAME, IX_CONST, IX_ADD, IX_SUB, IX_PRIMED, IX_DIV, IX_NORMALIZE, IX_SLICE, IX_VIRTUAL = range(9)
@@ -110,7 +112,7 @@ EXPORTS = [
     "tl_tensor_download", "tl_tensor_upload_f32", "tl_tensor_download_f32",
     "tl_tensor_download_bits", "tl_tensor_device_ptr", "tl_tensor_set", "tl_sparse_upload",
     "tl_query_format", "tl_set_sharding", "tl_profile_enable", "tl_profile_read",
-    "tl_profile_reset", "tl_launch_count", "tl_stream",
+    "tl_profile_reset", "tl_launch_count", "tl_stream", "tl_closure_noalloc",
 ]
 
 
@@ -152,6 +154,7 @@ def _declare(lib):
         "tl_profile_reset": (C.c_int32, [vp]),
         "tl_launch_count": (C.c_int64, [vp]),
         "tl_stream": (C.c_void_p, [vp]),
+        "tl_closure_noalloc": (C.c_int32, [C.c_int64, vp, vp, vp, C.c_int32, vp, P(C.c_int32)]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)

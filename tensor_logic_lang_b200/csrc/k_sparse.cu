@@ -401,6 +401,25 @@ tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, 
     return L.done();
 }
 
+// The same right-form sweep with every buffer supplied by the caller and no
+// context: for the allocation-free entry point (noalloc.cu).
+cudaError_t launch_closure_right_raw(uint32_t* R, int64_t rows, int64_t words, const int64_t* rowptr,
+                                     const int32_t* colidx, int64_t e_rows, int* changed,
+                                     unsigned long long* counter, int32_t* pending, cudaStream_t stream) {
+    const size_t smem = (size_t)kClosureWarps * (words + kWindowWords * 16) * 4;
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    int dev = 0, sms = 148, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_closure_right, 32 * kClosureWarps, smem);
+    if (per_sm < 1) per_sm = 1;
+    int64_t grid = std::min<int64_t>((rows + kClosureWarps - 1) / kClosureWarps, (int64_t)sms * per_sm);
+    if (grid < 1) grid = 1;
+    k_closure_right<<<(unsigned)grid, 32 * kClosureWarps, smem, stream>>>(R, rows, words, rowptr, colidx, e_rows,
+                                                                         changed, counter, pending);
+    return cudaGetLastError();
+}
+
 tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed) {
     const int64_t n = R->dims[0], words = R->bits_words;
     const size_t bytes = (size_t)n * words * 4;
