@@ -10,15 +10,13 @@
 //   per-term relu message passing   src/codegen/einsum.zig:20-196, expr.zig:245-249
 //
 // Closure on bit rows.  With R in {0,1} and E >= 0, step(R[x,y] E[y,z]) is
-// R[x,y] AND (E[y,z] > 0), and `max=` is OR, so one sweep of the right form
-// over row x is R[x] |= OR_{y in R[x]} succ(y).  A warp keeps row x (n bits)
-// in shared memory and expands its set bits in ascending y, re-reading a
-// 32-word chunk until it is stable; bits a successor sets at higher indices
-// are expanded later in the same sweep.  This is the reference's in-place
-// (Gauss-Seidel) order restricted to one row, so on an edge set with u < v
-// a row closes in its first sweep and the second sweep only confirms, the
-// same two sweeps the reference takes; on any edge set the fixpoint reached
-// is the least one above the start, bit for bit.  A device-side changed word
+// R[x,y] AND (E[y,z] > 0), and `max=` is OR, so the right form's update of
+// row x is R[x] |= OR_{y in R[x]} succ(y); rows never read other rows.  A
+// warp keeps row x (n bits) in shared memory and closes it within one sweep
+// (see k_closure_right).  The reference's in-place z-ascending loop also
+// closes every row in its first sweep when the edges run u < v, so both take
+// two sweeps there (the second confirms); on any edge set the fixpoint is the
+// least one above the start, bit for bit.  A device-side changed word
 // records whether any row gained a bit.
 #include <vector>
 
@@ -73,87 +71,177 @@ __global__ void k_bits_to_dense(const uint32_t* bits, int64_t rows, int64_t cols
     }
 }
 
-// Right-form sweep.  A warp takes rows from a shared counter (the rows with
-// the largest reach sets, low indices on a u < v DAG, start first), holds the
-// row in shared memory, and walks it in windows of 1024 bits.  The set,
-// not yet expanded bits of a window are compacted into a work list that all
-// 32 lanes expand together; the window is re-read until no new bit appears
-// in it.  pending[r] is the lowest word that may hold a bit not expanded in
-// an earlier sweep: a successor that lands below the current window (a back
-// edge) is left for the next sweep, as in the reference's in-place order,
-// and a row with nothing pending is already closed, so its sweep changes
-// nothing and is skipped without loading the row.
+// Right-form sweep on bit rows.
+//
+// Rows are independent under R[x] |= OR_{y in R[x]} succ(y).  A warp holds row
+// x in shared memory and closes it within the sweep:
+//  * rows are grabbed 32 at a time from a counter (heaviest rows, the low
+//    indices of a u < v DAG, first); the 32 lanes check the rows' pending
+//    words together and only rows with work are loaded;
+//  * pending[r] is the lowest word of row r that may hold a bit whose
+//    successors are not in the row yet (0 at the first sweep; none once the
+//    row is closed);
+//  * the set bits at or above that word go into a queue in shared memory;
+//    each step the 32 lanes take one queued bit each and OR its successors
+//    (CSR) into the row, queueing every bit that was new.
+// The row is closed when the queue drains, so a row never needs a second
+// sweep: on an edge set with u < v the first sweep closes every row (as the
+// reference's in-place z-ascending loop does) and the second one finds no
+// pending row, so the sweep counts match the reference's (2).  On edge sets
+// with back edges the fixpoint is the same bit for bit, reached in at most as
+// many sweeps.  If the queue overflows, the row falls back to a windowed scan
+// that re-expands every set bit in ascending order (idempotent), and a bit
+// that scan sets below its window is left pending for the next sweep.
 constexpr int kClosureWarps = 4;
 constexpr int kWindowWords = 32;
+constexpr int kQueue = 1024;        // queued bit positions per warp (uint32)
+
+// successors of y into the row; queue new bits (or flag an overflow)
+__device__ __forceinline__ bool expand_into(uint32_t* row, int64_t y, const int64_t* __restrict__ rowptr,
+                                            const int32_t* __restrict__ colidx, int64_t e_rows, uint32_t* q,
+                                            int* qtail, int head, bool* overflow) {
+    bool grew = false;
+    if (y >= e_rows) return false;
+    const int64_t e1 = rowptr[y + 1];
+    for (int64_t e = rowptr[y]; e < e1; ++e) {
+        const int32_t z = colidx[e];
+        const uint32_t bit = 1u << (z & 31);
+        if (row[z >> 5] & bit) continue;
+        const uint32_t old = atomicOr(&row[z >> 5], bit);
+        if (old & bit) continue;
+        grew = true;
+        const int pos = atomicAdd(qtail, 1);
+        if (pos < head + kQueue) q[pos % kQueue] = (uint32_t)z;
+        else *overflow = true;
+    }
+    return grew;
+}
+
+// Windowed ascending scan from word `from`: expands every set bit (again),
+// re-reading each 1024-bit window until stable.  Returns the lowest word a
+// successor landed in below its window (left pending), INT32_MAX if none.
+__device__ int32_t expand_windows(uint32_t* row, int64_t words, int64_t from, const int64_t* __restrict__ rowptr,
+                                  const int32_t* __restrict__ colidx, int64_t e_rows, uint16_t* wl, bool* grew) {
+    const int lane = threadIdx.x & 31;
+    int32_t low = INT32_MAX;
+    for (int64_t c0 = (from / kWindowWords) * kWindowWords; c0 < words; c0 += kWindowWords) {
+        const int64_t w = c0 + lane;
+        uint32_t done = 0;
+        for (;;) {
+            const uint32_t pend = (w < words ? row[w] : 0u) & ~done;
+            const int cnt = __popc(pend);
+            int pre = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, pre, o);
+                if (lane >= o) pre += v;
+            }
+            const int total = __shfl_sync(0xffffffffu, pre, 31);
+            if (total == 0) break;
+            int at = pre - cnt;
+            for (uint32_t m = pend; m; m &= m - 1) wl[at++] = (uint16_t)(lane * 32 + __ffs(m) - 1);
+            done |= pend;
+            __syncwarp();
+            for (int i = lane; i < total; i += 32) {
+                const int64_t y = c0 * 32 + wl[i];
+                if (y >= e_rows) continue;
+                const int64_t e1 = rowptr[y + 1];
+                for (int64_t e = rowptr[y]; e < e1; ++e) {
+                    const int32_t z = colidx[e];
+                    const uint32_t bit = 1u << (z & 31);
+                    if (row[z >> 5] & bit) continue;
+                    const uint32_t old = atomicOr(&row[z >> 5], bit);
+                    if (!(old & bit)) {
+                        *grew = true;
+                        if ((z >> 5) < c0) low = min(low, (int32_t)(z >> 5));
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) low = min(low, __shfl_xor_sync(0xffffffffu, low, o));
+    return low;
+}
 
 __global__ void __launch_bounds__(32 * kClosureWarps)
     k_closure_right(uint32_t* R, int64_t local_rows, int64_t words, const int64_t* __restrict__ rowptr,
                     const int32_t* __restrict__ colidx, int64_t e_rows, int* changed, unsigned long long* next_row,
                     int32_t* pending) {
     extern __shared__ uint32_t smem_u[];
+    __shared__ int qtail_s[kClosureWarps];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    uint32_t* row = smem_u + (int64_t)wib * (words + kWindowWords * 32 / 2);
-    uint16_t* wl = reinterpret_cast<uint16_t*>(row + words);
+    uint32_t* row = smem_u + (int64_t)wib * (words + kQueue);
+    uint32_t* q = row + words;
+    uint16_t* wl = reinterpret_cast<uint16_t*>(q);       // the windowed fallback reuses the queue
+    int* qtail = &qtail_s[wib];
+    bool any_changed = false;
     for (;;) {
-        unsigned long long r = 0;
-        if (lane == 0) r = atomicAdd(next_row, 1ull);
-        r = __shfl_sync(0xffffffffu, r, 0);
-        if ((int64_t)r >= local_rows) break;
-        const int64_t start_w = pending[r];
-        if (start_w >= words) continue;                  // closed row: nothing to expand
-        uint32_t* grow = R + (int64_t)r * words;
-        for (int64_t w = lane; w < words; w += 32) row[w] = grow[w];
-        __syncwarp();
-        bool grew = false;
-        int32_t low = INT32_MAX;
-        for (int64_t c0 = (start_w / kWindowWords) * kWindowWords; c0 < words; c0 += kWindowWords) {
-            const int64_t w = c0 + lane;
-            uint32_t done = 0;
-            for (;;) {
-                const uint32_t cur = w < words ? row[w] : 0u;
-                const uint32_t pend = cur & ~done;
-                const int cnt = __popc(pend);
-                int pre = cnt;                          // inclusive prefix over lanes
+        unsigned long long base = 0;
+        if (lane == 0) base = atomicAdd(next_row, 32ull);
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if ((int64_t)base >= local_rows) break;
+        const int64_t mine = (int64_t)base + lane;
+        const int32_t my_pend = mine < local_rows ? pending[mine] : INT32_MAX;
+        unsigned todo = __ballot_sync(0xffffffffu, my_pend < words);
+        while (todo) {
+            const int src = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int64_t r = (int64_t)base + src;
+            const int64_t start_w = __shfl_sync(0xffffffffu, my_pend, src);
+            uint32_t* grow = R + r * words;
+            for (int64_t w = lane; w < words; w += 32) row[w] = grow[w];
+            if (lane == 0) *qtail = 0;
+            __syncwarp();
+            // queue the row's set bits from its pending word on
+            bool overflow = false;
+            int stored = 0;
+            for (int64_t w0 = start_w & ~int64_t(31); w0 < words && !overflow; w0 += 32) {
+                const int64_t w = w0 + lane;
+                const uint32_t bits = (w < words && w >= start_w) ? row[w] : 0u;
+                const int cnt = __popc(bits);
+                int pre = cnt;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
                     const int v = __shfl_up_sync(0xffffffffu, pre, o);
                     if (lane >= o) pre += v;
                 }
                 const int total = __shfl_sync(0xffffffffu, pre, 31);
-                if (total == 0) break;
-                int at = pre - cnt;
-                for (uint32_t m = pend; m; m &= m - 1) wl[at++] = (uint16_t)(lane * 32 + __ffs(m) - 1);
-                done |= pend;
+                if (stored + total > kQueue) { overflow = true; break; }
+                int at = stored + pre - cnt;
+                for (uint32_t m = bits; m; m &= m - 1) q[at++] = (uint32_t)(w * 32 + __ffs(m) - 1);
+                stored += total;
+            }
+            if (lane == 0) *qtail = stored;
+            __syncwarp();
+            bool grew = false;
+            int head = 0;
+            while (!overflow) {
+                const int tail = *(volatile int*)qtail;
+                if (head >= tail) break;
+                const int take = min(32, tail - head);
+                uint32_t y = 0;
+                if (lane < take) y = q[(head + lane) % kQueue];
                 __syncwarp();
-                for (int i = lane; i < total; i += 32) {
-                    const int64_t y = c0 * 32 + wl[i];
-                    if (y >= e_rows) continue;
-                    const int64_t e1 = rowptr[y + 1];
-                    for (int64_t e = rowptr[y]; e < e1; ++e) {
-                        const int32_t z = colidx[e];
-                        const uint32_t bit = 1u << (z & 31);
-                        if (!(row[z >> 5] & bit)) {
-                            const uint32_t old = atomicOr(&row[z >> 5], bit);
-                            if (!(old & bit)) {
-                                grew = true;
-                                if ((z >> 5) < c0) low = min(low, (int32_t)(z >> 5));
-                            }
-                        }
-                    }
-                }
+                bool ovf = false;
+                if (lane < take) grew |= expand_into(row, y, rowptr, colidx, e_rows, q, qtail, head + take, &ovf);
+                head += take;
+                overflow = __any_sync(0xffffffffu, ovf);
                 __syncwarp();
             }
+            int32_t low = INT32_MAX;
+            if (overflow) low = expand_windows(row, words, 0, rowptr, colidx, e_rows, wl, &grew);
+            const bool row_grew = __any_sync(0xffffffffu, grew);
+            if (lane == 0) pending[r] = low;
+            if (row_grew) {
+                for (int64_t w = lane; w < words; w += 32) grow[w] = row[w];
+                any_changed = true;
+            }
+            __syncwarp();
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) low = min(low, __shfl_xor_sync(0xffffffffu, low, o));
-        const bool any = __any_sync(0xffffffffu, grew);
-        if (lane == 0) pending[r] = low;
-        if (any) {
-            for (int64_t w = lane; w < words; w += 32) grow[w] = row[w];
-            if (lane == 0) *changed = 1;
-        }
-        __syncwarp();
     }
+    if (lane == 0 && any_changed) *changed = 1;
 }
 
 // Left-form sweep Rnew[x] = R[x] | OR_{z in succ(x)} R[z] from the previous
@@ -365,7 +453,7 @@ tl_status launch_dense_to_csr(tl_ctx* c, Tensor* t) {
 
 tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, int sweep) {
     const int64_t words = R->bits_words;
-    const size_t smem = (size_t)kClosureWarps * (words + kWindowWords * 16) * 4;
+    const size_t smem = (size_t)kClosureWarps * (words + kQueue) * 4;
     if (smem > 200 * 1024)
         return fail(c, TL_ERR_UNSUPPORTED, "closure rows of %lld bits exceed shared memory", (long long)R->dims[1]);
     static size_t attr = 0;
@@ -406,7 +494,7 @@ tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, 
 cudaError_t launch_closure_right_raw(uint32_t* R, int64_t rows, int64_t words, const int64_t* rowptr,
                                      const int32_t* colidx, int64_t e_rows, int* changed,
                                      unsigned long long* counter, int32_t* pending, cudaStream_t stream) {
-    const size_t smem = (size_t)kClosureWarps * (words + kWindowWords * 16) * 4;
+    const size_t smem = (size_t)kClosureWarps * (words + kQueue) * 4;
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
     int dev = 0, sms = 148, per_sm = 0;
     cudaGetDevice(&dev);

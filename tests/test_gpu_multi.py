@@ -1,0 +1,90 @@
+"""Row-sharded closure and message passing on 2+ GPUs (one process per GPU,
+NCCL all-reduce of the changed word per sweep, NCCL all-gather of the
+per-node transform per layer), reassembled and checked against the f64
+oracle.  Skipped when the box has fewer than two GPUs."""
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tensor_logic_lang_b200 import abi, configs, shard
+from tensor_logic_lang_b200 import inputs as gen
+
+from gpu_helpers import TOL_TF32, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _world():
+    return min(torch.cuda.device_count(), 8) if torch.cuda.is_available() else 0
+
+
+def _closure_worker(rank, world, nid, n, q):
+    from tensor_logic_lang_b200.runtime import Context
+    ctx = Context(device=rank, rank=rank, world_size=world, nccl_id=nid, comm_timeout_ms=60000)
+    try:
+        ctx.set_sharding("Reach", abi.SHARD_ROWS)
+        p, _, sp, _ = configs.program(configs.closure, n=n)
+        ctx.run(p)
+        q.put((rank, "closure", ctx.bits("Reach", rows=shard.local_count(n, rank, world)), ctx.sweeps))
+    finally:
+        ctx.close()
+
+
+def _gnn_worker(rank, world, nid, n, f, q):
+    from tensor_logic_lang_b200.runtime import Context
+    ctx = Context(device=rank, rank=rank, world_size=world, nccl_id=nid, comm_timeout_ms=60000)
+    try:
+        for name in ("Adj", "H0", "H1", "H2"):
+            ctx.set_sharding(name, abi.SHARD_ROWS)
+        p, _, _, _ = configs.program(configs.gnn, n=n, f=f)
+        ctx.run(p)
+        rows = shard.local_count(n, rank, world)
+        q.put((rank, "gnn", ctx.tensor("H1", rows=rows), ctx.tensor("H2", rows=rows)))
+    finally:
+        ctx.close()
+
+
+def _run(target, world, *args):
+    from tensor_logic_lang_b200.runtime import unique_id
+    nid = unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, world, nid) + args + (q,)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return sorted(out, key=lambda t: t[0])
+
+
+@pytest.mark.skipif(_world() < 2, reason="needs two GPUs")
+def test_sharded_closure(oracle_lib):
+    world, n = _world(), 8192
+    out = _run(_closure_worker, world, n)
+    got = shard.assemble([o[2] for o in out], n)
+    _, _, sp, _ = configs.closure(n=n)
+    rows, cols, _ = sp["Edge"]
+    colptr, rowidx = gen.csr_from_coo(n, cols, rows)
+    R = np.zeros((n, n // 32), dtype=np.uint32)
+    np.bitwise_or.at(R, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
+    sweeps = oracle_lib.closure_right(n, colptr, rowidx, R)
+    np.testing.assert_array_equal(got, R)
+    assert all(o[3] == sweeps == 2 for o in out)
+
+
+@pytest.mark.skipif(_world() < 2, reason="needs two GPUs")
+def test_sharded_gnn(oracle_lib):
+    world, n, f = _world(), 4096, 128
+    out = _run(_gnn_worker, world, n, f)
+    h1 = shard.assemble([o[2] for o in out], n)
+    h2 = shard.assemble([o[3] for o in out], n)
+    _, d, sp, _ = configs.gnn(n=n, f=f)
+    rows, cols, _ = sp["Adj"]
+    rowptr, colidx = gen.csr_from_coo(n, rows, cols)
+    r1 = oracle_lib.gnn_layer(rowptr, colidx, d["H0"], d["W1"])
+    r2 = oracle_lib.gnn_layer(rowptr, colidx, r1, d["W2"])
+    assert_close(h1, r1, TOL_TF32, "H1")
+    assert_close(h2, r2, TOL_TF32, "H2")
