@@ -648,10 +648,12 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     ok = ok && (pb.mn ? make_map(&mb, pb.dst, p.N, Ke, pb.ld, 32, true) : make_map(&mb, pb.dst, Ke, p.N, pb.ld, BN, false));
     if (!ok) return launch_simt(c, p);
     const int num_kb = (int)((Ke + TC_BK - 1) / TC_BK);
-    // split K when the output tiles cannot fill the SMs (each split >= 4 k-blocks)
+    // split K only when the output tiles fill less than half of the SMs (each
+    // split >= 4 k-blocks): the atomic epilogue of a split costs more than the
+    // idle SMs of a grid that is already half a wave or more
     const int64_t tiles = ((p.N + BN - 1) / BN) * ((p.M + TC_BM - 1) / TC_BM);
     int splits = 1;
-    if (!p.epi_relu && tiles < c->sm_count && num_kb >= 8) {
+    if (!p.epi_relu && tiles * 2 <= c->sm_count && num_kb >= 8) {
         splits = (int)std::min<int64_t>((c->sm_count + tiles - 1) / tiles, num_kb / 4);
         if (splits < 1) splits = 1;
     }

@@ -74,116 +74,99 @@ __global__ void k_bits_to_dense(const uint32_t* bits, int64_t rows, int64_t cols
 // Right-form sweep on bit rows.
 //
 // Rows are independent under R[x] |= OR_{y in R[x]} succ(y).  A warp holds row
-// x in shared memory and closes it within the sweep:
-//  * rows are grabbed 32 at a time from a counter (heaviest rows, the low
-//    indices of a u < v DAG, first); the 32 lanes check the rows' pending
-//    words together and only rows with work are loaded;
+// x in shared memory and closes it within the sweep (a breadth-first search
+// from x over the successor lists):
+//  * rows are taken from a counter, one at a time in the first sweep (every
+//    row has work, and rows with large reach must not queue up behind one
+//    another on a single warp) and 32 at a time afterwards, when the 32 lanes
+//    check the rows' pending words together and load only rows with work;
 //  * pending[r] is the lowest word of row r that may hold a bit whose
 //    successors are not in the row yet (0 at the first sweep; none once the
 //    row is closed);
-//  * the set bits at or above that word go into a queue in shared memory;
-//    each step the 32 lanes take one queued bit each and OR its successors
-//    (CSR) into the row, queueing every bit that was new.
-// The row is closed when the queue drains, so a row never needs a second
-// sweep: on an edge set with u < v the first sweep closes every row (as the
-// reference's in-place z-ascending loop does) and the second one finds no
-// pending row, so the sweep counts match the reference's (2).  On edge sets
-// with back edges the fixpoint is the same bit for bit, reached in at most as
-// many sweeps.  If the queue overflows, the row falls back to a windowed scan
-// that re-expands every set bit in ascending order (idempotent), and a bit
-// that scan sets below its window is left pending for the next sweep.
-constexpr int kClosureWarps = 4;
-constexpr int kWindowWords = 32;
-constexpr int kQueue = 1024;        // queued bit positions per warp (uint32)
+//  * the row's set bits at or above that word start in the "spill" bit set;
+//    the spill set feeds a circular queue of bit positions, and each step
+//    every lane takes up to kItems queued bits, loads their successors
+//    (kEdges per item per pass, all loads of a pass in flight together) and
+//    ORs them into the row; every bit that was new joins the queue, or the
+//    spill set when the queue is full.
+// Every bit that enters the row is expanded exactly once, so the row is
+// closed when queue and spill set are empty; a row never needs a second
+// sweep.  On an edge set with u < v the first sweep closes every row (as the
+// reference's in-place z-ascending loop does) and the second finds no pending
+// row, so the sweep counts match the reference's (2).  On edge sets with back
+// edges the fixpoint is the same bit for bit, reached in at most as many
+// sweeps.
+constexpr int kQueue = 1024;   // queued bit positions per warp (uint32)
+constexpr int kItems = 4;      // queued bits one lane expands per step
+constexpr int kEdges = 4;      // successors one lane loads per item per pass
 
-// successors of y into the row; queue new bits (or flag an overflow)
-__device__ __forceinline__ bool expand_into(uint32_t* row, int64_t y, const int64_t* __restrict__ rowptr,
-                                            const int32_t* __restrict__ colidx, int64_t e_rows, uint32_t* q,
-                                            int* qtail, int head, bool* overflow) {
-    bool grew = false;
-    if (y >= e_rows) return false;
-    const int64_t e1 = rowptr[y + 1];
-    for (int64_t e = rowptr[y]; e < e1; ++e) {
-        const int32_t z = colidx[e];
-        const uint32_t bit = 1u << (z & 31);
-        if (row[z >> 5] & bit) continue;
-        const uint32_t old = atomicOr(&row[z >> 5], bit);
-        if (old & bit) continue;
-        grew = true;
-        const int pos = atomicAdd(qtail, 1);
-        if (pos < head + kQueue) q[pos % kQueue] = (uint32_t)z;
-        else *overflow = true;
+__device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
     }
-    return grew;
+    return v;
 }
 
-// Windowed ascending scan from word `from`: expands every set bit (again),
-// re-reading each 1024-bit window until stable.  Returns the lowest word a
-// successor landed in below its window (left pending), INT32_MAX if none.
-__device__ int32_t expand_windows(uint32_t* row, int64_t words, int64_t from, const int64_t* __restrict__ rowptr,
-                                  const int32_t* __restrict__ colidx, int64_t e_rows, uint16_t* wl, bool* grew) {
-    const int lane = threadIdx.x & 31;
-    int32_t low = INT32_MAX;
-    for (int64_t c0 = (from / kWindowWords) * kWindowWords; c0 < words; c0 += kWindowWords) {
-        const int64_t w = c0 + lane;
-        uint32_t done = 0;
-        for (;;) {
-            const uint32_t pend = (w < words ? row[w] : 0u) & ~done;
-            const int cnt = __popc(pend);
-            int pre = cnt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int v = __shfl_up_sync(0xffffffffu, pre, o);
-                if (lane >= o) pre += v;
+// Shared-memory words one warp of the sweep uses: row, spill set, queue.
+__host__ __device__ __forceinline__ int64_t closure_warp_words(int64_t words) { return 2 * words + kQueue; }
+
+// Moves up to `room` set bits of the spill set, lowest first from word `lo`,
+// into the queue at position `tail`, clearing them.  Returns how many it
+// moved and leaves in `lo` the lowest word that may still hold a bit (`words`
+// when the set is empty).  Warp-uniform.
+__device__ int harvest_spill(uint32_t* spill, int64_t words, int64_t& lo, uint32_t* q, int tail, int room,
+                             int lane) {
+    int stored = 0;
+    for (int64_t w0 = lo & ~int64_t(31); w0 < words; w0 += 32) {
+        const int64_t w = w0 + lane;
+        const uint32_t bits = w < words ? spill[w] : 0u;
+        const int cnt = __popc(bits);
+        const int pre = warp_inclusive_scan(cnt, lane);
+        const int total = __shfl_sync(0xffffffffu, pre, 31);
+        const int start = stored + pre - cnt;
+        const int allow = max(0, min(cnt, room - start));
+        uint32_t take = bits;
+        if (allow < cnt) {
+            take = 0;
+            uint32_t m = bits;
+            for (int i = 0; i < allow; ++i) {
+                take |= m & (0u - m);
+                m &= m - 1;
             }
-            const int total = __shfl_sync(0xffffffffu, pre, 31);
-            if (total == 0) break;
-            int at = pre - cnt;
-            for (uint32_t m = pend; m; m &= m - 1) wl[at++] = (uint16_t)(lane * 32 + __ffs(m) - 1);
-            done |= pend;
-            __syncwarp();
-            for (int i = lane; i < total; i += 32) {
-                const int64_t y = c0 * 32 + wl[i];
-                if (y >= e_rows) continue;
-                const int64_t e1 = rowptr[y + 1];
-                for (int64_t e = rowptr[y]; e < e1; ++e) {
-                    const int32_t z = colidx[e];
-                    const uint32_t bit = 1u << (z & 31);
-                    if (row[z >> 5] & bit) continue;
-                    const uint32_t old = atomicOr(&row[z >> 5], bit);
-                    if (!(old & bit)) {
-                        *grew = true;
-                        if ((z >> 5) < c0) low = min(low, (int32_t)(z >> 5));
-                    }
-                }
-            }
-            __syncwarp();
         }
+        int at = tail + start;
+        for (uint32_t m = take; m; m &= m - 1) q[(at++) % kQueue] = (uint32_t)(w * 32 + __ffs(m) - 1);
+        if (take) spill[w] = bits & ~take;
+        if (stored + total > room) {
+            const unsigned left = __ballot_sync(0xffffffffu, (bits & ~take) != 0u);
+            lo = w0 + (__ffs(left) - 1);
+            return room;
+        }
+        stored += total;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) low = min(low, __shfl_xor_sync(0xffffffffu, low, o));
-    return low;
+    lo = words;
+    return stored;
 }
 
-__global__ void __launch_bounds__(32 * kClosureWarps)
+__global__ void __launch_bounds__(128)
     k_closure_right(uint32_t* R, int64_t local_rows, int64_t words, const int64_t* __restrict__ rowptr,
                     const int32_t* __restrict__ colidx, int64_t e_rows, int* changed, unsigned long long* next_row,
-                    int32_t* pending) {
+                    int32_t* pending, int grab) {
     extern __shared__ uint32_t smem_u[];
-    __shared__ int qtail_s[kClosureWarps];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    uint32_t* row = smem_u + (int64_t)wib * (words + kQueue);
-    uint32_t* q = row + words;
-    uint16_t* wl = reinterpret_cast<uint16_t*>(q);       // the windowed fallback reuses the queue
-    int* qtail = &qtail_s[wib];
+    uint32_t* row = smem_u + (int64_t)wib * closure_warp_words(words);
+    uint32_t* spill = row + words;
+    uint32_t* q = spill + words;
     bool any_changed = false;
     for (;;) {
         unsigned long long base = 0;
-        if (lane == 0) base = atomicAdd(next_row, 32ull);
+        if (lane == 0) base = atomicAdd(next_row, (unsigned long long)grab);
         base = __shfl_sync(0xffffffffu, base, 0);
         if ((int64_t)base >= local_rows) break;
         const int64_t mine = (int64_t)base + lane;
-        const int32_t my_pend = mine < local_rows ? pending[mine] : INT32_MAX;
+        const int32_t my_pend = (lane < grab && mine < local_rows) ? pending[mine] : INT32_MAX;
         unsigned todo = __ballot_sync(0xffffffffu, my_pend < words);
         while (todo) {
             const int src = __ffs(todo) - 1;
@@ -191,50 +174,92 @@ __global__ void __launch_bounds__(32 * kClosureWarps)
             const int64_t r = (int64_t)base + src;
             const int64_t start_w = __shfl_sync(0xffffffffu, my_pend, src);
             uint32_t* grow = R + r * words;
-            for (int64_t w = lane; w < words; w += 32) row[w] = grow[w];
-            if (lane == 0) *qtail = 0;
-            __syncwarp();
-            // queue the row's set bits from its pending word on
-            bool overflow = false;
-            int stored = 0;
-            for (int64_t w0 = start_w & ~int64_t(31); w0 < words && !overflow; w0 += 32) {
-                const int64_t w = w0 + lane;
-                const uint32_t bits = (w < words && w >= start_w) ? row[w] : 0u;
-                const int cnt = __popc(bits);
-                int pre = cnt;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int v = __shfl_up_sync(0xffffffffu, pre, o);
-                    if (lane >= o) pre += v;
-                }
-                const int total = __shfl_sync(0xffffffffu, pre, 31);
-                if (stored + total > kQueue) { overflow = true; break; }
-                int at = stored + pre - cnt;
-                for (uint32_t m = bits; m; m &= m - 1) q[at++] = (uint32_t)(w * 32 + __ffs(m) - 1);
-                stored += total;
+            for (int64_t w = lane; w < words; w += 32) {
+                const uint32_t v = grow[w];
+                row[w] = v;
+                spill[w] = w >= start_w ? v : 0u;
             }
-            if (lane == 0) *qtail = stored;
             __syncwarp();
+            int64_t lo = start_w;   // lowest spill word that may hold a bit
+            int head = 0, tail = 0;
             bool grew = false;
-            int head = 0;
-            while (!overflow) {
-                const int tail = *(volatile int*)qtail;
-                if (head >= tail) break;
-                const int take = min(32, tail - head);
-                uint32_t y = 0;
-                if (lane < take) y = q[(head + lane) % kQueue];
-                __syncwarp();
-                bool ovf = false;
-                if (lane < take) grew |= expand_into(row, y, rowptr, colidx, e_rows, q, qtail, head + take, &ovf);
+            for (;;) {
+                if (head == tail) {
+                    if (lo >= words) break;
+                    const int got = harvest_spill(spill, words, lo, q, tail, kQueue, lane);
+                    __syncwarp();
+                    tail += got;
+                    if (got == 0) break;
+                    continue;
+                }
+                const int take = min(32 * kItems, tail - head);
+                int64_t b[kItems], e[kItems];
+#pragma unroll
+                for (int k = 0; k < kItems; ++k) {
+                    const int idx = k * 32 + lane;
+                    const uint32_t y = idx < take ? q[(head + idx) % kQueue] : 0u;
+                    b[k] = 0;
+                    e[k] = 0;
+                    if (idx < take && (int64_t)y < e_rows) {
+                        b[k] = rowptr[y];
+                        e[k] = rowptr[y + 1];
+                    }
+                }
+                __syncwarp();   // the taken slots may be refilled from here on
                 head += take;
-                overflow = __any_sync(0xffffffffu, ovf);
-                __syncwarp();
+                for (int64_t off = 0;; off += kEdges) {
+                    int32_t z[kItems][kEdges];
+#pragma unroll
+                    for (int k = 0; k < kItems; ++k)
+#pragma unroll
+                        for (int j = 0; j < kEdges; ++j)
+                            z[k][j] = b[k] + off + j < e[k] ? colidx[b[k] + off + j] : -1;
+                    uint32_t fresh = 0;
+#pragma unroll
+                    for (int k = 0; k < kItems; ++k)
+#pragma unroll
+                        for (int j = 0; j < kEdges; ++j) {
+                            const int32_t zz = z[k][j];
+                            if (zz < 0) continue;
+                            const uint32_t bit = 1u << (zz & 31);
+                            if (row[zz >> 5] & bit) continue;
+                            if (!(atomicOr(&row[zz >> 5], bit) & bit)) fresh |= 1u << (k * kEdges + j);
+                        }
+                    const int cnt = __popc(fresh);
+                    const int pre = warp_inclusive_scan(cnt, lane);
+                    const int total = __shfl_sync(0xffffffffu, pre, 31);
+                    int at = tail + pre - cnt;
+                    int64_t low = INT64_MAX;
+#pragma unroll
+                    for (int k = 0; k < kItems; ++k)
+#pragma unroll
+                        for (int j = 0; j < kEdges; ++j) {
+                            if (!((fresh >> (k * kEdges + j)) & 1u)) continue;
+                            const int32_t zz = z[k][j];
+                            if (at < head + kQueue) {
+                                q[at % kQueue] = (uint32_t)zz;
+                            } else {
+                                atomicOr(&spill[zz >> 5], 1u << (zz & 31));
+                                low = min(low, (int64_t)(zz >> 5));
+                            }
+                            ++at;
+                        }
+                    if (total) {
+                        grew = true;
+                        tail = min(tail + total, head + kQueue);
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) low = min(low, __shfl_xor_sync(0xffffffffu, low, o));
+                        lo = min(lo, low);
+                    }
+                    bool more = false;
+#pragma unroll
+                    for (int k = 0; k < kItems; ++k) more = more || (b[k] + off + kEdges < e[k]);
+                    __syncwarp();
+                    if (!__any_sync(0xffffffffu, more)) break;
+                }
             }
-            int32_t low = INT32_MAX;
-            if (overflow) low = expand_windows(row, words, 0, rowptr, colidx, e_rows, wl, &grew);
-            const bool row_grew = __any_sync(0xffffffffu, grew);
-            if (lane == 0) pending[r] = low;
-            if (row_grew) {
+            if (lane == 0) pending[r] = INT32_MAX;
+            if (grew) {
                 for (int64_t w = lane; w < words; w += 32) grow[w] = row[w];
                 any_changed = true;
             }
@@ -242,6 +267,27 @@ __global__ void __launch_bounds__(32 * kClosureWarps)
         }
     }
     if (lane == 0 && any_changed) *changed = 1;
+}
+
+// Warps per block and blocks per SM for a sweep over rows of `words` words
+// with at most `smem_cap` bytes of shared memory per block: the split that
+// keeps the most warps resident.
+static void closure_shape(int64_t words, size_t smem_cap, int* wpb_out, int* per_sm_out, size_t* smem_out) {
+    const size_t per_warp = (size_t)closure_warp_words(words) * 4;
+    int best_wpb = 1, best_per_sm = 0;
+    for (int wpb = 1; wpb <= 4; ++wpb) {
+        const size_t smem = per_warp * wpb;
+        if (smem > smem_cap) break;
+        int per_sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_closure_right, 32 * wpb, smem);
+        if (per_sm * wpb > best_per_sm * best_wpb) {
+            best_wpb = wpb;
+            best_per_sm = per_sm;
+        }
+    }
+    *wpb_out = best_wpb;
+    *per_sm_out = best_per_sm < 1 ? 1 : best_per_sm;
+    *smem_out = per_warp * best_wpb;
 }
 
 // Left-form sweep Rnew[x] = R[x] | OR_{z in succ(x)} R[z] from the previous
@@ -453,14 +499,10 @@ tl_status launch_dense_to_csr(tl_ctx* c, Tensor* t) {
 
 tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, int sweep) {
     const int64_t words = R->bits_words;
-    const size_t smem = (size_t)kClosureWarps * (words + kQueue) * 4;
-    if (smem > 200 * 1024)
+    constexpr size_t kSmemCap = 200 * 1024;
+    if ((size_t)closure_warp_words(words) * 4 > kSmemCap)
         return fail(c, TL_ERR_UNSUPPORTED, "closure rows of %lld bits exceed shared memory", (long long)R->dims[1]);
-    static size_t attr = 0;
-    if (smem > 48 * 1024 && smem > attr) {
-        TL_CK(c, cudaFuncSetAttribute(k_closure_right, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = smem;
-    }
+    TL_CK(c, cudaFuncSetAttribute(k_closure_right, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
     const int64_t rows = R->bits_rows;
     // fixpoint-long state: the per-row pending word (0 = expand everything)
     if ((size_t)rows * 4 > c->aux_cap) {
@@ -478,33 +520,36 @@ tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, 
     // algorithmic bytes of one sweep: read and write the local bit rows, read the CSR
     const double bytes = (double)rows * words * 4.0 * 2.0 + (double)(E->csr_rows + 1) * 8.0 + (double)E->nnz * 4.0;
     LaunchScope L(c, "closure_sweep", bytes, 0);
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_closure_right, 32 * kClosureWarps, smem);
-    if (per_sm < 1) per_sm = 1;
-    int64_t grid = std::min<int64_t>((rows + kClosureWarps - 1) / kClosureWarps, (int64_t)c->sm_count * per_sm);
+    int wpb = 1, per_sm = 1;
+    size_t smem = 0;
+    closure_shape(words, kSmemCap, &wpb, &per_sm, &smem);
+    int64_t grid = std::min<int64_t>((rows + wpb - 1) / wpb, (int64_t)c->sm_count * per_sm);
     if (grid < 1) grid = 1;
-    k_closure_right<<<(unsigned)grid, 32 * kClosureWarps, smem, c->stream>>>(R->bits, rows, words, E->rowptr,
-                                                                            E->colidx, E->csr_rows, d_changed,
-                                                                            counter, pending);
+    k_closure_right<<<(unsigned)grid, 32 * wpb, smem, c->stream>>>(R->bits, rows, words, E->rowptr, E->colidx,
+                                                                   E->csr_rows, d_changed, counter, pending,
+                                                                   sweep == 0 ? 1 : 32);
     return L.done();
 }
 
 // The same right-form sweep with every buffer supplied by the caller and no
-// context: for the allocation-free entry point (noalloc.cu).
+// context: for the allocation-free entry point (noalloc.cu).  Blocks stay
+// within the default 48 KB of shared memory.
 cudaError_t launch_closure_right_raw(uint32_t* R, int64_t rows, int64_t words, const int64_t* rowptr,
                                      const int32_t* colidx, int64_t e_rows, int* changed,
-                                     unsigned long long* counter, int32_t* pending, cudaStream_t stream) {
-    const size_t smem = (size_t)kClosureWarps * (words + kQueue) * 4;
-    if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    int dev = 0, sms = 148, per_sm = 0;
+                                     unsigned long long* counter, int32_t* pending, int sweep,
+                                     cudaStream_t stream) {
+    constexpr size_t kSmemCap = 48 * 1024;
+    if ((size_t)closure_warp_words(words) * 4 > kSmemCap) return cudaErrorInvalidValue;
+    int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_closure_right, 32 * kClosureWarps, smem);
-    if (per_sm < 1) per_sm = 1;
-    int64_t grid = std::min<int64_t>((rows + kClosureWarps - 1) / kClosureWarps, (int64_t)sms * per_sm);
+    int wpb = 1, per_sm = 1;
+    size_t smem = 0;
+    closure_shape(words, kSmemCap, &wpb, &per_sm, &smem);
+    int64_t grid = std::min<int64_t>((rows + wpb - 1) / wpb, (int64_t)sms * per_sm);
     if (grid < 1) grid = 1;
-    k_closure_right<<<(unsigned)grid, 32 * kClosureWarps, smem, stream>>>(R, rows, words, rowptr, colidx, e_rows,
-                                                                         changed, counter, pending);
+    k_closure_right<<<(unsigned)grid, 32 * wpb, smem, stream>>>(R, rows, words, rowptr, colidx, e_rows, changed,
+                                                                counter, pending, sweep == 0 ? 1 : 32);
     return cudaGetLastError();
 }
 

@@ -21,7 +21,8 @@
 namespace tl {
 cudaError_t launch_closure_right_raw(uint32_t* R, int64_t rows, int64_t words, const int64_t* rowptr,
                                      const int32_t* colidx, int64_t e_rows, int* changed,
-                                     unsigned long long* counter, int32_t* pending, cudaStream_t stream);
+                                     unsigned long long* counter, int32_t* pending, int sweep,
+                                     cudaStream_t stream);
 }
 
 namespace {
@@ -77,8 +78,8 @@ extern "C" tl_status tl_closure_noalloc(int64_t n, const int64_t* d_rowptr, cons
     int host_changed = 1;
     while (sweeps < max_sweeps && host_changed) {
         if (cudaMemsetAsync(scratch, 0, kControlBytes, s) != cudaSuccess) return TL_ERR_CUDA;
-        if (tl::launch_closure_right_raw(d_reach, n, words, d_rowptr, d_colidx, n, changed, counter, pending, s) !=
-            cudaSuccess)
+        if (tl::launch_closure_right_raw(d_reach, n, words, d_rowptr, d_colidx, n, changed, counter, pending, sweeps,
+                                         s) != cudaSuccess)
             return TL_ERR_CUDA;
         // the changed word into a host stack variable (no pinned buffer needed)
         if (cudaMemcpyAsync(&host_changed, changed, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
