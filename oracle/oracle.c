@@ -1095,8 +1095,20 @@ void or_gemm(int64_t M, int64_t N, int64_t K, const double* A, int64_t sam, int6
  * reference; Edge is read from a bit matrix (its dense f64 view would need
  * n*n*8 bytes).  Used as the timed CPU sample of the reference algorithm. */
 int64_t or_closure_literal_rows(int64_t n, const uint32_t* Ebits, int64_t x0, int64_t nrows, double* Rrows) {
+    return or_closure_literal_rows_mt(n, Ebits, x0, nrows, Rrows, 1);
+}
+
+/* The same literal sweep with the rows spread over n_threads host threads
+   (rows are independent within the right-form sweep). */
+int64_t or_closure_literal_rows_mt(int64_t n, const uint32_t* Ebits, int64_t x0, int64_t nrows, double* Rrows,
+                                   int32_t n_threads) {
     int64_t W = (n + 31) / 32;
     int64_t changed = 0;
+    (void)n_threads;
+#ifdef _OPENMP
+    if (n_threads > 0) omp_set_num_threads(n_threads);
+#endif
+    #pragma omp parallel for schedule(dynamic, 1) reduction(+ : changed)
     for (int64_t x = 0; x < nrows; ++x) {
         double* row = Rrows + x * n;
         for (int64_t z = 0; z < n; ++z) {

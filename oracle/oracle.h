@@ -69,6 +69,8 @@ void or_gemm(int64_t M, int64_t N, int64_t K, const double* A, int64_t sam, int6
 
 /* One literal right-form sweep over rows [x0, x0+nrows) (timed CPU sample). */
 int64_t or_closure_literal_rows(int64_t n, const uint32_t* Ebits, int64_t x0, int64_t nrows, double* Rrows);
+int64_t or_closure_literal_rows_mt(int64_t n, const uint32_t* Ebits, int64_t x0, int64_t nrows, double* Rrows,
+                                   int32_t n_threads);
 
 #ifdef __cplusplus
 }

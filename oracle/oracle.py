@@ -52,6 +52,9 @@ def _load(name="liboracle.so"):
     lib.or_closure_literal_rows.restype = C.c_int64
     lib.or_closure_literal_rows.argtypes = [C.c_int64, C.POINTER(C.c_uint32), C.c_int64, C.c_int64,
                                             C.POINTER(C.c_double)]
+    lib.or_closure_literal_rows_mt.restype = C.c_int64
+    lib.or_closure_literal_rows_mt.argtypes = [C.c_int64, C.POINTER(C.c_uint32), C.c_int64, C.c_int64,
+                                               C.POINTER(C.c_double), C.c_int32]
     return lib
 
 
@@ -146,9 +149,11 @@ def gemm(A, B, C_init=None, relu_per_term=False, scale=1.0, threads=0):
     return out
 
 
-def closure_literal_rows(n, Ebits, R_rows, x0=0, libname="liboracle.so"):
-    """One literal reference-order sweep over the given f64 rows (in place)."""
+def closure_literal_rows(n, Ebits, R_rows, x0=0, threads=1, libname="liboracle.so"):
+    """One literal reference-order sweep over the given f64 rows (in place),
+    rows spread over `threads` host threads."""
     Ebits = np.ascontiguousarray(Ebits, dtype=np.uint32)
     assert R_rows.dtype == np.float64 and R_rows.flags.c_contiguous
-    return lib(libname).or_closure_literal_rows(n, Ebits.ctypes.data_as(C.POINTER(C.c_uint32)), x0,
-                                                R_rows.shape[0], R_rows.ctypes.data_as(C.POINTER(C.c_double)))
+    return lib(libname).or_closure_literal_rows_mt(n, Ebits.ctypes.data_as(C.POINTER(C.c_uint32)), x0,
+                                                   R_rows.shape[0], R_rows.ctypes.data_as(C.POINTER(C.c_double)),
+                                                   int(threads))

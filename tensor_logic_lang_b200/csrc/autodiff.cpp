@@ -173,11 +173,15 @@ tl_status run_grad(tl_ctx* c, const Grad& g) {
             if (!y) return TL_OK;
         }
         if (!upp && g.rule != R_LOG) return TL_OK;     // zero upstream adds zeros
-        TL_TRY(ensure_dense(c, out));
         const int rule = g.rule == R_PASS ? G_PASS : g.rule == R_RELU ? G_RELU : g.rule == R_SIGMOID ? G_SIGMOID
                          : g.rule == R_TANH ? G_TANH : g.rule == R_EXP ? G_EXP : G_LOG;
+        // a fresh (calloc) gradient buffer that the rule covers is written, not zeroed and added to
+        const bool fresh = out->zero && !out->dense_valid && upp &&
+                           grad_elem_covers(rule, out->total, up->total, x ? x->total : 0);
+        if (fresh) TL_TRY(alloc_dense_public(c, out));
+        else TL_TRY(ensure_dense(c, out));
         TL_TRY(launch_grad_elem(c, rule, out->dense, out->total, upp, up->total, xp, x ? x->total : 0, yp,
-                                y ? y->total : 0));
+                                y ? y->total : 0, fresh ? 1 : 0));
         mark_written_dense(out);
         out->boolean = false;
         return TL_OK;

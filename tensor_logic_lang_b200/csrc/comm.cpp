@@ -11,7 +11,9 @@
 #include <string.h>
 
 #include <chrono>
+#include <cstdlib>
 #include <thread>
+#include <vector>
 
 #include "tl_internal.h"
 
@@ -75,6 +77,108 @@ tl_status comm_allgather(tl_ctx* c, const void* d_send, void* d_recv, size_t byt
     ncclResult_t r = ncclAllGather(d_send, d_recv, bytes_per_rank, ncclChar, (ncclComm_t)c->comm, c->stream);
     if (r != ncclSuccess) return nccl_fail(c, r, "ncclAllGather");
     return TL_OK;
+}
+
+// ----------------------------------------------------------------------------
+// Fixpoint flags over peer memory.  Each rank allocates a slot array
+// (kMaxPeers ranks x 2 sweep parities x 8 bytes), exports it with a CUDA IPC
+// handle and maps every other rank's array, so the one-launch fixpoint can
+// store its changed word straight into every peer's memory over NVLink.  The
+// handles travel in one all-gather.  If any rank cannot take part (ranks
+// sharing a GPU, more ranks than kMaxPeers, a handle that does not open),
+// a second collective makes every rank fall back to the per-sweep all-reduce,
+// so all ranks take the same path.
+// ----------------------------------------------------------------------------
+namespace {
+struct PeerRecord {
+    cudaIpcMemHandle_t handle;
+    unsigned char uuid[16];
+    int32_t ok;
+    int32_t pad[3];
+};
+constexpr size_t kSlotBytes = 4096;
+}  // namespace
+
+void comm_peer_release(tl_ctx* c) {
+    for (int j = 0; j < kMaxPeers; ++j) {
+        if (c->peer_slots[j] && j != c->rank) cudaIpcCloseMemHandle(c->peer_slots[j]);
+        c->peer_slots[j] = nullptr;
+    }
+    if (c->peer_own) cudaFree(c->peer_own);
+    c->peer_own = nullptr;
+    cudaGetLastError();
+}
+
+tl_status comm_peer_setup(tl_ctx* c) {
+    if (c->peer_state != 0) return TL_OK;
+    c->peer_state = -1;
+    if (!c->comm) return fail(c, TL_ERR_COMM, "no communicator");
+    const int world = c->world;
+    PeerRecord mine{};
+    mine.ok = world <= kMaxPeers && !getenv("TL_NO_PEER_FLAGS");
+    if (mine.ok && cudaMalloc(&c->peer_own, kSlotBytes) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaMemsetAsync(c->peer_own, 0, kSlotBytes, c->stream) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaIpcGetMemHandle(&mine.handle, c->peer_own) != cudaSuccess) mine.ok = 0;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, c->device) == cudaSuccess) memcpy(mine.uuid, prop.uuid.bytes, 16);
+    else mine.ok = 0;
+    cudaGetLastError();
+
+    std::vector<PeerRecord> all(world);
+    PeerRecord* d = nullptr;
+    TL_CK(c, cudaMalloc(&d, sizeof(PeerRecord) * (world + 1)));
+    tl_status st = TL_OK;
+    do {
+        if (cudaMemcpyAsync(d + world, &mine, sizeof mine, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+            st = fail(c, TL_ERR_CUDA, "peer flag set-up: copy");
+            break;
+        }
+        ncclResult_t r = ncclAllGather(d + world, d, sizeof(PeerRecord), ncclChar, (ncclComm_t)c->comm, c->stream);
+        if (r != ncclSuccess) {
+            st = nccl_fail(c, r, "ncclAllGather");
+            break;
+        }
+        if ((st = comm_wait(c)) != TL_OK) break;
+        if (cudaMemcpy(all.data(), d, sizeof(PeerRecord) * world, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            st = fail(c, TL_ERR_CUDA, "peer flag set-up: copy back");
+            break;
+        }
+        int ok = 1;
+        for (int j = 0; j < world; ++j) {
+            ok = ok && all[j].ok;
+            for (int i = 0; i < j; ++i) ok = ok && memcmp(all[i].uuid, all[j].uuid, 16) != 0;
+        }
+        for (int j = 0; ok && j < world; ++j) {
+            if (j == c->rank) {
+                c->peer_slots[j] = (unsigned long long*)c->peer_own;
+                continue;
+            }
+            void* p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, all[j].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+                break;
+            }
+            c->peer_slots[j] = (unsigned long long*)p;
+        }
+        // every rank takes the peer path only if every rank can
+        int* flag = reinterpret_cast<int*>(d + world);
+        const int bad = ok ? 0 : 1;
+        if (cudaMemcpyAsync(flag, &bad, sizeof bad, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+            st = fail(c, TL_ERR_CUDA, "peer flag set-up: copy");
+            break;
+        }
+        if ((st = comm_allreduce_max_int(c, flag, 1)) != TL_OK) break;
+        int any_bad = 1;
+        if (cudaMemcpy(&any_bad, flag, sizeof any_bad, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            st = fail(c, TL_ERR_CUDA, "peer flag set-up: copy back");
+            break;
+        }
+        c->peer_state = any_bad ? -1 : 1;
+    } while (false);
+    cudaFree(d);
+    if (c->peer_state != 1) comm_peer_release(c);
+    return st;
 }
 
 }  // namespace tl

@@ -1,0 +1,595 @@
+// The right-form closure fixpoint in one cooperative launch.
+//
+// Reference semantics (src/codegen/fixpoint.zig:46-98, 167-297): repeat
+// sweeps of  R[x,z] max= step(R[x,y] E[y,z])  until a sweep changes nothing,
+// at most max_sweeps times.  On bit rows one sweep is R[x] |= OR_{y in R[x]}
+// succ(y) for every row x; rows never read other rows.
+//
+// One launch runs every sweep.  Blocks stay resident (cooperative launch) and
+// take rows from a counter; after each sweep they meet at a grid barrier,
+// where the last block to arrive settles the sweep: it reads the changed
+// word, on a multi-GPU context exchanges it with every other rank through
+// peer memory (one 8-byte store per peer over NVLink, then a wait for the
+// peers' stores), and decides whether another sweep runs.  The host reads
+// the sweep count once, after the launch.  Every wait is bounded by
+// %globaltimer; a wait that runs out records an error word and the kernel
+// returns.
+//
+// Per row, a warp keeps the row in shared memory and closes it with a
+// breadth-first search over a successor table: node y's entry is one 32-byte
+// sector holding up to 8 successors (unused slots hold a sentinel bit that is
+// always set), so a queued bit costs one load.  Nodes with more than 8
+// successors keep 7 in the table, mark slot 7, and the rest are read from the
+// CSR.  Each step a lane takes up to kFixItems queued bits; every successor
+// that was not in the row is set and queued, or put in the spill bit set
+// when the queue is full.  Each bit that enters the row is expanded exactly
+// once, so the row is closed when queue and spill set are empty and never
+// needs a second sweep: on an edge set with u < v the first sweep closes
+// every row, as the reference's in-place z-ascending loop does, and the
+// second finds nothing pending (2 sweeps, as the reference).
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
+#include "tl_internal.h"
+
+namespace tl {
+namespace {
+
+constexpr int kFixQueue = 1024;   // queued bit positions per warp
+constexpr int kFixItems = 4;      // queued bits one lane expands per step
+constexpr int kFixWarps = 4;      // most warps per block
+static_assert((kFixQueue & (kFixQueue - 1)) == 0, "queue positions wrap with a mask");
+static_assert(kFixItems == 4, "the extra-successor pass selects among 4 items");
+
+struct FixState {
+    unsigned long long next_row[2];   // row counters, by sweep parity
+    int changed[2];                   // a row grew this sweep, by parity
+    unsigned int bar_count;           // blocks arrived at the barrier
+    unsigned int bar_gen;             // barriers completed
+    int go;                           // another sweep runs
+    int sweeps;                       // sweeps completed
+    int last_changed;                 // the last sweep changed a row (all ranks)
+    int err;                          // 1: barrier wait ran out, 2: peer wait ran out
+};
+
+struct FixArgs {
+    uint32_t* R;
+    int64_t rows, words, wpad;
+    const int4* succ;
+    const int64_t* rowptr;
+    const int32_t* colidx;
+    int64_t e_rows;
+    int32_t* pending;
+    FixState* st;
+    int lazy;                  // rows not written yet: row r starts as succ(r * row_stride + row_offset)
+    int64_t row_stride, row_offset;
+    int max_sweeps;
+    unsigned nblocks;
+    int world, rank;
+    unsigned long long* slots[kMaxPeers];   // every rank's slot array, [rank][parity]
+    unsigned long long token0;              // sweeps this context exchanged before
+    unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void store_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long load_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int scan_incl(int v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    return v;
+}
+
+__device__ __forceinline__ int64_t warp_min64(int64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v, o));
+    return v;
+}
+
+// Queue slot `pos` if it lies below `limit`, else the spill set.
+__device__ __forceinline__ void enqueue(uint32_t* q, uint32_t* spill, int pos, int limit, int32_t z, int64_t& low) {
+    if (pos < limit) {
+        q[(unsigned)pos & (kFixQueue - 1)] = (uint32_t)z;
+    } else {
+        atomicOr(&spill[z >> 5], 1u << (z & 31));
+        low = min(low, (int64_t)(z >> 5));
+    }
+}
+
+// Test-and-set of bit z of the row; true when it was not set before.
+__device__ __forceinline__ bool set_new(uint32_t* row, int32_t z) {
+    const uint32_t bit = 1u << (z & 31);
+    if (row[z >> 5] & bit) return false;
+    return !(atomicOr(&row[z >> 5], bit) & bit);
+}
+
+// Moves up to `room` bits of the spill set, lowest first from word `lo`, into
+// the queue at `tail`, clearing them; leaves in `lo` the lowest word that may
+// still hold a bit (`words` when none).  Warp-uniform.
+__device__ __forceinline__ int harvest(uint32_t* spill, int64_t words, int64_t& lo, uint32_t* q, int tail, int room, int lane) {
+    int stored = 0;
+    for (int64_t w0 = lo & ~int64_t(31); w0 < words; w0 += 32) {
+        const int64_t w = w0 + lane;
+        const uint32_t bits = w < words ? spill[w] : 0u;
+        const int cnt = __popc(bits);
+        const int pre = scan_incl(cnt, lane);
+        const int total = __shfl_sync(0xffffffffu, pre, 31);
+        const int start = stored + pre - cnt;
+        const int allow = max(0, min(cnt, room - start));
+        uint32_t take = bits;
+        if (allow < cnt) {
+            take = 0;
+            uint32_t m = bits;
+            for (int i = 0; i < allow; ++i) {
+                take |= m & (0u - m);
+                m &= m - 1;
+            }
+        }
+        int at = tail + start;
+        for (uint32_t m = take; m; m &= m - 1)
+            q[(unsigned)(at++) & (kFixQueue - 1)] = (uint32_t)(w * 32 + __ffs(m) - 1);
+        if (take) spill[w] = bits & ~take;
+        if (stored + total > room) {
+            const unsigned left = __ballot_sync(0xffffffffu, (bits & ~take) != 0u);
+            lo = w0 + (__ffs(left) - 1);
+            return room;
+        }
+        stored += total;
+    }
+    lo = words;
+    return stored;
+}
+
+// Closes every pending row taken from `next_row`; true if a row grew.
+__device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long* next_row, int grab, bool lazy,
+                                           uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
+    const int64_t words = a.words;
+    const bool vec = (words & 3) == 0;
+    bool any = false;
+    for (;;) {
+        unsigned long long base = 0;
+        if (lane == 0) base = atomicAdd(next_row, (unsigned long long)grab);
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if ((int64_t)base >= a.rows) break;
+        const int64_t mine = (int64_t)base + lane;
+        const int32_t my_pend = (lane < grab && mine < a.rows) ? a.pending[mine] : INT32_MAX;
+        unsigned todo = __ballot_sync(0xffffffffu, my_pend < words);
+        while (todo) {
+            const int src = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int64_t r = (int64_t)base + src;
+            const int64_t start_w = __shfl_sync(0xffffffffu, my_pend, src);
+            uint32_t* grow = a.R + r * words;
+
+            int head = 0, tail = 0;
+            int64_t lo = words;
+            if (lazy) {
+                // the row is step(E)'s row: start empty with the row's own
+                // node queued; its successors (the starting bits) do not
+                // count as growth
+                for (int64_t w = lane * 4; w < a.wpad; w += 128)
+                    *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
+                if (lane == 0) q[0] = (uint32_t)(r * a.row_stride + a.row_offset);
+                tail = 1;
+                __syncwarp();
+            } else {
+            // load the row; its set bits from the pending word on are the
+            // first frontier (queue, then spill set)
+            int stored = 0;
+            int64_t low = INT64_MAX;
+            for (int64_t w0 = 0; w0 < words; w0 += 128) {
+                const int64_t w = w0 + lane * 4;
+                uint32_t v[4] = {0u, 0u, 0u, 0u};
+                if (vec) {
+                    if (w < words) {
+                        const uint4 t = *reinterpret_cast<const uint4*>(grow + w);
+                        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+                        *reinterpret_cast<uint4*>(row + w) = t;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (w + i < words) {
+                            v[i] = grow[w + i];
+                            row[w + i] = v[i];
+                        }
+                }
+                int cnt = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (w + i < start_w) v[i] = 0u;
+                    cnt += __popc(v[i]);
+                }
+                if (!__any_sync(0xffffffffu, cnt)) continue;
+                const int pre = scan_incl(cnt, lane);
+                const int total = __shfl_sync(0xffffffffu, pre, 31);
+                if (cnt) {
+                    int at = stored + pre - cnt;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        for (uint32_t m = v[i]; m; m &= m - 1, ++at) {
+                            if (at < kFixQueue) {
+                                q[at] = (uint32_t)((w + i) * 32 + __ffs(m) - 1);
+                            } else {
+                                spill[w + i] |= m & (0u - m);
+                                low = min(low, w + i);
+                            }
+                        }
+                }
+                stored += total;
+            }
+            tail = min(stored, kFixQueue);
+            lo = warp_min64(low);
+            if (lo > words) lo = words;
+            __syncwarp();
+            }
+
+            bool grew = false;
+            for (;;) {
+                if (head == tail) {
+                    if (lo >= words) break;
+                    const int got = harvest(spill, words, lo, q, tail, kFixQueue, lane);
+                    __syncwarp();
+                    tail += got;
+                    if (got == 0) break;
+                    continue;
+                }
+                // growth counts except while expanding a lazy row's own node
+                const bool counts = !lazy || head != 0;
+                const int take = min(32 * kFixItems, tail - head);
+                const int nk = (take + 31) >> 5;
+                int4 A[kFixItems], B[kFixItems];
+                int32_t Y[kFixItems];
+#pragma unroll
+                for (int k = 0; k < kFixItems; ++k) {
+                    A[k] = make_int4(-1, -1, -1, -1);
+                    B[k] = make_int4(-1, -1, -1, -1);
+                    Y[k] = -1;
+                    if (k < nk) {
+                        const int idx = k * 32 + lane;
+                        if (idx < take) {
+                            const int32_t y = (int32_t)q[(unsigned)(head + idx) & (kFixQueue - 1)];
+                            Y[k] = y;
+                            A[k] = __ldg(&a.succ[2 * (int64_t)y]);
+                            B[k] = __ldg(&a.succ[2 * (int64_t)y + 1]);
+                        }
+                    }
+                }
+                __syncwarp();   // the taken slots may be refilled from here on
+                head += take;
+                const int limit = head + kFixQueue;
+                unsigned long long fresh = 0;
+#pragma unroll
+                for (int k = 0; k < kFixItems; ++k) {
+                    if (k < nk && Y[k] >= 0) {
+                        const int32_t s[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if ((j < 7 || s[j] >= 0) && set_new(row, s[j])) fresh |= 1ull << (k * 8 + j);
+                    }
+                }
+                const int cnt = __popcll(fresh);
+                const int pre = scan_incl(cnt, lane);
+                const int total = __shfl_sync(0xffffffffu, pre, 31);
+                int64_t slow = INT64_MAX;
+                if (fresh) {
+                    int at = tail + pre - cnt;
+#pragma unroll
+                    for (int k = 0; k < kFixItems; ++k) {
+                        if (!((fresh >> (k * 8)) & 0xffull)) continue;
+                        const int32_t s[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if ((fresh >> (k * 8 + j)) & 1ull) enqueue(q, spill, at++, limit, s[j], slow);
+                    }
+                }
+                if (total) {
+                    grew = grew || counts;
+                    tail = min(tail + total, limit);
+                }
+                // successors past the table's 7 (slot 7 marked with -2), one
+                // per lane per round, items of a lane taken in turn
+                unsigned xm = 0;
+#pragma unroll
+                for (int k = 0; k < kFixItems; ++k)
+                    if (k < nk && Y[k] >= 0 && B[k].w == -2) xm |= 1u << k;
+                if (__any_sync(0xffffffffu, xm)) {
+                    int64_t e = 0, e_end = 0;
+                    for (;;) {
+                        if (e >= e_end && xm) {
+                            const int k = __ffs(xm) - 1;
+                            xm &= xm - 1;
+                            const int32_t y = k == 0 ? Y[0] : k == 1 ? Y[1] : k == 2 ? Y[2] : Y[3];
+                            e = a.rowptr[y] + 7;
+                            e_end = a.rowptr[y + 1];
+                        }
+                        if (!__any_sync(0xffffffffu, e < e_end)) break;
+                        bool f = false;
+                        int32_t z = 0;
+                        if (e < e_end) {
+                            z = a.colidx[e++];
+                            f = set_new(row, z);
+                        }
+                        const unsigned bal = __ballot_sync(0xffffffffu, f);
+                        if (f) enqueue(q, spill, tail + __popc(bal & ((1u << lane) - 1u)), limit, z, slow);
+                        if (bal) {
+                            grew = grew || counts;
+                            tail = min(tail + __popc(bal), limit);
+                        }
+                    }
+                }
+                lo = min(lo, warp_min64(slow));
+                __syncwarp();
+            }
+            if (lane == 0) a.pending[r] = INT32_MAX;
+            if (grew || lazy) {
+                if (vec) {
+                    for (int64_t w = lane * 4; w < words; w += 128)
+                        *reinterpret_cast<uint4*>(grow + w) = *reinterpret_cast<const uint4*>(row + w);
+                } else {
+                    for (int64_t w = lane; w < words; w += 32) grow[w] = row[w];
+                }
+                any = any || grew;
+            }
+            __syncwarp();
+        }
+    }
+    return any;
+}
+
+// Last block of a sweep on a multi-GPU context: publish this rank's changed
+// word to every rank (slot [rank][parity] of each rank's array), then wait for
+// every rank's word of this sweep.  The parity slots keep a rank that is one
+// sweep ahead from overwriting a word not read yet.  Returns the OR.
+__device__ int exchange_changed(const FixArgs& a, int s, int c, int* ok) {
+    const unsigned long long token = a.token0 + (unsigned long long)s + 1;
+    const unsigned long long v = (token << 1) | (c ? 1ull : 0ull);
+    const int par = s & 1;
+    for (int j = 0; j < a.world; ++j) store_release_sys(a.slots[j] + 2 * a.rank + par, v);
+    int any = c;
+    const unsigned long long t0 = global_ns();
+    const unsigned long long* mine = a.slots[a.rank];
+    for (int j = 0; j < a.world; ++j) {
+        unsigned long long got = load_acquire_sys(mine + 2 * j + par);
+        while ((got >> 1) < token) {
+            if (global_ns() - t0 > a.timeout_ns) {
+                atomicExch(&a.st->err, 2);
+                *ok = 0;
+                return 0;
+            }
+            __nanosleep(64);
+            got = load_acquire_sys(mine + 2 * j + par);
+        }
+        any |= (int)(got & 1ull);
+    }
+    return any;
+}
+
+// Grid barrier at the end of sweep s; false if a wait ran out.
+__device__ bool sweep_barrier(const FixArgs& a, int s) {
+    __shared__ int ok_s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        __threadfence();
+        const unsigned prev = atomicAdd(&a.st->bar_count, 1u);
+        if (prev == a.nblocks - 1) {
+            __threadfence();
+            int c = *(volatile int*)&a.st->changed[s & 1];
+            if (a.world > 1) c = exchange_changed(a, s, c, &ok);
+            a.st->next_row[(s + 1) & 1] = 0;
+            a.st->changed[(s + 1) & 1] = 0;
+            a.st->sweeps = s + 1;
+            a.st->last_changed = c;
+            a.st->go = (ok && c && s + 1 < a.max_sweeps) ? 1 : 0;
+            a.st->bar_count = 0;
+            __threadfence();
+            atomicExch(&a.st->bar_gen, (unsigned)(s + 1));
+        } else {
+            const unsigned long long t0 = global_ns();
+            while (*(volatile unsigned*)&a.st->bar_gen < (unsigned)(s + 1)) {
+                if (global_ns() - t0 > a.timeout_ns) {
+                    atomicExch(&a.st->err, 1);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(128);
+            }
+        }
+        __threadfence();
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0;
+}
+
+__global__ void __launch_bounds__(32 * kFixWarps, 4) k_closure_fix(const FixArgs a) {
+    extern __shared__ __align__(16) uint32_t smem_fix[];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    uint32_t* row = smem_fix + (int64_t)wib * (2 * a.wpad + 4 + kFixQueue);
+    uint32_t* spill = row + a.wpad + 4;
+    uint32_t* q = spill + a.wpad;
+    // the sentinel successor (bit 0 of word wpad) reads as already set
+    if (lane == 0) row[a.wpad] = 0xffffffffu;
+    for (int64_t w = lane; w < a.wpad; w += 32) spill[w] = 0u;
+    __syncwarp();
+    for (int s = 0; s < a.max_sweeps; ++s) {
+        const bool grew = close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, a.lazy && s == 0, row, spill, q,
+                                     lane);
+        if (lane == 0 && grew) *(volatile int*)&a.st->changed[s & 1] = 1;
+        if (!sweep_barrier(a, s)) return;
+        if (!*(volatile int*)&a.st->go) return;
+    }
+}
+
+// Successor table: entry y = 8 int32.  deg <= 8: the successors, unused
+// slots the sentinel; deg > 8: the first 7, slot 7 = -2 (the rest from the
+// CSR at rowptr[y] + 7).  Nodes without a CSR row have none.
+__global__ void k_build_succ(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ colidx, int64_t e_rows,
+                             int64_t nodes, int32_t sentinel, int4* __restrict__ out) {
+    for (int64_t y = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; y < nodes; y += (int64_t)gridDim.x * blockDim.x) {
+        int32_t s[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[j] = sentinel;
+        if (y < e_rows) {
+            const int64_t b = rowptr[y], d = rowptr[y + 1] - b;
+            const int inl = d > 8 ? 7 : (int)d;
+            for (int j = 0; j < inl; ++j) s[j] = colidx[b + j];
+            if (d > 8) s[7] = -2;
+        }
+        out[2 * y] = make_int4(s[0], s[1], s[2], s[3]);
+        out[2 * y + 1] = make_int4(s[4], s[5], s[6], s[7]);
+    }
+}
+
+size_t fix_smem_per_warp(int64_t words) {
+    const int64_t wpad = (words + 3) & ~int64_t(3);
+    return (size_t)(2 * wpad + 4 + kFixQueue) * 4;
+}
+
+}  // namespace
+
+tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweeps, int* sweeps_out,
+                                  bool* changed_out, bool* handled) {
+    *handled = false;
+    constexpr size_t kSmemCap = 200 * 1024;
+    const int64_t words = R->bits_words, rows = R->bits_rows;
+    const int64_t wpad = (words + 3) & ~int64_t(3);
+    // one table entry per bit position of a row (padding bits included)
+    const int64_t nodes = words * 32;
+    if (fix_smem_per_warp(words) > kSmemCap || wpad * 32 >= INT32_MAX || E->nnz >= INT32_MAX) return TL_OK;
+    if (getenv("TL_CLOSURE_PER_SWEEP")) return TL_OK;
+    if (c->world > 1) {
+        TL_TRY(comm_peer_setup(c));
+        if (c->peer_state != 1) return TL_OK;
+    }
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
+    if (!coop) return TL_OK;
+    *handled = true;
+
+    // successor table, rebuilt when the CSR or the row width changed
+    const int32_t sentinel = (int32_t)(wpad * 32);
+    if (E->succ_stamp != E->csr_stamp || E->succ_nodes != nodes || E->succ_sentinel != sentinel || !E->succ) {
+        if (nodes * 2 > E->succ_cap) {
+            TL_CK(c, cudaStreamSynchronize(c->stream));
+            cudaFree(E->succ);
+            E->succ = nullptr;
+            E->succ_cap = 0;
+            TL_CK(c, cudaMalloc(&E->succ, (size_t)std::max<int64_t>(nodes * 2, 2) * sizeof(int4)));
+            E->succ_cap = std::max<int64_t>(nodes * 2, 2);
+        }
+        LaunchScope L(c, "closure_successor_table", (double)nodes * 32.0 + (double)E->nnz * 4.0);
+        const int64_t blocks = std::min<int64_t>((nodes + 255) / 256, (int64_t)c->sm_count * 8);
+        k_build_succ<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, c->stream>>>(E->rowptr, E->colidx, E->csr_rows,
+                                                                                   nodes, sentinel, E->succ);
+        TL_TRY(L.done());
+        E->succ_stamp = E->csr_stamp;
+        E->succ_nodes = nodes;
+        E->succ_sentinel = sentinel;
+    }
+
+    // fixpoint-long state: pending word per row (0: expand everything)
+    if ((size_t)rows * 4 > c->aux_cap) {
+        TL_CK(c, cudaStreamSynchronize(c->stream));
+        cudaFree(c->aux);
+        c->aux = nullptr;
+        c->aux_cap = 0;
+        TL_CK(c, cudaMalloc(&c->aux, std::max<size_t>((size_t)rows * 4, 4096)));
+        c->aux_cap = std::max<size_t>((size_t)rows * 4, 4096);
+    }
+    static_assert(sizeof(FixState) <= 128, "control block and its pinned mirror");
+    if (!c->fix_state) TL_CK(c, cudaMalloc(&c->fix_state, 256));
+    if (rows > 0) TL_CK(c, cudaMemsetAsync(c->aux, 0, (size_t)rows * 4, c->stream));
+    TL_CK(c, cudaMemsetAsync(c->fix_state, 0, sizeof(FixState), c->stream));
+
+    // shape: the warps-per-block split that keeps the most warps resident
+    TL_CK(c, cudaFuncSetAttribute(k_closure_fix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
+    const size_t per_warp = fix_smem_per_warp(words);
+    int wpb = 1, per_sm = 0;
+    for (int w = 1; w <= kFixWarps; ++w) {
+        if (per_warp * w > kSmemCap) break;
+        int b = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_closure_fix, 32 * w, per_warp * w);
+        if (b * w > per_sm * wpb) {
+            wpb = w;
+            per_sm = b;
+        }
+    }
+    if (per_sm < 1) return fail(c, TL_ERR_UNSUPPORTED, "closure fixpoint: no resident block fits");
+    int64_t grid = std::min<int64_t>((int64_t)c->sm_count * per_sm, std::max<int64_t>((rows + wpb - 1) / wpb, 1));
+
+    FixArgs a{};
+    a.R = R->bits;
+    a.rows = rows;
+    a.words = words;
+    a.wpad = wpad;
+    a.succ = E->succ;
+    a.rowptr = E->rowptr;
+    a.colidx = E->colidx;
+    a.e_rows = E->csr_rows;
+    a.pending = (int32_t*)c->aux;
+    a.st = (FixState*)c->fix_state;
+    // rows that step(E) left unwritten start from E's successor lists
+    a.lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp ? 1 : 0;
+    // local row r is global row r * world + rank of a row-sharded relation
+    a.row_stride = 1;
+    a.row_offset = 0;
+    if (R->shard == TL_SHARD_ROWS && c->world > 1) {
+        a.row_stride = c->world;
+        a.row_offset = c->rank;
+    }
+    a.max_sweeps = max_sweeps;
+    a.nblocks = (unsigned)grid;
+    a.world = c->world;
+    a.rank = c->rank;
+    for (int j = 0; j < kMaxPeers; ++j) a.slots[j] = c->peer_slots[j];
+    a.token0 = c->peer_tokens;
+    a.timeout_ns = (unsigned long long)std::max(c->opts.comm_timeout_ms, 1000) * 1000000ull;
+
+    const double sweep_bytes = (double)rows * words * 8.0 + (double)nodes * 32.0;
+    {
+        LaunchScope L(c, "closure_fixpoint", sweep_bytes);
+        void* args[] = {&a};
+        TL_CK(c, cudaLaunchCooperativeKernel((const void*)k_closure_fix, dim3((unsigned)grid), dim3(32 * wpb), args,
+                                             per_warp * wpb, c->stream));
+        TL_TRY(L.done());
+    }
+    FixState h{};
+    TL_CK(c, cudaMemcpyAsync(c->h_flags + 32, c->fix_state, sizeof(FixState), cudaMemcpyDeviceToHost, c->stream));
+    TL_CK(c, cudaStreamSynchronize(c->stream));
+    memcpy(&h, c->h_flags + 32, sizeof(FixState));
+    // algorithmic bytes of the launch: every sweep reads and writes the rows
+    if (c->prof && !c->pending.empty() && c->pending.back().name == "closure_fixpoint")
+        c->pending.back().bytes = sweep_bytes * std::max(h.sweeps, 1);
+    if (c->world > 1) c->peer_tokens += (unsigned long long)h.sweeps;
+    if (h.err) {
+        if (c->world > 1) c->peer_state = -1;   // ranks may disagree on the token count now
+        return fail(c, h.err == 2 ? TL_ERR_COMM : TL_ERR_CUDA,
+                    "closure fixpoint: %s wait ran out after %d sweeps", h.err == 2 ? "peer" : "grid barrier",
+                    h.sweeps);
+    }
+    R->lazy_src = nullptr;   // every row is written now
+    *sweeps_out = h.sweeps;
+    *changed_out = h.last_changed != 0;
+    return TL_OK;
+}
+
+}  // namespace tl

@@ -16,6 +16,9 @@
 // relu(a b) = a+ b+ + a- b- (K doubles): a prep kernel writes [A+|A-] and
 // [B+;B-] as K-major copies.
 #include <cuda.h>
+#include <stdint.h>
+
+#include <algorithm>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -114,6 +117,206 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const __grid_constant__ GemmP
             if (p.beta) v += *cp;
             *cp = v;
             if (p.epi_relu) p.D[gm * p.sdm + gn * p.sdn] = fmaxf(v, 0.f);
+        }
+    }
+}
+
+// ============================================================================
+// Skinny shapes (no per-term nonlinearity), fp32 FFMA, bandwidth-bound
+// ============================================================================
+// C[M, N <= 16] = scale * A[M, K] B[K, N] with a long K (the output layer and
+// its weight gradient): a block owns 32 rows of C and one K range (blockIdx.y;
+// partial sums are added with atomics when K is split).  B's K range streams
+// through shared memory in 256-row chunks, padded to 16 columns.
+//  A_MCONT (A's rows contiguous, e.g. a transposed activation): lane = row,
+//    the 8 warps take interleaved k, each thread keeps 16 sums, and the warps'
+//    sums are added in shared memory.
+//  otherwise (A's k contiguous): warp w owns rows 4w..4w+3, lanes take 4
+//    consecutive k (one 128-bit load when aligned), and the 64 sums are
+//    reduced across the warp at the end.
+constexpr int SK_BM = 32, SK_KC = 256;
+
+template <bool A_MCONT>
+__global__ void __launch_bounds__(256) k_gemm_skinny_n(const __grid_constant__ GemmPlan p, int64_t k_per_split,
+                                                       int vec) {
+    // A_MCONT reads one k row of B for all lanes (broadcast): k-major rows;
+    // otherwise lanes read consecutive k of one column: n-major rows
+    __shared__ __align__(16) float Bs[A_MCONT ? SK_KC : 16][A_MCONT ? 16 : SK_KC];
+    __shared__ float red[A_MCONT ? 8 : 1][SK_BM][17];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t m0 = (int64_t)blockIdx.x * SK_BM;
+    const int64_t kb = (int64_t)blockIdx.y * k_per_split;
+    const int64_t ke = kb + k_per_split < p.K ? kb + k_per_split : p.K;
+    constexpr int NACC = A_MCONT ? 16 : 64;
+    float acc[NACC];
+#pragma unroll
+    for (int i = 0; i < NACC; ++i) acc[i] = 0.f;
+    for (int64_t kc = kb; kc < ke; kc += SK_KC) {
+        const int kn = (int)(ke - kc < SK_KC ? ke - kc : SK_KC);
+        __syncthreads();
+        for (int i = threadIdx.x; i < SK_KC * 16; i += 256) {
+            const int kk = i >> 4, nn = i & 15;
+            const float v = (kk < kn && nn < p.N) ? p.B[(kc + kk) * p.sbk + nn * p.sbn] : 0.f;
+            if (A_MCONT) Bs[kk][nn] = v;
+            else Bs[nn][kk] = v;
+        }
+        __syncthreads();
+        if (A_MCONT) {
+            const int64_t m = m0 + lane;
+            const float* ap = p.A + m * p.sam + kc * p.sak;
+            // four k per warp and round, their loads issued together
+            for (int k0 = w; k0 < kn; k0 += 32) {
+                float a[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int kk = k0 + 8 * u;
+                    a[u] = (m < p.M && kk < kn) ? ap[kk * p.sak] : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int kk = k0 + 8 * u;
+                    if (kk >= kn) break;
+                    const float4* b4 = reinterpret_cast<const float4*>(Bs[kk]);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 b = b4[q];
+                        acc[4 * q + 0] = fmaf(a[u], b.x, acc[4 * q + 0]);
+                        acc[4 * q + 1] = fmaf(a[u], b.y, acc[4 * q + 1]);
+                        acc[4 * q + 2] = fmaf(a[u], b.z, acc[4 * q + 2]);
+                        acc[4 * q + 3] = fmaf(a[u], b.w, acc[4 * q + 3]);
+                    }
+                }
+            }
+        } else {
+            // the chunk's two 128-wide k rounds: all eight row loads first
+            float a2[2][4][4];
+#pragma unroll
+            for (int it = 0; it < 2; ++it)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int kk = lane * 4 + it * 128;
+                    const int64_t m = m0 + w * 4 + r;
+                    const float* ap = p.A + m * p.sam + (kc + kk) * p.sak;
+                    if (m < p.M && vec && kk + 3 < kn) {
+                        const float4 t = *reinterpret_cast<const float4*>(ap);
+                        a2[it][r][0] = t.x; a2[it][r][1] = t.y; a2[it][r][2] = t.z; a2[it][r][3] = t.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) a2[it][r][i] = (m < p.M && kk + i < kn) ? ap[i * p.sak] : 0.f;
+                    }
+                }
+#pragma unroll
+            for (int it = 0; it < 2; ++it) {
+                const int kk = lane * 4 + it * 128;
+                if (kk >= kn) break;
+                float (&a)[4][4] = a2[it];
+                // column n of B at this lane's 4 k: one conflict-free 128-bit load
+#pragma unroll
+                for (int nn = 0; nn < 16; ++nn) {
+                    const float4 b = *reinterpret_cast<const float4*>(&Bs[nn][kk]);
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        float t = acc[r * 16 + nn];
+                        t = fmaf(a[r][0], b.x, t);
+                        t = fmaf(a[r][1], b.y, t);
+                        t = fmaf(a[r][2], b.z, t);
+                        acc[r * 16 + nn] = fmaf(a[r][3], b.w, t);
+                    }
+                }
+            }
+        }
+    }
+    const bool atomic = gridDim.y > 1;
+    auto put = [&](int64_t m, int n, float v) {
+        if (m >= p.M || n >= p.N) return;
+        float* cp = p.C + m * p.scm + n * p.scn;
+        v *= p.scale;
+        if (atomic) atomicAdd(cp, v);
+        else *cp = p.beta ? *cp + v : v;
+    };
+    if (A_MCONT) {
+#pragma unroll
+        for (int n = 0; n < 16; ++n) red[w][lane][n] = acc[n];
+        __syncthreads();
+        for (int i = threadIdx.x; i < SK_BM * 16; i += 256) {
+            const int r = i >> 4, n = i & 15;
+            float v = 0.f;
+#pragma unroll
+            for (int ww = 0; ww < 8; ++ww) v += red[ww][r][n];
+            put(m0 + r, n, v);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+        // every lane holds the 64 sums; lane l writes sums 2l and 2l + 1
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+            if ((i >> 1) == lane) put(m0 + w * 4 + (i >> 4), i & 15, acc[i]);
+    }
+}
+
+// C[M, N] = scale * A[M, K <= 16] B[K, N] (an outer-product-like GEMM whose
+// cost is writing C): block x stages B's columns n0 .. n0 + TK_COLS and its
+// rows of A (at most TK_ROWS) in shared memory, thread t keeps
+// B[:, n0 + 4t .. +3] in registers (K padded to 16 with zeros), and each row
+// costs the thread four broadcast shared loads, 64 FMAs and one 128-bit store.
+constexpr int TK_ROWS = 16, TK_THREADS = 128, TK_COLS = 4 * TK_THREADS;
+
+__global__ void __launch_bounds__(TK_THREADS) k_gemm_thin_k(const __grid_constant__ GemmPlan p, int64_t rows_per_block,
+                                                     int vec) {
+    __shared__ __align__(16) float As[TK_ROWS][16];
+    __shared__ float Bsh[16][TK_COLS + 4];   // the block's columns of B, k-major
+    const int64_t n0 = (int64_t)blockIdx.x * TK_COLS;
+    const int64_t n = n0 + threadIdx.x * 4;
+    // B's block slice in one pass, walking whichever of k / n is contiguous
+    for (int i = threadIdx.x; i < 16 * TK_COLS; i += blockDim.x) {
+        const int k = p.sbk == 1 ? (i % 16) : (i / TK_COLS);
+        const int j = p.sbk == 1 ? (i / 16) : (i % TK_COLS);
+        Bsh[k][j] = (k < p.K && n0 + j < p.N) ? p.B[k * p.sbk + (n0 + j) * p.sbn] : 0.f;
+    }
+    const int64_t mb = (int64_t)blockIdx.y * rows_per_block;
+    const int64_t me = mb + rows_per_block < p.M ? mb + rows_per_block : p.M;
+    for (int i = threadIdx.x; i < TK_ROWS * 16; i += blockDim.x) {
+        const int r = i >> 4, k = i & 15;
+        As[r][k] = (mb + r < me && k < p.K) ? p.A[(mb + r) * p.sam + k * p.sak] : 0.f;
+    }
+    __syncthreads();
+    float b[16][4];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[k][j] = Bsh[k][threadIdx.x * 4 + j];
+    if (n >= p.N) return;
+    for (int64_t m = mb; m < me; ++m) {
+        const float4* a4 = reinterpret_cast<const float4*>(As[m - mb]);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 a = a4[q];
+            const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[j] = fmaf(av[i], b[4 * q + i][j], acc[j]);
+        }
+        float* cp = p.C + m * p.scm + n * p.scn;
+        if (vec && n + 3 < p.N) {
+            float4 v = make_float4(acc[0] * p.scale, acc[1] * p.scale, acc[2] * p.scale, acc[3] * p.scale);
+            if (p.beta) {
+                const float4 o = *reinterpret_cast<const float4*>(cp);
+                v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+            }
+            *reinterpret_cast<float4*>(cp) = v;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (n + j < p.N) {
+                    const float v = acc[j] * p.scale;
+                    float* q = cp + j * p.scn;
+                    *q = p.beta ? *q + v : v;
+                }
         }
     }
 }
@@ -426,25 +629,35 @@ __device__ __forceinline__ float seg_op(int op, float x) {
     }
 }
 
-// K-major copy dst[r * ld + s * K + k], k fastest (coalesced for K-contiguous sources).
-__global__ void k_prep_kmajor(const float* __restrict__ S, int64_t s_r, int64_t s_k, int64_t R, int64_t K, int nseg,
-                              unsigned ops, float sgn, float* __restrict__ D, int64_t ld) {
-    const int64_t total = R * K;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / K, k = i % K;
-        const float x = S[r * s_r + k * s_k] * sgn;
-        for (int s = 0; s < nseg; ++s) D[r * ld + s * K + k] = seg_op((ops >> (4 * s)) & 15, x);
-    }
-}
-
-// MN-major copy dst[(s * K + k) * ld + r], r fastest (coalesced for R-contiguous sources).
-__global__ void k_prep_mnmajor(const float* __restrict__ S, int64_t s_r, int64_t s_k, int64_t R, int64_t K, int nseg,
-                               unsigned ops, float sgn, float* __restrict__ D, int64_t ld) {
-    const int64_t total = R * K;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t k = i / R, r = i % R;
-        const float x = S[r * s_r + k * s_k] * sgn;
-        for (int s = 0; s < nseg; ++s) D[(s * K + k) * ld + r] = seg_op((ops >> (4 * s)) & 15, x);
+// Row-wise segment copy: for each source row i (stride src_rs, len elements,
+// contiguous) and segment s, dst[i * dst_rs + s * dst_ss + j] = op_s(x[j]).
+// Serves both orientations: K-major copies of K-contiguous sources (rows = R)
+// and MN-major copies of MN-contiguous sources (rows = K).  A 2-D grid (row
+// chunks x rows) needs no index division; 128-bit loads and stores when every
+// stride and base is 16-byte aligned.
+__global__ void __launch_bounds__(256) k_prep_rows(const float* __restrict__ S, int64_t src_rs, int64_t rows,
+                                                   int64_t len, int nseg, unsigned ops, float sgn,
+                                                   float* __restrict__ D, int64_t dst_rs, int64_t dst_ss, int vec) {
+    for (int64_t i = blockIdx.y; i < rows; i += gridDim.y) {
+        const float* src = S + i * src_rs;
+        float* dst = D + i * dst_rs;
+        if (vec) {
+            for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; j < len;
+                 j += (int64_t)gridDim.x * blockDim.x * 4) {
+                float4 x = *reinterpret_cast<const float4*>(src + j);
+                x.x *= sgn; x.y *= sgn; x.z *= sgn; x.w *= sgn;
+                for (int s = 0; s < nseg; ++s) {
+                    const int op = (ops >> (4 * s)) & 15;
+                    *reinterpret_cast<float4*>(dst + s * dst_ss + j) =
+                        make_float4(seg_op(op, x.x), seg_op(op, x.y), seg_op(op, x.z), seg_op(op, x.w));
+                }
+            }
+        } else {
+            for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < len; j += (int64_t)gridDim.x * blockDim.x) {
+                const float x = src[j] * sgn;
+                for (int s = 0; s < nseg; ++s) dst[s * dst_ss + j] = seg_op((ops >> (4 * s)) & 15, x);
+            }
+        }
     }
 }
 
@@ -544,7 +757,56 @@ bool tcgen05_available(tl_ctx* c) {
     return major == 10 && minor == 0 && get_encode() != nullptr && !env_flag("TL_GEMM_SIMT");
 }
 
+static tl_status launch_simt(tl_ctx* c, const GemmPlan& p);
+
+// Skinny shapes without a per-term nonlinearity; false if the shape is not one.
+static bool launch_skinny(tl_ctx* c, const GemmPlan& p, tl_status* st) {
+    if (p.relu_term || p.epi_relu || p.K <= 0) return false;
+    if (p.N <= 16 && p.K >= 128 && (p.sam == 1 || p.sak == 1)) {
+        const bool mcont = p.sam == 1 && p.sak != 1;
+        const int64_t mblocks = (p.M + SK_BM - 1) / SK_BM;
+        // K split so the grid covers about two blocks per SM, ranges of whole chunks
+        int64_t splits = std::max<int64_t>(1, ((int64_t)c->sm_count * 2 + mblocks - 1) / mblocks);
+        const int64_t chunks = (p.K + SK_KC - 1) / SK_KC;
+        if (splits > chunks) splits = chunks;
+        const int64_t per = ((chunks + splits - 1) / splits) * SK_KC;
+        splits = (p.K + per - 1) / per;
+        if (splits > 1 && !p.beta) {
+            GemmPlan z = p;   // zero C (a K = 0 pass), then add the partial sums
+            z.K = 0;
+            *st = launch_simt(c, z);
+            if (*st != TL_OK) return true;
+        }
+        const int vec = !mcont && (p.sam & 3) == 0 && ((uintptr_t)p.A & 15) == 0 ? 1 : 0;
+        LaunchScope L(c, "gemm_skinny_fp32", (double)(p.M * p.K + p.K * p.N + p.M * p.N * (1 + p.beta)) * 4.0,
+                      2.0 * p.M * p.N * p.K);
+        dim3 g((unsigned)mblocks, (unsigned)splits);
+        if (mcont) k_gemm_skinny_n<true><<<g, 256, 0, c->stream>>>(p, per, vec);
+        else k_gemm_skinny_n<false><<<g, 256, 0, c->stream>>>(p, per, vec);
+        *st = L.done();
+        return true;
+    }
+    if (p.K <= 16 && p.N >= 64 && p.M >= 64) {
+        const int vec = p.scn == 1 && (p.scm & 3) == 0 && ((uintptr_t)p.C & 15) == 0 ? 1 : 0;
+        const int64_t nblocks = (p.N + TK_COLS - 1) / TK_COLS;
+        // about four blocks per SM over the rows, at most TK_ROWS rows a block
+        int64_t rows = std::max<int64_t>(1, (p.M * nblocks + (int64_t)c->sm_count * 4 - 1) / ((int64_t)c->sm_count * 4));
+        if (rows > TK_ROWS) rows = TK_ROWS;
+        const int64_t mblocks = (p.M + rows - 1) / rows;
+        LaunchScope L(c, "gemm_thin_k_fp32", (double)(p.M * p.K + p.K * p.N + p.M * p.N * (1 + p.beta)) * 4.0,
+                      2.0 * p.M * p.N * p.K);
+        k_gemm_thin_k<<<dim3((unsigned)nblocks, (unsigned)mblocks), TK_THREADS, 0, c->stream>>>(p, rows, vec);
+        *st = L.done();
+        return true;
+    }
+    return false;
+}
+
 static tl_status launch_simt(tl_ctx* c, const GemmPlan& p) {
+    if (p.K > 0 && !env_flag("TL_GEMM_NO_SKINNY")) {
+        tl_status st = TL_OK;
+        if (launch_skinny(c, p, &st)) return st;
+    }
     const float sgn = p.scale < 0.f ? -1.f : 1.f;
     const float mag = fabsf(p.scale);
     const int bn = p.N <= 16 ? 16 : 64;
@@ -626,14 +888,17 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
         wp += (((size_t)(q->mn ? Ke : q->R) * q->ld * 4) + 255) & ~size_t(255);
         const float* src = q == &pa ? p.A : p.B;
         LaunchScope L(c, q->name, (double)q->R * p.K * 4.0 * (1 + nseg));
-        int64_t blocks = (q->R * p.K + 255) / 256;
-        if (blocks > (int64_t)c->sm_count * 32) blocks = (int64_t)c->sm_count * 32;
-        if (q->mn) {
-            k_prep_mnmajor<<<(unsigned)blocks, 256, 0, c->stream>>>(src, q->s_r, q->s_k, q->R, p.K, nseg, q->ops,
-                                                                   q->sgn, q->dst, q->ld);
-        } else if (q->s_k == 1) {
-            k_prep_kmajor<<<(unsigned)blocks, 256, 0, c->stream>>>(src, q->s_r, q->s_k, q->R, p.K, nseg, q->ops,
-                                                                  q->sgn, q->dst, q->ld);
+        if (q->mn || q->s_k == 1) {
+            // rows of the contiguous dim: R rows of K (K-major) or K rows of R (MN-major)
+            const int64_t rows = q->mn ? p.K : q->R, len = q->mn ? q->R : p.K;
+            const int64_t src_rs = q->mn ? q->s_k : q->s_r;
+            const int64_t dst_ss = q->mn ? p.K * q->ld : p.K;
+            const bool vec = (len & 3) == 0 && (src_rs & 3) == 0 && (q->ld & 3) == 0 && (dst_ss & 3) == 0 &&
+                             ((uintptr_t)src & 15) == 0 && ((uintptr_t)q->dst & 15) == 0;
+            const int64_t per_row = vec ? (len + 3) / 4 : len;
+            dim3 g((unsigned)std::min<int64_t>((per_row + 255) / 256, 64), (unsigned)std::min<int64_t>(rows, 65535));
+            k_prep_rows<<<g, 256, 0, c->stream>>>(src, src_rs, rows, len, nseg, q->ops, q->sgn, q->dst, q->ld, dst_ss,
+                                                  vec ? 1 : 0);
         } else {
             dim3 g((unsigned)((q->R + 31) / 32), (unsigned)((p.K + 31) / 32));
             k_prep_transpose<<<g, dim3(32, 8), 0, c->stream>>>(src, q->s_r, q->s_k, q->R, p.K, nseg, q->ops, q->sgn,

@@ -492,7 +492,9 @@ tl_status launch_dense_to_csr(tl_ctx* c, Tensor* t) {
     t->nnz = nnz;
     t->csr_rows = rows;
     t->csr_valid = true;
+    t->csr_stamp = next_csr_stamp();
     t->csr_nonneg = hf[0] == 0;
+    t->csr_pos = t->csr_nonneg;   // only nonzero values are stored
     t->csr_ones = hf[1] == 0;
     return TL_OK;
 }

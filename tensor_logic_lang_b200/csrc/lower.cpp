@@ -12,6 +12,7 @@
 //   genSave / genLoad          src/codegen/llvm.zig:565-633 (paths without quotes)
 #include <math.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -516,6 +517,16 @@ tl_status try_step_bits(tl_ctx* c, const tl_equation* eq, const Analysis& a, Ten
     if (E->dims[0] != lhs->dims[0] || E->dims[1] != lhs->dims[1]) return TL_OK;
     // a sharded source needs a sharded destination; a replicated one feeds either
     if (c->world > 1 && E->shard == TL_SHARD_ROWS && lhs->shard != TL_SHARD_ROWS) return TL_OK;
+    if (c->lazy_eq == eq && E->csr_pos && E->csr_rows == E->dims[0]) {
+        // the closure fixpoint that runs next reads these rows: it builds
+        // them from E's successor lists instead of reading them back
+        TL_TRY(alloc_bits_public(c, lhs));
+        mark_written_bits(lhs);
+        lhs->lazy_src = E;
+        lhs->lazy_stamp = E->csr_stamp;
+        *done = true;
+        return TL_OK;
+    }
     TL_TRY(launch_csr_to_bits(c, E, lhs));
     mark_written_bits(lhs);
     *done = true;
@@ -812,7 +823,8 @@ static ClosureForm match_closure(tl_ctx* c, const tl_equation* eq, Tensor** Rout
         return NOT_CLOSURE;
     if (!R->boolean) return NOT_CLOSURE;
     // step(r * e) == (r > 0) && (e > 0) needs e >= 0 (r is 0/1)
-    if (!(E->csr_valid ? E->csr_nonneg : E->boolean)) return NOT_CLOSURE;
+    // the bit-row sweeps treat every stored entry as an edge: values must be > 0
+    if (!(E->csr_valid ? E->csr_pos : E->boolean)) return NOT_CLOSURE;
     // the sweeps read successor lists of every row: the relation is replicated
     if (E->csr_valid && E->csr_rows != E->dims[0]) return NOT_CLOSURE;
     if (form == CLOSURE_LEFT && R->shard == TL_SHARD_ROWS && c->world > 1) return NOT_CLOSURE;
@@ -878,7 +890,20 @@ static tl_status run_fixpoint(tl_ctx* c, const tl_equation* eqs, int n, int32_t*
         if (E->shard == TL_SHARD_ROWS && c->world > 1) form = NOT_CLOSURE;
         else {
             TL_TRY(launch_dense_to_csr(c, E));
-            if (!E->csr_nonneg) form = NOT_CLOSURE;
+            if (!E->csr_pos) form = NOT_CLOSURE;
+        }
+    }
+    if (form == CLOSURE_RIGHT) {
+        // rows left unwritten by step(E) are built by the one-launch fixpoint
+        if (!(R->bits_valid && R->lazy_src == E)) TL_TRY(ensure_bits(c, R));
+        bool handled = false;
+        TL_TRY(launch_closure_fixpoint(c, R, E, max_sweeps, &sweeps, &changed, &handled));
+        if (handled) {
+            mark_written_bits(R);
+            c->last_sweeps = sweeps;
+            if (sweeps_out) *sweeps_out = sweeps;
+            if (changed) fail(c, TL_OK, "fixpoint stopped at the %d-sweep cap", sweeps);
+            return TL_OK;
         }
     }
     if (form != NOT_CLOSURE) TL_TRY(ensure_bits(c, R));
@@ -972,6 +997,47 @@ static tl_status run_sparse_load(tl_ctx* c, const tl_statement* st) {
     return tl_sparse_upload(static_cast<tl_tensor*>(t), st->size, st->coo_rows, st->coo_cols, st->host_data);
 }
 
+// True if statement st names tensor t (a backward pass counts as naming every tensor).
+static bool names_tensor(const tl_statement* st, const char* t) {
+    switch (st->kind) {
+    case TL_STMT_EQUATION:
+        if (!strcmp(st->eq.lhs.tensor, t)) return true;
+        for (int k = 0; k < st->eq.n_refs && k < TL_MAX_REFS; ++k)
+            if (!strcmp(st->eq.refs[k].tensor, t)) return true;
+        return false;
+    case TL_STMT_SPARSE: return !strcmp(st->sparse.tensor, t);
+    case TL_STMT_SPARSE_LOAD: case TL_STMT_LOAD: case TL_STMT_SAVE: return !strcmp(st->name, t);
+    case TL_STMT_BACKWARD: return true;
+    default: return false;
+    }
+}
+
+// The equation R[..] = step(E[..]) whose bit rows may stay unwritten until the
+// fixpoint: the program's only recursive equation reads R and E, and no
+// statement after it touches R or E before the fixpoint runs.
+static const tl_equation* lazy_step_equation(const tl_statement* s, int n) {
+    const tl_equation* rec = nullptr;
+    int n_rec = 0;
+    for (int i = 0; i < n; ++i)
+        if (s[i].kind == TL_STMT_EQUATION && is_recursive(&s[i].eq)) { ++n_rec; rec = &s[i].eq; }
+    if (n_rec != 1 || rec->accum != TL_ACC_MAX || rec->n_refs != 2 || getenv("TL_NO_LAZY_STEP")) return nullptr;
+    const char* R = rec->lhs.tensor;
+    const char* E = !strcmp(rec->refs[0].tensor, R) ? rec->refs[1].tensor : rec->refs[0].tensor;
+    if (!strcmp(E, R)) return nullptr;
+    for (int i = n - 1; i >= 0; --i) {
+        const tl_statement* st = &s[i];
+        if (st->kind == TL_STMT_EQUATION && &st->eq == rec) continue;
+        if (!names_tensor(st, R) && !names_tensor(st, E)) continue;
+        const tl_equation* eq = &st->eq;
+        if (st->kind == TL_STMT_EQUATION && !strcmp(eq->lhs.tensor, R) && eq->n_refs == 1 &&
+            !strcmp(eq->refs[0].tensor, E) && eq->n_code == 2 && eq->code[1].op == TL_OP_NL &&
+            eq->code[1].arg == TL_NL_STEP && !is_recursive(eq))
+            return eq;
+        return nullptr;
+    }
+    return nullptr;
+}
+
 extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n) {
     if (!c || (n > 0 && !s)) return TL_ERR_INVALID;
     TL_CK(c, cudaSetDevice(c->device));
@@ -1006,6 +1072,11 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
             }
         }
     }
+    struct LazyReset {
+        tl_ctx* c;
+        ~LazyReset() { c->lazy_eq = nullptr; }
+    } lazy_reset{c};
+    c->lazy_eq = lazy_step_equation(s, n);
     for (int i = 0; i < n; ++i) {
         const tl_statement* st = &s[i];
         switch (st->kind) {
@@ -1031,6 +1102,7 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
         default: return fail(c, TL_ERR_INVALID, "unknown statement kind %d", st->kind);
         }
     }
+    c->lazy_eq = nullptr;
     c->last_sweeps = 0;
     if (!rec.empty()) TL_TRY(run_fixpoint(c, rec.data(), (int)rec.size(), nullptr));
     for (int i = 0; i < n; ++i) {

@@ -14,6 +14,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstring>
 
@@ -99,6 +100,11 @@ Tensor* find_defined(tl_ctx* c, const std::string& name) {
 // ============================================================================
 // tensor storages
 // ============================================================================
+uint64_t next_csr_stamp() {
+    static std::atomic<uint64_t> stamp{0};
+    return ++stamp;
+}
+
 static void free_storage(Tensor* t) {
     cudaFree(t->dense); t->dense = nullptr; t->dense_elems = 0;
     cudaFree(t->bits); t->bits = nullptr; t->bits_words = t->bits_rows = 0;
@@ -106,6 +112,8 @@ static void free_storage(Tensor* t) {
     t->rowptr = nullptr; t->colidx = nullptr; t->vals = nullptr; t->csr_cap = 0;
     cudaFree(t->colptr); cudaFree(t->rowidx);
     t->colptr = nullptr; t->rowidx = nullptr; t->csc_cap = 0;
+    cudaFree(t->succ); t->succ = nullptr; t->succ_cap = 0; t->succ_stamp = 0;
+    t->lazy_src = nullptr;
     t->dense_valid = t->bits_valid = t->csr_valid = t->csc_valid = false;
 }
 
@@ -198,6 +206,7 @@ tl_status ensure_dense(tl_ctx* c, Tensor* t) {
     if (t->zero) {
         TL_CK(c, cudaMemsetAsync(t->dense, 0, dense_local_elems(c, t) * sizeof(float), c->stream));
     } else if (t->bits_valid) {
+        TL_TRY(ensure_bits(c, t));   // writes lazy bit rows first
         TL_TRY(launch_bits_to_dense(c, t));
     } else if (t->csr_valid) {
         TL_TRY(launch_csr_to_dense(c, t));
@@ -210,6 +219,13 @@ tl_status ensure_dense(tl_ctx* c, Tensor* t) {
 
 tl_status ensure_bits(tl_ctx* c, Tensor* t) {
     TL_TRY(alloc_bits(c, t));
+    if (t->bits_valid && t->lazy_src) {
+        Tensor* src = t->lazy_src;
+        t->lazy_src = nullptr;
+        if (!src->csr_valid || src->csr_stamp != t->lazy_stamp)
+            return fail(c, TL_ERR_INVALID, "%s: the relation its rows were defined from changed", t->name.c_str());
+        return launch_csr_to_bits(c, src, t);
+    }
     if (t->bits_valid) return TL_OK;
     if (t->zero) {
         TL_CK(c, cudaMemsetAsync(t->bits, 0, t->bits_rows * t->bits_words * 4, c->stream));
@@ -220,6 +236,7 @@ tl_status ensure_bits(tl_ctx* c, Tensor* t) {
         TL_TRY(launch_dense_to_bits(c, t));
     }
     t->bits_valid = true;
+    t->lazy_src = nullptr;
     return TL_OK;
 }
 
@@ -231,12 +248,14 @@ tl_status ensure_csr(tl_ctx* c, Tensor* t) {
 tl_status alloc_bits_public(tl_ctx* c, Tensor* t) { return alloc_bits(c, t); }
 
 void mark_written_dense(Tensor* t) {
+    t->lazy_src = nullptr;
     t->dense_valid = true;
     t->zero = false;
     t->bits_valid = t->csr_valid = t->csc_valid = false;
 }
 
 void mark_written_bits(Tensor* t) {
+    t->lazy_src = nullptr;
     t->bits_valid = true;
     t->zero = false;
     t->boolean = true;
@@ -309,9 +328,11 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     c->tensors.clear();
     for (auto& p : c->pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
     for (auto e : c->event_pool) cudaEventDestroy(e);
+    comm_peer_release(c);
     if (c->comm) comm_destroy(c);
     for (int i = 0; i < 4; ++i) cudaFree(c->ws[i]);
     cudaFree(c->aux);
+    cudaFree(c->fix_state);
     cudaFree(c->d_flags);
     cudaFreeHost(c->h_flags);
     cudaStreamDestroy(c->stream);
@@ -565,7 +586,7 @@ extern "C" tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* 
     std::vector<float> out_val;
     out_col.reserve(order.size());
     out_val.reserve(order.size());
-    bool nonneg = true, ones = true;
+    bool nonneg = true, ones = true, pos = true;
     for (int64_t r = 0; r < lrows; ++r) {
         auto b = order.begin() + rowptr[r], en = order.begin() + rowptr[r + 1];
         std::stable_sort(b, en, [&](int64_t x, int64_t y) { return cols[x] < cols[y]; });
@@ -573,6 +594,7 @@ extern "C" tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* 
             if (it + 1 != en && cols[*(it + 1)] == cols[*it]) continue;
             const float v = vals ? (float)vals[*it] : 1.0f;
             nonneg = nonneg && v >= 0.0f;
+            pos = pos && v > 0.0f;
             ones = ones && v == 1.0f;
             out_col.push_back((int32_t)cols[*it]);
             out_val.push_back(v);
@@ -600,7 +622,9 @@ extern "C" tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* 
     t->zero = false;
     t->defined = true;
     t->csr_valid = true;
+    t->csr_stamp = next_csr_stamp();
     t->csr_nonneg = nonneg;
+    t->csr_pos = pos;
     t->csr_ones = ones;
     t->boolean = nonneg && ones;
     t->dense_valid = t->bits_valid = t->csc_valid = false;

@@ -15,6 +15,7 @@
 namespace tl {
 
 constexpr int kMaxVars = 12;
+constexpr int kMaxPeers = 8;   // ranks of one box that exchange fixpoint flags over NVLink
 
 // ----------------------------------------------------------------------------
 // Device tensor with several interchangeable storages.
@@ -53,6 +54,7 @@ struct Tensor {
     int64_t nnz = 0, csr_cap = 0, csr_rows = 0;
     bool csr_valid = false;
     bool csr_nonneg = false;  // every stored value >= 0
+    bool csr_pos = false;     // every stored value > 0 (each entry is an edge of step(E))
     bool csr_ones = false;    // every stored value == 1
 
     // CSC (predecessor lists) of a rank-2 tensor, global
@@ -60,6 +62,21 @@ struct Tensor {
     int32_t* rowidx = nullptr;
     int64_t csc_cap = 0;
     bool csc_valid = false;
+
+    // bit rows not written yet: row r holds step(lazy_src) row r * world + rank
+    // (row r when not sharded); ensure_bits writes them, the one-launch
+    // closure fixpoint builds them in shared memory instead
+    Tensor* lazy_src = nullptr;
+    uint64_t lazy_stamp = 0;
+
+    // CSR generation: changes whenever the CSR contents are rebuilt
+    uint64_t csr_stamp = 0;
+    // successor table of the one-launch closure fixpoint, built from the CSR
+    int4* succ = nullptr;
+    int64_t succ_cap = 0;       // int4 entries
+    uint64_t succ_stamp = 0;    // csr_stamp it was built from (0: none)
+    int64_t succ_nodes = 0;     // node count and sentinel it was built for
+    int32_t succ_sentinel = 0;
 
     int64_t local_rows(int rank_, int world) const {
         if (shard != TL_SHARD_ROWS || world <= 1 || this->rank < 1) return this->rank >= 1 ? dims[0] : 1;
@@ -107,6 +124,17 @@ struct tl_ctx {
     void* aux = nullptr;        // state kept across the sweeps of one fixpoint
     size_t aux_cap = 0;
     int* h_flags = nullptr;     // pinned mirror
+    void* fix_state = nullptr;  // control block of the one-launch closure fixpoint
+    // the equation of tl_program_run whose step(E) result may stay unwritten
+    // until the closure fixpoint that reads it next
+    const tl_equation* lazy_eq = nullptr;
+
+    // multi-GPU fixpoint flags: every rank's slot array mapped into this
+    // process (peer memory over NVLink), set up on first use
+    int peer_state = 0;                              // 0 not tried, 1 ready, -1 unavailable
+    unsigned long long* peer_slots[tl::kMaxPeers] = {};
+    void* peer_own = nullptr;                        // this rank's slot array
+    unsigned long long peer_tokens = 0;              // sweeps exchanged so far
 
     // profiling
     bool prof = false;
@@ -251,11 +279,23 @@ tl_status launch_bits_to_dense(tl_ctx* c, Tensor* t);
 tl_status launch_dense_to_csr(tl_ctx* c, Tensor* t);
 tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, int sweep);
 tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed);
+// every right-form sweep of a fixpoint in one cooperative launch; *handled is
+// false when the shapes or the context do not allow it (the caller then runs
+// one launch per sweep)
+tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweeps, int* sweeps_out,
+                                  bool* changed_out, bool* handled);
+uint64_t next_csr_stamp();
+// multi-GPU fixpoint flags over peer memory (comm.cpp); collective over all ranks
+tl_status comm_peer_setup(tl_ctx* c);
+void comm_peer_release(tl_ctx* c);
 
 // elementwise gradient rules
+// overwrite: out holds logical zeros that are not in memory yet (no memset
+// needed when the rule covers every element, see grad_elem_covers)
 tl_status launch_grad_elem(tl_ctx* c, int rule, float* out, int64_t out_total, const float* up,
                            int64_t up_total, const float* x, int64_t x_total, const float* y,
-                           int64_t y_total);
+                           int64_t y_total, int overwrite = 0);
+bool grad_elem_covers(int rule, int64_t out_total, int64_t up_total, int64_t x_total);
 tl_status launch_grad_softmax(tl_ctx* c, float* out, int64_t out_total, const float* up,
                               int64_t up_total, const float* y, int64_t y_total);
 tl_status launch_fill(tl_ctx* c, float* p, int64_t n, float v);

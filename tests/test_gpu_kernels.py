@@ -44,7 +44,12 @@ GEMM_CASES = [
     (512, 512, 128, "mk", "kn", "mn", "scale"),     # literal scale
     (512, 512, 130, "mk", "kn", "mn", "accum"),     # += into existing values, K not /4
     (2048, 64, 2048, "mk", "kn", "mn", ""),         # N = 64 tile, long K
-    (1024, 10, 4096, "mk", "kn", "mn", ""),         # skinny N: SIMT split-K
+    (1024, 10, 4096, "mk", "kn", "mn", ""),         # skinny N, A k-contiguous, split K
+    (4096, 10, 1024, "km", "kn", "mn", ""),         # skinny N, A row-contiguous (weight gradient)
+    (1000, 13, 777, "mk", "nk", "mn", "accum"),     # skinny N, unaligned rows, strided B, +=
+    (512, 16, 300, "km", "nk", "nm", "scale"),      # skinny N, transposed output, scale
+    (1024, 4096, 10, "mk", "nk", "mn", ""),         # thin K (input gradient of a 10-wide layer)
+    (1000, 1000, 7, "mk", "kn", "mn", "accum"),     # thin K, tails, +=
 ]
 
 
@@ -173,6 +178,82 @@ def test_closure_with_cycles(ctx, oracle_lib):
                                 "Reach[x,z] max= step(Reach[x,y] Edge[y,z])\n"
     ref = both(ctx, oracle_lib, src, sparse={"Edge": (rows, cols, None)})
     np.testing.assert_array_equal(ctx.tensor("Reach"), ref.tensor("Reach"))
+
+
+def _closure_case(ctx, oracle_lib, n, rows, cols):
+    src = decl(x=n, y=n, z=n) + "sparse Edge[x, y]\nReach[x,y] = step(Edge[x,y])\n" \
+                                "Reach[x,z] max= step(Reach[x,y] Edge[y,z])\n"
+    ctx.run(lang.Program(src, sparse_inputs={"Edge": (rows, cols, None)}))
+    got = ctx.bits("Reach")
+    colptr, rowidx = gen.csr_from_coo(n, cols, rows)
+    R = np.zeros((n, (n + 31) // 32), dtype=np.uint32)
+    np.bitwise_or.at(R, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
+    sweeps = oracle_lib.closure_right(n, colptr, rowidx, R)
+    np.testing.assert_array_equal(got, R)
+    return sweeps
+
+
+def test_closure_high_degree_nodes(ctx, oracle_lib):
+    # nodes with more successors than the successor table holds inline
+    n, rng = 3000, np.random.default_rng(21)
+    pairs = set()
+    for u in range(n - 1):
+        d = 40 if u % 50 == 0 else int(rng.integers(0, 6))
+        for v in rng.integers(u + 1, n, size=d):
+            pairs.add((u, int(v)))
+    pr = np.array(sorted(pairs), dtype=np.int64)
+    sweeps = _closure_case(ctx, oracle_lib, n, pr[:, 0], pr[:, 1])
+    assert ctx.sweeps == sweeps == 2
+
+
+def test_closure_large_frontier(ctx, oracle_lib):
+    # rows whose first frontier and later frontiers outgrow the queue (spill set)
+    n, rng = 4096, np.random.default_rng(22)
+    pairs = set()
+    for u in range(8):
+        for v in rng.choice(np.arange(u + 1, n), 2500, replace=False):
+            pairs.add((u, int(v)))
+    r2, c2 = gen.random_dag(n, 6, 23)
+    pairs.update(zip(r2.tolist(), c2.tolist()))
+    pr = np.array(sorted(pairs), dtype=np.int64)
+    sweeps = _closure_case(ctx, oracle_lib, n, pr[:, 0], pr[:, 1])
+    assert ctx.sweeps == sweeps == 2
+
+
+@pytest.mark.parametrize("n", [33, 1000, 2017])
+def test_closure_odd_widths_and_cycles(ctx, oracle_lib, n):
+    # row widths that are not a multiple of 128 bits, with back edges
+    rng = np.random.default_rng(n)
+    pairs = np.unique(rng.integers(0, n, size=(3 * n, 2)), axis=0)
+    pairs = pairs[pairs[:, 0] != pairs[:, 1]]
+    _closure_case(ctx, oracle_lib, n, pairs[:, 0], pairs[:, 1])
+
+
+def test_closure_explicit_zero_edges(ctx, oracle_lib):
+    # stored 0.0 entries are not edges of step(Edge): the closure must not follow them
+    n = 200
+    rows, cols = gen.random_dag(n, 3, 31)
+    vals = np.ones(len(rows))
+    vals[::3] = 0.0
+    src = decl(x=n, y=n, z=n) + "sparse Edge[x, y]\nReach[x,y] = step(Edge[x,y])\n" \
+                                "Reach[x,z] max= step(Reach[x,y] Edge[y,z])\n"
+    ref = both(ctx, oracle_lib, src, sparse={"Edge": (rows, cols, vals)})
+    np.testing.assert_array_equal(ctx.tensor("Reach"), ref.tensor("Reach"))
+
+
+def test_closure_one_launch_matches_per_sweep(ctx, oracle_lib, monkeypatch):
+    # the one-launch fixpoint and the per-sweep launches give the same bits and sweeps
+    n = 2048
+    rows, cols = gen.random_dag(n, 5, 24)
+    src = decl(x=n, y=n, z=n) + "sparse Edge[x, y]\nReach[x,y] = step(Edge[x,y])\n" \
+                                "Reach[x,z] max= step(Reach[x,y] Edge[y,z])\n"
+    p = lang.Program(src, sparse_inputs={"Edge": (rows, cols, None)})
+    ctx.run(p)
+    one, s1 = ctx.bits("Reach"), ctx.sweeps
+    monkeypatch.setenv("TL_CLOSURE_PER_SWEEP", "1")
+    ctx.run(p)
+    np.testing.assert_array_equal(ctx.bits("Reach"), one)
+    assert ctx.sweeps == s1 == 2
 
 
 def test_generic_recursive_dense(ctx, oracle_lib):
