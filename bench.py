@@ -169,16 +169,15 @@ def l2_flush(buf):
     buf.add_(1)   # writes 256 MiB (> 126 MB L2) on torch's stream
 
 
-def time_steps(ctx, step, steps, warmup, dist, flush, profile=True):
+def time_steps(ctx, step, steps, warmup, dist, flush):
+    """Device time of `steps` steps after `warmup` untimed ones, per-launch
+    profiling off; returns (ms, launches in the timed steps)."""
     import torch
     timer = StreamTimer(ctx)
     for _ in range(warmup):
         step()
     ctx.sync()
     torch.cuda.synchronize()
-    if profile:
-        ctx.profile(True)
-        ctx.profile_reset()
     dist.barrier()
     total = 0.0
     launches0 = ctx.launches
@@ -194,6 +193,25 @@ def time_steps(ctx, step, steps, warmup, dist, flush, profile=True):
     torch.cuda.synchronize()
     dist.barrier()
     return total, ctx.launches - launches0
+
+
+def profile_steps(ctx, step, steps, dist, flush):
+    """Per-kernel device times (CUDA events around every launch) over `steps`
+    more steps, taken after the timed ones so the events cost the headline nothing."""
+    import torch
+    ctx.profile(True)
+    ctx.profile_reset()
+    dist.barrier()
+    for _ in range(steps):
+        l2_flush(flush)
+        torch.cuda.synchronize()
+        step()
+        ctx.sync()
+    torch.cuda.synchronize()
+    dist.barrier()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    return prof
 
 
 # ---------------------------------------------------------------------------- closure
@@ -231,9 +249,8 @@ def run_closure(args, dist, peaks):
     clocks = ClockSampler(dist.local)
     clocks.start()
     ms, launches = time_steps(ctx, lambda: ctx.run(resident), args.steps, args.warmup, dist, flush)
-    prof = ctx.profile_read()
-    ctx.profile(False)
     clk = clocks.stop()
+    prof = profile_steps(ctx, lambda: ctx.run(resident), args.steps, dist, flush)
     ms_max = dist.max(ms)
     total_sweeps = sweeps * args.steps
     value = total_sweeps / (ms_max / 1e3)
@@ -255,7 +272,11 @@ def run_closure(args, dist, peaks):
             "unit": "GB/s", "frac": round(achieved / peaks[0], 4), "peak_source": peaks[2],
             "traffic": None, "algo_bytes_per_launch": algo_bytes, "avg_launch_ms": per_launch_ms,
             "sweeps_per_launch": sweeps if kname == "closure_fixpoint" else 1,
-            "share_of_step": round(st["total_ms"] / max(ms, 1e-9), 3)}
+            "share_of_step": round(st["total_ms"] / max(ms, 1e-9), 3),
+            # the launch's phases from the device clock (rows of each sweep,
+            # then its settling: grid barrier and, on several GPUs, the peer wait)
+            "phases_ms": {k.split(".", 1)[1]: round(v["total_ms"] / max(1, v["launches"]), 4)
+                          for k, v in prof.items() if k.startswith("closure_fixpoint.")}}
 
     # end to end: host COO -> CSR -> device, the fixpoint, full Reach bits back to the host
     e2e_total = 0.0
@@ -315,8 +336,7 @@ def run_einsum_configs(args, peaks):
                 s.coo_rows = None
                 s.coo_cols = None
         ms, launches = time_steps(ctx, lambda: ctx.run(p_res), args.steps, args.warmup, One(), flush)
-        prof = ctx.profile_read()
-        ctx.profile(False)
+        prof = profile_steps(ctx, lambda: ctx.run(p_res), args.steps, One(), flush)
         per = ms / args.steps
         top = max(prof.items(), key=lambda kv: kv[1]["total_ms"]) if prof else ("", {})
         tc = prof.get("gemm_tcgen05_tf32")

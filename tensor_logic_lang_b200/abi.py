@@ -182,7 +182,7 @@ def load_library(path=None):
     # NCCL: load the same libnccl.so.2 torch uses before our library resolves it.
     try:
         import nvidia.nccl  # noqa: F401
-        nccl_dir = os.path.join(os.path.dirname(nvidia.nccl.__file__), "lib")
+        nccl_dir = os.path.join(list(nvidia.nccl.__path__)[0], "lib")
         cand = os.path.join(nccl_dir, "libnccl.so.2")
         if os.path.exists(cand):
             C.CDLL(cand, mode=C.RTLD_GLOBAL)

@@ -23,7 +23,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 def nccl_paths():
     try:
         import nvidia.nccl
-        base = os.path.dirname(nvidia.nccl.__file__)
+        # a namespace package: no __file__, one directory in __path__
+        base = list(nvidia.nccl.__path__)[0]
         inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
         if os.path.exists(os.path.join(inc, "nccl.h")):
             return inc, lib

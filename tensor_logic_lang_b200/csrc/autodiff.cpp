@@ -292,9 +292,8 @@ tl_status run_backward(tl_ctx* c, const char* loss, const char (*params)[TL_NAME
         Tensor* t;
         TL_TRY(new_tensor(c, std::string("dL_d") + loss, L->rank, L->dims, &t));
         TL_TRY(ensure_dense(c, t));
-        const float one = 1.0f;
-        TL_CK(c, cudaMemcpyAsync(t->dense, &one, 4, cudaMemcpyHostToDevice, c->stream));
-        TL_CK(c, cudaStreamSynchronize(c->stream));
+        // dL/dL = 1 (a device fill: no host memory, no synchronisation)
+        TL_TRY(launch_fill(c, t->dense, 1, 1.0f));
         mark_written_dense(t);
     }
     for (auto& gr : g.grads) TL_TRY(run_grad(c, gr));

@@ -27,6 +27,8 @@
 // needs a second sweep: on an edge set with u < v the first sweep closes
 // every row, as the reference's in-place z-ascending loop does, and the
 // second finds nothing pending (2 sweeps, as the reference).
+#include <stdio.h>
+
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
@@ -38,7 +40,8 @@ namespace {
 
 constexpr int kFixQueue = 1024;   // queued bit positions per warp
 constexpr int kFixItems = 4;      // queued bits one lane expands per step
-constexpr int kFixWarps = 4;      // most warps per block
+constexpr int kFixWarps = 8;      // most warps per block (the team of a heavy row)
+constexpr int kHeavyBudget = 2048; // with teams on: queued bits a lone warp expands before handing the row over
 static_assert((kFixQueue & (kFixQueue - 1)) == 0, "queue positions wrap with a mask");
 static_assert(kFixItems == 4, "the extra-successor pass selects among 4 items");
 
@@ -51,7 +54,17 @@ struct FixState {
     int sweeps;                       // sweeps completed
     int last_changed;                 // the last sweep changed a row (all ranks)
     int err;                          // 1: barrier wait ran out, 2: peer wait ran out
+    int n_heavy;                      // rows handed to teams this sweep
+    int heavy_next;                   // next of them a team takes
+    // %globaltimer marks of the first kFixMarks sweeps: launch, every block's
+    // lone-warp rows done (latest), team rows done, sweep settled (after the
+    // peer exchange)
+    unsigned long long t_start;
+    unsigned long long t_rows[2];
+    unsigned long long t_team[2];
+    unsigned long long t_settled[2];
 };
+constexpr int kFixMarks = 2;
 
 struct FixArgs {
     uint32_t* R;
@@ -61,7 +74,11 @@ struct FixArgs {
     const int32_t* colidx;
     int64_t e_rows;
     int32_t* pending;
+    int32_t* heavy;            // rows handed to teams (one slot per local row)
     FixState* st;
+    int team;                  // warps per block
+    unsigned team_qmask;       // team queue positions - 1 (a power of two)
+    int team_budget;           // rows handed to teams after this many queued bits (0: no teams)
     int lazy;                  // rows not written yet: row r starts as succ(r * row_stride + row_offset)
     int64_t row_stride, row_offset;
     int max_sweeps;
@@ -104,9 +121,10 @@ __device__ __forceinline__ int64_t warp_min64(int64_t v) {
 }
 
 // Queue slot `pos` if it lies below `limit`, else the spill set.
-__device__ __forceinline__ void enqueue(uint32_t* q, uint32_t* spill, int pos, int limit, int32_t z, int64_t& low) {
+__device__ __forceinline__ void enqueue(uint32_t* q, unsigned qmask, uint32_t* spill, int pos, int limit, int32_t z,
+                                        int64_t& low) {
     if (pos < limit) {
-        q[(unsigned)pos & (kFixQueue - 1)] = (uint32_t)z;
+        q[(unsigned)pos & qmask] = (uint32_t)z;
     } else {
         atomicOr(&spill[z >> 5], 1u << (z & 31));
         low = min(low, (int64_t)(z >> 5));
@@ -123,7 +141,8 @@ __device__ __forceinline__ bool set_new(uint32_t* row, int32_t z) {
 // Moves up to `room` bits of the spill set, lowest first from word `lo`, into
 // the queue at `tail`, clearing them; leaves in `lo` the lowest word that may
 // still hold a bit (`words` when none).  Warp-uniform.
-__device__ __forceinline__ int harvest(uint32_t* spill, int64_t words, int64_t& lo, uint32_t* q, int tail, int room, int lane) {
+__device__ __forceinline__ int harvest(uint32_t* spill, int64_t words, int64_t& lo, uint32_t* q, unsigned qmask,
+                                      int tail, int room, int lane) {
     int stored = 0;
     for (int64_t w0 = lo & ~int64_t(31); w0 < words; w0 += 32) {
         const int64_t w = w0 + lane;
@@ -144,7 +163,7 @@ __device__ __forceinline__ int harvest(uint32_t* spill, int64_t words, int64_t& 
         }
         int at = tail + start;
         for (uint32_t m = take; m; m &= m - 1)
-            q[(unsigned)(at++) & (kFixQueue - 1)] = (uint32_t)(w * 32 + __ffs(m) - 1);
+            q[(unsigned)(at++) & qmask] = (uint32_t)(w * 32 + __ffs(m) - 1);
         if (take) spill[w] = bits & ~take;
         if (stored + total > room) {
             const unsigned left = __ballot_sync(0xffffffffu, (bits & ~take) != 0u);
@@ -158,8 +177,10 @@ __device__ __forceinline__ int harvest(uint32_t* spill, int64_t words, int64_t& 
 }
 
 // Closes every pending row taken from `next_row`; true if a row grew.
+// budget > 0: a row still open after that many queued bits is handed to the
+// block's team (the row stays unwritten and pending).
 __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long* next_row, int grab, bool lazy,
-                                           uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
+                                           int budget, uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
     const bool vec = (words & 3) == 0;
     bool any = false;
@@ -241,11 +262,17 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
             __syncwarp();
             }
 
-            bool grew = false;
+            bool grew = false, heavy = false;
             for (;;) {
+                if (budget && head > budget) {
+                    // too much work for one warp: leave the row (unwritten,
+                    // still pending) to a team of warps after this phase
+                    heavy = true;
+                    break;
+                }
                 if (head == tail) {
                     if (lo >= words) break;
-                    const int got = harvest(spill, words, lo, q, tail, kFixQueue, lane);
+                    const int got = harvest(spill, words, lo, q, kFixQueue - 1, tail, kFixQueue, lane);
                     __syncwarp();
                     tail += got;
                     if (got == 0) break;
@@ -297,7 +324,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
                         const int32_t s[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
-                            if ((fresh >> (k * 8 + j)) & 1ull) enqueue(q, spill, at++, limit, s[j], slow);
+                            if ((fresh >> (k * 8 + j)) & 1ull) enqueue(q, kFixQueue - 1, spill, at++, limit, s[j], slow);
                     }
                 }
                 if (total) {
@@ -328,7 +355,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
                             f = set_new(row, z);
                         }
                         const unsigned bal = __ballot_sync(0xffffffffu, f);
-                        if (f) enqueue(q, spill, tail + __popc(bal & ((1u << lane) - 1u)), limit, z, slow);
+                        if (f) enqueue(q, kFixQueue - 1, spill, tail + __popc(bal & ((1u << lane) - 1u)), limit, z, slow);
                         if (bal) {
                             grew = grew || counts;
                             tail = min(tail + __popc(bal), limit);
@@ -338,7 +365,13 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
                 lo = min(lo, warp_min64(slow));
                 __syncwarp();
             }
-            if (lane == 0) a.pending[r] = INT32_MAX;
+            if (heavy) {
+                if (lane == 0) a.heavy[atomicAdd(&a.st->n_heavy, 1)] = (int32_t)r;
+                for (int64_t w = lane * 4; w < a.wpad; w += 128)
+                    *reinterpret_cast<uint4*>(spill + w) = make_uint4(0u, 0u, 0u, 0u);
+                __syncwarp();
+                continue;
+            }
             if (grew || lazy) {
                 if (vec) {
                     for (int64_t w = lane * 4; w < words; w += 128)
@@ -348,6 +381,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
                 }
                 any = any || grew;
             }
+            if (lane == 0) a.pending[r] = INT32_MAX;
             __syncwarp();
         }
     }
@@ -382,29 +416,192 @@ __device__ int exchange_changed(const FixArgs& a, int s, int c, int* ok) {
     return any;
 }
 
-// Grid barrier at the end of sweep s; false if a wait ran out.
-__device__ bool sweep_barrier(const FixArgs& a, int s) {
+// One row closed by the whole block (a team of a.team warps): the row, its
+// spill set and one large queue (every warp's queue space) are shared; each
+// step every lane takes up to kFixItems queued bits, and new bits are placed
+// with one shared-memory atomic per warp.  Returns true if the row grew.
+__device__ bool team_close_row(const FixArgs& a, int64_t r, int64_t start_w, bool lazy, uint32_t* row,
+                               uint32_t* spill, uint32_t* q) {
+    __shared__ int s_head, s_tail, s_grew;
+    __shared__ unsigned long long s_lo;
+    const int lane = threadIdx.x & 31;
+    const int T = blockDim.x;
+    const unsigned qmask = a.team_qmask;
+    const int QT = (int)qmask + 1;
+    const int64_t words = a.words;
+    const bool vec = (words & 3) == 0;
+    uint32_t* grow = a.R + r * words;
+    if (lazy) {
+        for (int64_t w = threadIdx.x * 4; w < a.wpad; w += 4 * T)
+            *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
+        if (threadIdx.x == 0) {
+            q[0] = (uint32_t)(r * a.row_stride + a.row_offset);
+            s_head = 0;
+            s_tail = 1;
+            s_lo = (unsigned long long)words;
+        }
+    } else {
+        // every set bit from the pending word on starts in the spill set
+        for (int64_t w = threadIdx.x; w < words; w += T) {
+            const uint32_t v = grow[w];
+            row[w] = v;
+            spill[w] = w >= start_w ? v : 0u;
+        }
+        if (threadIdx.x == 0) {
+            s_head = 0;
+            s_tail = 0;
+            s_lo = (unsigned long long)start_w;
+        }
+    }
+    if (threadIdx.x == 0) s_grew = 0;
+    for (;;) {
+        __syncthreads();
+        const int h = s_head, t = s_tail;
+        if (h == t) {
+            if (s_lo >= (unsigned long long)words) break;
+            if (threadIdx.x < 32) {
+                int64_t lo = (int64_t)s_lo;
+                const int got = harvest(spill, words, lo, q, qmask, t, QT, lane);
+                if (lane == 0) {
+                    s_tail = t + got;
+                    s_lo = (unsigned long long)lo;
+                }
+            }
+            continue;
+        }
+        const bool counts = !lazy || h != 0;
+        const int take = min(T * kFixItems, t - h);
+        int4 A[kFixItems], B[kFixItems];
+        int32_t Y[kFixItems];
+#pragma unroll
+        for (int k = 0; k < kFixItems; ++k) {
+            A[k] = make_int4(-1, -1, -1, -1);
+            B[k] = make_int4(-1, -1, -1, -1);
+            Y[k] = -1;
+            const int idx = k * T + threadIdx.x;
+            if (idx < take) {
+                const int32_t y = (int32_t)q[(unsigned)(h + idx) & qmask];
+                Y[k] = y;
+                A[k] = __ldg(&a.succ[2 * (int64_t)y]);
+                B[k] = __ldg(&a.succ[2 * (int64_t)y + 1]);
+            }
+        }
+        __syncthreads();   // every taken slot is read: they may be refilled
+        const int limit = h + take + QT;
+        unsigned long long fresh = 0;
+#pragma unroll
+        for (int k = 0; k < kFixItems; ++k) {
+            if (Y[k] >= 0) {
+                const int32_t sv[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if ((j < 7 || sv[j] >= 0) && set_new(row, sv[j])) fresh |= 1ull << (k * 8 + j);
+            }
+        }
+        const int cnt = __popcll(fresh);
+        const int pre = scan_incl(cnt, lane);
+        const int total = __shfl_sync(0xffffffffu, pre, 31);
+        int64_t slow = INT64_MAX;
+        if (total) {
+            int base = 0;
+            if (lane == 31) base = atomicAdd(&s_tail, total);
+            base = __shfl_sync(0xffffffffu, base, 31);
+            int at = base + pre - cnt;
+#pragma unroll
+            for (int k = 0; k < kFixItems; ++k) {
+                if (!((fresh >> (k * 8)) & 0xffull)) continue;
+                const int32_t sv[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if ((fresh >> (k * 8 + j)) & 1ull) enqueue(q, qmask, spill, at++, limit, sv[j], slow);
+            }
+            if (counts && lane == 0) s_grew = 1;
+        }
+        unsigned xm = 0;
+#pragma unroll
+        for (int k = 0; k < kFixItems; ++k)
+            if (Y[k] >= 0 && B[k].w == -2) xm |= 1u << k;
+        if (__any_sync(0xffffffffu, xm)) {
+            int64_t e = 0, e_end = 0;
+            for (;;) {
+                if (e >= e_end && xm) {
+                    const int k = __ffs(xm) - 1;
+                    xm &= xm - 1;
+                    const int32_t y = k == 0 ? Y[0] : k == 1 ? Y[1] : k == 2 ? Y[2] : Y[3];
+                    e = a.rowptr[y] + 7;
+                    e_end = a.rowptr[y + 1];
+                }
+                if (!__any_sync(0xffffffffu, e < e_end)) break;
+                bool f = false;
+                int32_t z = 0;
+                if (e < e_end) {
+                    z = a.colidx[e++];
+                    f = set_new(row, z);
+                }
+                const unsigned bal = __ballot_sync(0xffffffffu, f);
+                if (bal) {
+                    int base = 0;
+                    if (lane == 0) base = atomicAdd(&s_tail, __popc(bal));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (f) enqueue(q, qmask, spill, base + __popc(bal & ((1u << lane) - 1u)), limit, z, slow);
+                    if (counts && lane == 0) s_grew = 1;
+                }
+            }
+        }
+        slow = warp_min64(slow);
+        if (lane == 0 && slow != INT64_MAX) atomicMin(&s_lo, (unsigned long long)slow);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            s_head = h + take;
+            if (s_tail > h + take + QT) s_tail = h + take + QT;   // the rest went to the spill set
+        }
+    }
+    const bool grew = s_grew != 0;
+    if (grew || lazy) {
+        if (vec) {
+            for (int64_t w = threadIdx.x * 4; w < words; w += 4 * T)
+                *reinterpret_cast<uint4*>(grow + w) = *reinterpret_cast<const uint4*>(row + w);
+        } else {
+            for (int64_t w = threadIdx.x; w < words; w += T) grow[w] = row[w];
+        }
+    }
+    if (threadIdx.x == 0) a.pending[r] = INT32_MAX;
+    __syncthreads();
+    return grew;
+}
+
+// Grid barrier number `gen` (1, 2, ...).  At the end of sweep s (settle) the
+// last block to arrive settles the sweep: reads the changed word, exchanges it
+// with the other ranks, decides whether another sweep runs.  False if a wait
+// ran out.
+__device__ bool grid_barrier(const FixArgs& a, unsigned gen, int s, bool settle) {
     __shared__ int ok_s;
     __syncthreads();
     if (threadIdx.x == 0) {
         int ok = 1;
+        if (s < kFixMarks) atomicMax(settle ? &a.st->t_team[s] : &a.st->t_rows[s], global_ns());
         __threadfence();
         const unsigned prev = atomicAdd(&a.st->bar_count, 1u);
         if (prev == a.nblocks - 1) {
             __threadfence();
-            int c = *(volatile int*)&a.st->changed[s & 1];
-            if (a.world > 1) c = exchange_changed(a, s, c, &ok);
-            a.st->next_row[(s + 1) & 1] = 0;
-            a.st->changed[(s + 1) & 1] = 0;
-            a.st->sweeps = s + 1;
-            a.st->last_changed = c;
-            a.st->go = (ok && c && s + 1 < a.max_sweeps) ? 1 : 0;
+            if (settle) {
+                int c = *(volatile int*)&a.st->changed[s & 1];
+                if (a.world > 1) c = exchange_changed(a, s, c, &ok);
+                a.st->next_row[(s + 1) & 1] = 0;
+                a.st->changed[(s + 1) & 1] = 0;
+                a.st->n_heavy = 0;
+                a.st->heavy_next = 0;
+                a.st->sweeps = s + 1;
+                a.st->last_changed = c;
+                a.st->go = (ok && c && s + 1 < a.max_sweeps) ? 1 : 0;
+                if (s < kFixMarks) a.st->t_settled[s] = global_ns();
+            }
             a.st->bar_count = 0;
             __threadfence();
-            atomicExch(&a.st->bar_gen, (unsigned)(s + 1));
+            atomicExch(&a.st->bar_gen, gen);
         } else {
             const unsigned long long t0 = global_ns();
-            while (*(volatile unsigned*)&a.st->bar_gen < (unsigned)(s + 1)) {
+            while (*(volatile unsigned*)&a.st->bar_gen < gen) {
                 if (global_ns() - t0 > a.timeout_ns) {
                     atomicExch(&a.st->err, 1);
                     ok = 0;
@@ -420,21 +617,45 @@ __device__ bool sweep_barrier(const FixArgs& a, int s) {
     return ok_s != 0;
 }
 
-__global__ void __launch_bounds__(32 * kFixWarps, 4) k_closure_fix(const FixArgs a) {
+__global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs a) {
     extern __shared__ __align__(16) uint32_t smem_fix[];
+    __shared__ int s_idx;
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     uint32_t* row = smem_fix + (int64_t)wib * (2 * a.wpad + 4 + kFixQueue);
     uint32_t* spill = row + a.wpad + 4;
     uint32_t* q = spill + a.wpad;
-    // the sentinel successor (bit 0 of word wpad) reads as already set
-    if (lane == 0) row[a.wpad] = 0xffffffffu;
-    for (int64_t w = lane; w < a.wpad; w += 32) spill[w] = 0u;
-    __syncwarp();
+    if (blockIdx.x == 0 && threadIdx.x == 0) a.st->t_start = global_ns();
+    unsigned gen = 0;
     for (int s = 0; s < a.max_sweeps; ++s) {
-        const bool grew = close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, a.lazy && s == 0, row, spill, q,
-                                     lane);
+        const bool lazy = a.lazy && s == 0;
+        // each warp's own row space: the sentinel successor (bit 0 of word
+        // wpad) reads as set; the spill set starts empty (a team row may have
+        // used this space as queue)
+        if (lane == 0) row[a.wpad] = 0xffffffffu;
+        for (int64_t w = lane * 4; w < a.wpad; w += 128)
+            *reinterpret_cast<uint4*>(spill + w) = make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+        bool grew = close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, lazy, a.team > 1 ? a.team_budget : 0,
+                               row, spill, q, lane);
         if (lane == 0 && grew) *(volatile int*)&a.st->changed[s & 1] = 1;
-        if (!sweep_barrier(a, s)) return;
+        if (a.team > 1 && a.team_budget > 0) {
+            if (!grid_barrier(a, ++gen, s, false)) return;
+            // rows handed over in this sweep, one per block at a time
+            const int n_heavy = *(volatile int*)&a.st->n_heavy;
+            uint32_t* trow = smem_fix;
+            for (;;) {
+                if (threadIdx.x == 0) s_idx = atomicAdd(&a.st->heavy_next, 1);
+                __syncthreads();
+                const int idx = s_idx;
+                __syncthreads();
+                if (idx >= n_heavy) break;
+                const int64_t r = a.heavy[idx];
+                const bool tg = team_close_row(a, r, lazy ? 0 : a.pending[r], lazy, trow, trow + a.wpad + 4,
+                                               trow + 2 * a.wpad + 4);
+                if (threadIdx.x == 0 && tg) *(volatile int*)&a.st->changed[s & 1] = 1;
+            }
+        }
+        if (!grid_barrier(a, ++gen, s, true)) return;
         if (!*(volatile int*)&a.st->go) return;
     }
 }
@@ -506,34 +727,43 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         E->succ_sentinel = sentinel;
     }
 
-    // fixpoint-long state: pending word per row (0: expand everything)
-    if ((size_t)rows * 4 > c->aux_cap) {
+    // fixpoint-long state: pending word per row (0: expand everything), then
+    // the list of rows handed to teams in a sweep
+    const size_t aux_need = std::max<size_t>((size_t)rows * 8, 4096);
+    if (aux_need > c->aux_cap) {
         TL_CK(c, cudaStreamSynchronize(c->stream));
         cudaFree(c->aux);
         c->aux = nullptr;
         c->aux_cap = 0;
-        TL_CK(c, cudaMalloc(&c->aux, std::max<size_t>((size_t)rows * 4, 4096)));
-        c->aux_cap = std::max<size_t>((size_t)rows * 4, 4096);
+        TL_CK(c, cudaMalloc(&c->aux, aux_need));
+        c->aux_cap = aux_need;
     }
     static_assert(sizeof(FixState) <= 128, "control block and its pinned mirror");
+    static_assert(kFixWarps * 32 <= 1024, "block size");
     if (!c->fix_state) TL_CK(c, cudaMalloc(&c->fix_state, 256));
     if (rows > 0) TL_CK(c, cudaMemsetAsync(c->aux, 0, (size_t)rows * 4, c->stream));
     TL_CK(c, cudaMemsetAsync(c->fix_state, 0, sizeof(FixState), c->stream));
 
-    // shape: the warps-per-block split that keeps the most warps resident
+    // shape: with teams (TL_CLOSURE_TEAMS) the largest block that fits, so a
+    // heavy row gets the most warps; otherwise the split that keeps the most
+    // warps resident
     TL_CK(c, cudaFuncSetAttribute(k_closure_fix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
     const size_t per_warp = fix_smem_per_warp(words);
+    const bool teams = getenv("TL_CLOSURE_TEAMS") != nullptr;
     int wpb = 1, per_sm = 0;
-    for (int w = 1; w <= kFixWarps; ++w) {
-        if (per_warp * w > kSmemCap) break;
+    for (int w = kFixWarps; w >= 1; w >>= 1) {
+        if (per_warp * w > kSmemCap) continue;
         int b = 0;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_closure_fix, 32 * w, per_warp * w);
-        if (b * w > per_sm * wpb) {
-            wpb = w;
-            per_sm = b;
-        }
+        if (b < 1) continue;
+        if (teams) { wpb = w; per_sm = b; break; }
+        if (b * w > per_sm * wpb) { wpb = w; per_sm = b; }
     }
     if (per_sm < 1) return fail(c, TL_ERR_UNSUPPORTED, "closure fixpoint: no resident block fits");
+    // a team's queue: every warp's space except the row and spill set it works on
+    const int64_t team_words = (int64_t)wpb * (int64_t)(per_warp / 4) - (2 * wpad + 4);
+    int64_t qt = 1;
+    while (qt * 2 <= team_words) qt *= 2;
     int64_t grid = std::min<int64_t>((int64_t)c->sm_count * per_sm, std::max<int64_t>((rows + wpb - 1) / wpb, 1));
 
     FixArgs a{};
@@ -546,6 +776,10 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.colidx = E->colidx;
     a.e_rows = E->csr_rows;
     a.pending = (int32_t*)c->aux;
+    a.heavy = (int32_t*)c->aux + rows;
+    a.team = wpb;
+    a.team_qmask = (unsigned)(qt - 1);
+    a.team_budget = teams ? kHeavyBudget : 0;
     a.st = (FixState*)c->fix_state;
     // rows that step(E) left unwritten start from E's successor lists
     a.lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp ? 1 : 0;
@@ -579,6 +813,30 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // algorithmic bytes of the launch: every sweep reads and writes the rows
     if (c->prof && !c->pending.empty() && c->pending.back().name == "closure_fixpoint")
         c->pending.back().bytes = sweep_bytes * std::max(h.sweeps, 1);
+    if (c->prof) {
+        // phases of the launch from the device's own clock: each sweep's row
+        // work (until the last block is done) and its settling (barrier and,
+        // on several GPUs, the wait for the other ranks)
+        unsigned long long prev = h.t_start;
+        auto add = [&](const char* what, int s, unsigned long long from, unsigned long long to) {
+            char nm[64];
+            snprintf(nm, sizeof nm, "closure_fixpoint.sweep%d_%s", s + 1, what);
+            KStat& k = c->stats[nm];
+            k.launches++;
+            k.total_ms += (double)(to - from) / 1e6;
+        };
+        for (int s = 0; s < std::min(h.sweeps, kFixMarks); ++s) {
+            // lone-warp rows (ends at the phase barrier), team rows, settling
+            const unsigned long long rows_end = h.t_rows[s] ? h.t_rows[s] : h.t_team[s];
+            if (!h.t_team[s] || !h.t_settled[s] || rows_end < prev || h.t_team[s] < rows_end ||
+                h.t_settled[s] < h.t_team[s])
+                break;
+            add("rows", s, prev, rows_end);
+            if (h.t_rows[s]) add("teams", s, rows_end, h.t_team[s]);
+            add("settle", s, h.t_team[s], h.t_settled[s]);
+            prev = h.t_settled[s];
+        }
+    }
     if (c->world > 1) c->peer_tokens += (unsigned long long)h.sweeps;
     if (h.err) {
         if (c->world > 1) c->peer_state = -1;   // ranks may disagree on the token count now

@@ -125,157 +125,180 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const __grid_constant__ GemmP
 // Skinny shapes (no per-term nonlinearity), fp32 FFMA, bandwidth-bound
 // ============================================================================
 // C[M, N <= 16] = scale * A[M, K] B[K, N] with a long K (the output layer and
-// its weight gradient): a block owns 32 rows of C and one K range (blockIdx.y;
-// partial sums are added with atomics when K is split).  B's K range streams
-// through shared memory in 256-row chunks, padded to 16 columns.
-//  A_MCONT (A's rows contiguous, e.g. a transposed activation): lane = row,
-//    the 8 warps take interleaved k, each thread keeps 16 sums, and the warps'
-//    sums are added in shared memory.
-//  otherwise (A's k contiguous): warp w owns rows 4w..4w+3, lanes take 4
-//    consecutive k (one 128-bit load when aligned), and the 64 sums are
-//    reduced across the warp at the end.
-constexpr int SK_BM = 32, SK_KC = 256;
+// its weight gradient).  Both kernels keep many loads of A in flight (the
+// cost is streaming A once) and add partial sums with atomics when K is split
+// over blockIdx.y (C zeroed first unless it accumulates).
+//
+// k_skinny_kcont, A's k contiguous: a block owns 32 rows (4 per warp) and a
+// 512-wide K range.  B's slice is staged n-major, so lane l reads column n at
+// k = 4l .. 4l+3 with one conflict-free 128-bit load shared by the warp's 4
+// rows; each lane keeps 8 128-bit loads of A in flight, and the warp reduces
+// its sums at the end.
+constexpr int SKC_RPW = 4, SKC_ROWS = 8 * SKC_RPW, SKC_K = 512;
+// k_skinny_mcont, A's rows contiguous (a transposed activation): lane = row,
+// a block owns 32 rows and a 256-wide K range, warp w takes k = w, w + 8, ...
+// (32 loads in flight per lane), B's slice is staged k-major (broadcast
+// reads), and the 8 warps' sums are added in shared memory.
+constexpr int SKM_ROWS = 32, SKM_K = 256;
 
-template <bool A_MCONT>
-__global__ void __launch_bounds__(256) k_gemm_skinny_n(const __grid_constant__ GemmPlan p, int64_t k_per_split,
-                                                       int vec) {
-    // A_MCONT reads one k row of B for all lanes (broadcast): k-major rows;
-    // otherwise lanes read consecutive k of one column: n-major rows
-    __shared__ __align__(16) float Bs[A_MCONT ? SK_KC : 16][A_MCONT ? 16 : SK_KC];
-    __shared__ float red[A_MCONT ? 8 : 1][SK_BM][17];
+__device__ __forceinline__ void skinny_put(const GemmPlan& p, int64_t m, int n, float v, bool atomic) {
+    if (m >= p.M || n >= p.N) return;
+    float* cp = p.C + m * p.scm + n * p.scn;
+    v *= p.scale;
+    if (atomic) atomicAdd(cp, v);
+    else *cp = p.beta ? *cp + v : v;
+}
+
+// B[k0 + kk, nn] for kk < KMAX, nn < 16 (zero past kn and N) into dst(kk, nn),
+// walking whichever of k / n is contiguous in memory.  Each of the 256
+// threads issues all of its KMAX * 16 / 256 loads before any store, so the
+// slice costs one memory round trip.
+template <int KMAX, typename F>
+__device__ __forceinline__ void stage_b(const GemmPlan& p, int64_t k0, int kn, F dst) {
+    constexpr int PER = KMAX * 16 / 256;
+    static_assert(KMAX * 16 % 256 == 0, "256 threads stage the slice");
+    float v[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+        const int i = threadIdx.x + u * 256;
+        const int kk = p.sbn == 1 ? (i >> 4) : (i % KMAX);
+        const int nn = p.sbn == 1 ? (i & 15) : (i / KMAX);
+        v[u] = (kk < kn && nn < p.N) ? p.B[(k0 + kk) * p.sbk + nn * p.sbn] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+        const int i = threadIdx.x + u * 256;
+        dst(p.sbn == 1 ? (i >> 4) : (i % KMAX), p.sbn == 1 ? (i & 15) : (i / KMAX), v[u]);
+    }
+}
+
+__global__ void __launch_bounds__(256) k_skinny_kcont(const __grid_constant__ GemmPlan p, int vec) {
+    __shared__ __align__(16) float Bt[16][SKC_K];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t m0 = (int64_t)blockIdx.x * SK_BM;
-    const int64_t kb = (int64_t)blockIdx.y * k_per_split;
-    const int64_t ke = kb + k_per_split < p.K ? kb + k_per_split : p.K;
-    constexpr int NACC = A_MCONT ? 16 : 64;
-    float acc[NACC];
+    const int64_t m0 = (int64_t)blockIdx.x * SKC_ROWS + w * SKC_RPW;
+    const int64_t kc = (int64_t)blockIdx.y * SKC_K;
+    const int kn = (int)(p.K - kc < SKC_K ? p.K - kc : SKC_K);
+    stage_b<SKC_K>(p, kc, kn, [&](int kk, int nn, float v) { Bt[nn][kk] = v; });
+    __syncthreads();
+    float acc[SKC_RPW][16];
 #pragma unroll
-    for (int i = 0; i < NACC; ++i) acc[i] = 0.f;
-    for (int64_t kc = kb; kc < ke; kc += SK_KC) {
-        const int kn = (int)(ke - kc < SK_KC ? ke - kc : SK_KC);
-        __syncthreads();
-        for (int i = threadIdx.x; i < SK_KC * 16; i += 256) {
-            const int kk = i >> 4, nn = i & 15;
-            const float v = (kk < kn && nn < p.N) ? p.B[(kc + kk) * p.sbk + nn * p.sbn] : 0.f;
-            if (A_MCONT) Bs[kk][nn] = v;
-            else Bs[nn][kk] = v;
-        }
-        __syncthreads();
-        if (A_MCONT) {
-            const int64_t m = m0 + lane;
-            const float* ap = p.A + m * p.sam + kc * p.sak;
-            // four k per warp and round, their loads issued together
-            for (int k0 = w; k0 < kn; k0 += 32) {
-                float a[4];
+    for (int r = 0; r < SKC_RPW; ++r)
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int kk = k0 + 8 * u;
-                    a[u] = (m < p.M && kk < kn) ? ap[kk * p.sak] : 0.f;
-                }
+        for (int nn = 0; nn < 16; ++nn) acc[r][nn] = 0.f;
+    // the warp's rows at 4 consecutive k per lane, two 128-wide k groups per
+    // round (8 loads of A in flight), each column of B read once per group
+    // and used by all the warp's rows
+    for (int g0 = 0; g0 < SKC_K / 128; g0 += 2) {
+        float a[2][SKC_RPW][4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int kk = k0 + 8 * u;
-                    if (kk >= kn) break;
-                    const float4* b4 = reinterpret_cast<const float4*>(Bs[kk]);
+        for (int u = 0; u < 2; ++u)
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 b = b4[q];
-                        acc[4 * q + 0] = fmaf(a[u], b.x, acc[4 * q + 0]);
-                        acc[4 * q + 1] = fmaf(a[u], b.y, acc[4 * q + 1]);
-                        acc[4 * q + 2] = fmaf(a[u], b.z, acc[4 * q + 2]);
-                        acc[4 * q + 3] = fmaf(a[u], b.w, acc[4 * q + 3]);
-                    }
+            for (int r = 0; r < SKC_RPW; ++r) {
+                const int kk = lane * 4 + 128 * (g0 + u);
+                const int64_t m = m0 + r;
+                const float* ap = p.A + m * p.sam + kc + kk;
+                if (m < p.M && vec && kk + 3 < kn) {
+                    const float4 t = *reinterpret_cast<const float4*>(ap);
+                    a[u][r][0] = t.x; a[u][r][1] = t.y; a[u][r][2] = t.z; a[u][r][3] = t.w;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) a[u][r][j] = (m < p.M && kk + j < kn) ? ap[j] : 0.f;
                 }
             }
-        } else {
-            // the chunk's two 128-wide k rounds: all eight row loads first
-            float a2[2][4][4];
 #pragma unroll
-            for (int it = 0; it < 2; ++it)
+        for (int u = 0; u < 2; ++u) {
+            const int kk = lane * 4 + 128 * (g0 + u);
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int kk = lane * 4 + it * 128;
-                    const int64_t m = m0 + w * 4 + r;
-                    const float* ap = p.A + m * p.sam + (kc + kk) * p.sak;
-                    if (m < p.M && vec && kk + 3 < kn) {
-                        const float4 t = *reinterpret_cast<const float4*>(ap);
-                        a2[it][r][0] = t.x; a2[it][r][1] = t.y; a2[it][r][2] = t.z; a2[it][r][3] = t.w;
-                    } else {
+            for (int nn = 0; nn < 16; ++nn) {
+                if (nn >= p.N) break;
+                const float4 b = *reinterpret_cast<const float4*>(&Bt[nn][kk]);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) a2[it][r][i] = (m < p.M && kk + i < kn) ? ap[i * p.sak] : 0.f;
-                    }
-                }
-#pragma unroll
-            for (int it = 0; it < 2; ++it) {
-                const int kk = lane * 4 + it * 128;
-                if (kk >= kn) break;
-                float (&a)[4][4] = a2[it];
-                // column n of B at this lane's 4 k: one conflict-free 128-bit load
-#pragma unroll
-                for (int nn = 0; nn < 16; ++nn) {
-                    const float4 b = *reinterpret_cast<const float4*>(&Bs[nn][kk]);
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        float t = acc[r * 16 + nn];
-                        t = fmaf(a[r][0], b.x, t);
-                        t = fmaf(a[r][1], b.y, t);
-                        t = fmaf(a[r][2], b.z, t);
-                        acc[r * 16 + nn] = fmaf(a[r][3], b.w, t);
-                    }
+                for (int r = 0; r < SKC_RPW; ++r) {
+                    float t = fmaf(a[u][r][0], b.x, acc[r][nn]);
+                    t = fmaf(a[u][r][1], b.y, t);
+                    t = fmaf(a[u][r][2], b.z, t);
+                    acc[r][nn] = fmaf(a[u][r][3], b.w, t);
                 }
             }
         }
     }
-    const bool atomic = gridDim.y > 1;
-    auto put = [&](int64_t m, int n, float v) {
-        if (m >= p.M || n >= p.N) return;
-        float* cp = p.C + m * p.scm + n * p.scn;
-        v *= p.scale;
-        if (atomic) atomicAdd(cp, v);
-        else *cp = p.beta ? *cp + v : v;
-    };
-    if (A_MCONT) {
 #pragma unroll
-        for (int n = 0; n < 16; ++n) red[w][lane][n] = acc[n];
-        __syncthreads();
-        for (int i = threadIdx.x; i < SK_BM * 16; i += 256) {
-            const int r = i >> 4, n = i & 15;
-            float v = 0.f;
+    for (int r = 0; r < SKC_RPW; ++r)
 #pragma unroll
-            for (int ww = 0; ww < 8; ++ww) v += red[ww][r][n];
-            put(m0 + r, n, v);
+        for (int nn = 0; nn < 16; ++nn) {
+            if (nn >= p.N) break;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[r][nn] += __shfl_xor_sync(0xffffffffu, acc[r][nn], o);
         }
-    } else {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+    for (int r = 0; r < SKC_RPW; ++r)
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-        // every lane holds the 64 sums; lane l writes sums 2l and 2l + 1
+        for (int nn = 0; nn < 16; ++nn)
+            if (lane == nn) skinny_put(p, m0 + r, nn, acc[r][nn], gridDim.y > 1);
+}
+
+__global__ void __launch_bounds__(256) k_skinny_mcont(const __grid_constant__ GemmPlan p) {
+    __shared__ __align__(16) float Bs[SKM_K][16];
+    __shared__ float red[8][SKM_ROWS][17];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t m = (int64_t)blockIdx.x * SKM_ROWS + lane;
+    const int64_t kc = (int64_t)blockIdx.y * SKM_K;
+    const int kn = (int)(p.K - kc < SKM_K ? p.K - kc : SKM_K);
+    stage_b<SKM_K>(p, kc, kn, [&](int kk, int nn, float v) { Bs[kk][nn] = v; });
+    constexpr int U = SKM_K / 8;
+    float a[U];
+    const float* ap = p.A + m * p.sam + kc * p.sak;
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
-            if ((i >> 1) == lane) put(m0 + w * 4 + (i >> 4), i & 15, acc[i]);
+    for (int u = 0; u < U; ++u) {
+        const int kk = w + 8 * u;
+        a[u] = (m < p.M && kk < kn) ? ap[kk * p.sak] : 0.f;
+    }
+    __syncthreads();
+    float acc[16];
+#pragma unroll
+    for (int nn = 0; nn < 16; ++nn) acc[nn] = 0.f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const float4* b4 = reinterpret_cast<const float4*>(Bs[w + 8 * u]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 b = b4[q];
+            acc[4 * q + 0] = fmaf(a[u], b.x, acc[4 * q + 0]);
+            acc[4 * q + 1] = fmaf(a[u], b.y, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(a[u], b.z, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(a[u], b.w, acc[4 * q + 3]);
+        }
+    }
+#pragma unroll
+    for (int nn = 0; nn < 16; ++nn) red[w][lane][nn] = acc[nn];
+    __syncthreads();
+    for (int i = threadIdx.x; i < SKM_ROWS * 16; i += 256) {
+        const int r = i >> 4, nn = i & 15;
+        float v = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < 8; ++ww) v += red[ww][r][nn];
+        skinny_put(p, (int64_t)blockIdx.x * SKM_ROWS + r, nn, v, gridDim.y > 1);
     }
 }
 
 // C[M, N] = scale * A[M, K <= 16] B[K, N] (an outer-product-like GEMM whose
-// cost is writing C): block x stages B's columns n0 .. n0 + TK_COLS and its
-// rows of A (at most TK_ROWS) in shared memory, thread t keeps
-// B[:, n0 + 4t .. +3] in registers (K padded to 16 with zeros), and each row
-// costs the thread four broadcast shared loads, 64 FMAs and one 128-bit store.
+// cost is writing C): thread t of block x loads B[:, 4t .. 4t+3] of the
+// block's TK_COLS columns into registers (K padded to 16 with zeros), the
+// block's rows of A (at most TK_ROWS) are staged in shared memory, and each
+// row costs the thread four broadcast shared loads, 64 FMAs and one 128-bit
+// store.
 constexpr int TK_ROWS = 16, TK_THREADS = 128, TK_COLS = 4 * TK_THREADS;
 
 __global__ void __launch_bounds__(TK_THREADS) k_gemm_thin_k(const __grid_constant__ GemmPlan p, int64_t rows_per_block,
                                                      int vec) {
     __shared__ __align__(16) float As[TK_ROWS][16];
-    __shared__ float Bsh[16][TK_COLS + 4];   // the block's columns of B, k-major
-    const int64_t n0 = (int64_t)blockIdx.x * TK_COLS;
-    const int64_t n = n0 + threadIdx.x * 4;
-    // B's block slice in one pass, walking whichever of k / n is contiguous
-    for (int i = threadIdx.x; i < 16 * TK_COLS; i += blockDim.x) {
-        const int k = p.sbk == 1 ? (i % 16) : (i / TK_COLS);
-        const int j = p.sbk == 1 ? (i / 16) : (i % TK_COLS);
-        Bsh[k][j] = (k < p.K && n0 + j < p.N) ? p.B[k * p.sbk + (n0 + j) * p.sbn] : 0.f;
-    }
+    const int64_t n = ((int64_t)blockIdx.x * TK_THREADS + threadIdx.x) * 4;
+    // this thread's 4 columns of B: up to 64 independent loads, all in flight
+    float b[16][4];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[k][j] = (k < p.K && n + j < p.N) ? p.B[k * p.sbk + (n + j) * p.sbn] : 0.f;
     const int64_t mb = (int64_t)blockIdx.y * rows_per_block;
     const int64_t me = mb + rows_per_block < p.M ? mb + rows_per_block : p.M;
     for (int i = threadIdx.x; i < TK_ROWS * 16; i += blockDim.x) {
@@ -283,11 +306,6 @@ __global__ void __launch_bounds__(TK_THREADS) k_gemm_thin_k(const __grid_constan
         As[r][k] = (mb + r < me && k < p.K) ? p.A[(mb + r) * p.sam + k * p.sak] : 0.f;
     }
     __syncthreads();
-    float b[16][4];
-#pragma unroll
-    for (int k = 0; k < 16; ++k)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) b[k][j] = Bsh[k][threadIdx.x * 4 + j];
     if (n >= p.N) return;
     for (int64_t m = mb; m < me; ++m) {
         const float4* a4 = reinterpret_cast<const float4*>(As[m - mb]);
@@ -764,14 +782,10 @@ static bool launch_skinny(tl_ctx* c, const GemmPlan& p, tl_status* st) {
     if (p.relu_term || p.epi_relu || p.K <= 0) return false;
     if (p.N <= 16 && p.K >= 128 && (p.sam == 1 || p.sak == 1)) {
         const bool mcont = p.sam == 1 && p.sak != 1;
-        const int64_t mblocks = (p.M + SK_BM - 1) / SK_BM;
-        // K split so the grid covers about two blocks per SM, ranges of whole chunks
-        int64_t splits = std::max<int64_t>(1, ((int64_t)c->sm_count * 2 + mblocks - 1) / mblocks);
-        const int64_t chunks = (p.K + SK_KC - 1) / SK_KC;
-        if (splits > chunks) splits = chunks;
-        const int64_t per = ((chunks + splits - 1) / splits) * SK_KC;
-        splits = (p.K + per - 1) / per;
-        if (splits > 1 && !p.beta) {
+        const int64_t rows = mcont ? SKM_ROWS : SKC_ROWS, kw = mcont ? SKM_K : SKC_K;
+        dim3 g((unsigned)((p.M + rows - 1) / rows), (unsigned)((p.K + kw - 1) / kw));
+        if (g.x > 2147483647u || g.y > 65535u) return false;
+        if (g.y > 1 && !p.beta) {
             GemmPlan z = p;   // zero C (a K = 0 pass), then add the partial sums
             z.K = 0;
             *st = launch_simt(c, z);
@@ -780,9 +794,8 @@ static bool launch_skinny(tl_ctx* c, const GemmPlan& p, tl_status* st) {
         const int vec = !mcont && (p.sam & 3) == 0 && ((uintptr_t)p.A & 15) == 0 ? 1 : 0;
         LaunchScope L(c, "gemm_skinny_fp32", (double)(p.M * p.K + p.K * p.N + p.M * p.N * (1 + p.beta)) * 4.0,
                       2.0 * p.M * p.N * p.K);
-        dim3 g((unsigned)mblocks, (unsigned)splits);
-        if (mcont) k_gemm_skinny_n<true><<<g, 256, 0, c->stream>>>(p, per, vec);
-        else k_gemm_skinny_n<false><<<g, 256, 0, c->stream>>>(p, per, vec);
+        if (mcont) k_skinny_mcont<<<g, 256, 0, c->stream>>>(p);
+        else k_skinny_kcont<<<g, 256, 0, c->stream>>>(p, vec);
         *st = L.done();
         return true;
     }

@@ -1038,6 +1038,234 @@ static const tl_equation* lazy_step_equation(const tl_statement* s, int n) {
     return nullptr;
 }
 
+// The statements of a run in order (non-recursive equations, declarations,
+// loads, backward); recursive equations are collected into `rec`.
+static tl_status run_statements(tl_ctx* c, const tl_statement* s, int n, const std::vector<tl_equation>& eqs,
+                                std::vector<tl_equation>* rec) {
+    for (int i = 0; i < n; ++i) {
+        const tl_statement* st = &s[i];
+        switch (st->kind) {
+        case TL_STMT_DOMAIN: case TL_STMT_QUERY: break;
+        case TL_STMT_EQUATION:
+            if (is_recursive(&st->eq)) rec->push_back(st->eq);
+            else {
+                // an element-wise relu right after a GEMM is written by its epilogue
+                const tl_equation* next = (i + 1 < n && s[i + 1].kind == TL_STMT_EQUATION &&
+                                           !is_recursive(&s[i + 1].eq)) ? &s[i + 1].eq : nullptr;
+                bool consumed = false;
+                TL_TRY(run_equation(c, &st->eq, next, &consumed));
+                if (consumed) ++i;
+            }
+            break;
+        case TL_STMT_SPARSE: TL_TRY(tl_sparse_decl(c, &st->sparse)); break;
+        case TL_STMT_SPARSE_LOAD: TL_TRY(run_sparse_load(c, st)); break;
+        case TL_STMT_BACKWARD:
+            TL_TRY(run_backward(c, st->name, st->params, st->n_params, eqs.data(), (int)eqs.size()));
+            break;
+        case TL_STMT_SAVE: TL_TRY(run_save(c, st)); break;
+        case TL_STMT_LOAD: TL_TRY(run_load(c, st)); break;
+        default: return fail(c, TL_ERR_INVALID, "unknown statement kind %d", st->kind);
+        }
+    }
+    return TL_OK;
+}
+
+// ----------------------------------------------------------------------------
+// Program runs as CUDA graphs.  A run whose statements only launch work on
+// the stream (no host data, files, queries, fixpoint or collectives) is
+// captured once its host state has repeated (the same tensors, storages and
+// flags at the start of two eager runs), and later runs with that state replay
+// the graph: one launch instead of the host work and launches of every
+// statement.  The host-visible state after a replay is the one the captured
+// run ended with.
+// ----------------------------------------------------------------------------
+namespace {
+
+struct TensorSnap {
+    char name[64];
+    int32_t rank, shard, succ_sentinel;
+    int64_t dims[TL_MAX_RANK];
+    int64_t total, dense_elems, bits_words, bits_rows, nnz, csr_cap, csr_rows, csc_cap, succ_cap, succ_nodes;
+    uint8_t defined, zero, boolean, is_sparse, dense_valid, bits_valid, csr_valid, csc_valid, csr_nonneg, csr_ones,
+        csr_pos, pad[5];
+    const void *dense, *bits, *rowptr, *colidx, *vals, *colptr, *rowidx, *succ, *lazy_src;
+    uint64_t csr_stamp, succ_stamp, lazy_stamp;
+};
+
+struct CtxSnap {
+    const void* ws[4];
+    size_t ws_cap[4];
+    const void* aux;
+    size_t aux_cap;
+};
+
+std::vector<uint8_t> snapshot(tl_ctx* c) {
+    std::vector<uint8_t> out;
+    CtxSnap cs;
+    memset(&cs, 0, sizeof cs);
+    for (int i = 0; i < 4; ++i) { cs.ws[i] = c->ws[i]; cs.ws_cap[i] = c->ws_cap[i]; }
+    cs.aux = c->aux;
+    cs.aux_cap = c->aux_cap;
+    out.insert(out.end(), (const uint8_t*)&cs, (const uint8_t*)&cs + sizeof cs);
+    for (auto& kv : c->tensors) {
+        const Tensor* t = kv.second.get();
+        TensorSnap z;
+        memset(&z, 0, sizeof z);
+        snprintf(z.name, sizeof z.name, "%s", kv.first.c_str());
+        z.rank = t->rank; z.shard = t->shard; z.succ_sentinel = t->succ_sentinel;
+        for (int k = 0; k < TL_MAX_RANK; ++k) z.dims[k] = t->dims[k];
+        z.total = t->total; z.dense_elems = t->dense_elems; z.bits_words = t->bits_words; z.bits_rows = t->bits_rows;
+        z.nnz = t->nnz; z.csr_cap = t->csr_cap; z.csr_rows = t->csr_rows; z.csc_cap = t->csc_cap;
+        z.succ_cap = t->succ_cap; z.succ_nodes = t->succ_nodes;
+        z.defined = t->defined; z.zero = t->zero; z.boolean = t->boolean; z.is_sparse = t->is_sparse;
+        z.dense_valid = t->dense_valid; z.bits_valid = t->bits_valid; z.csr_valid = t->csr_valid;
+        z.csc_valid = t->csc_valid; z.csr_nonneg = t->csr_nonneg; z.csr_ones = t->csr_ones; z.csr_pos = t->csr_pos;
+        z.dense = t->dense; z.bits = t->bits; z.rowptr = t->rowptr; z.colidx = t->colidx; z.vals = t->vals;
+        z.colptr = t->colptr; z.rowidx = t->rowidx; z.succ = t->succ; z.lazy_src = t->lazy_src;
+        z.csr_stamp = t->csr_stamp; z.succ_stamp = t->succ_stamp; z.lazy_stamp = t->lazy_stamp;
+        out.insert(out.end(), (const uint8_t*)&z, (const uint8_t*)&z + sizeof z);
+    }
+    return out;
+}
+
+// Puts the flags of a snapshot back (storages are the same by construction);
+// tensors the snapshot does not know become absent logical zeros.
+void apply_snapshot(tl_ctx* c, const std::vector<uint8_t>& snap) {
+    std::map<std::string, const TensorSnap*> by;
+    for (size_t off = sizeof(CtxSnap); off + sizeof(TensorSnap) <= snap.size(); off += sizeof(TensorSnap)) {
+        const TensorSnap* z = reinterpret_cast<const TensorSnap*>(snap.data() + off);
+        by[z->name] = z;
+    }
+    for (auto& kv : c->tensors) {
+        Tensor* t = kv.second.get();
+        auto it = by.find(kv.first);
+        if (it == by.end()) {
+            t->defined = false; t->zero = true;
+            t->dense_valid = t->bits_valid = t->csr_valid = t->csc_valid = false;
+            t->lazy_src = nullptr;
+            continue;
+        }
+        const TensorSnap* z = it->second;
+        t->defined = z->defined; t->zero = z->zero; t->boolean = z->boolean; t->is_sparse = z->is_sparse;
+        t->dense_valid = z->dense_valid; t->bits_valid = z->bits_valid; t->csr_valid = z->csr_valid;
+        t->csc_valid = z->csc_valid; t->csr_nonneg = z->csr_nonneg; t->csr_ones = z->csr_ones; t->csr_pos = z->csr_pos;
+        t->nnz = z->nnz; t->csr_rows = z->csr_rows; t->csr_stamp = z->csr_stamp; t->succ_stamp = z->succ_stamp;
+        t->succ_nodes = z->succ_nodes; t->succ_sentinel = z->succ_sentinel;
+        t->lazy_src = const_cast<Tensor*>(static_cast<const Tensor*>(z->lazy_src));
+        t->lazy_stamp = z->lazy_stamp;
+    }
+}
+
+bool graphable(tl_ctx* c, const tl_statement* s, int n) {
+    if (c->prof || c->world > 1 || getenv("TL_NO_GRAPHS")) return false;
+    for (int i = 0; i < n; ++i) {
+        const tl_statement* st = &s[i];
+        switch (st->kind) {
+        case TL_STMT_QUERY: case TL_STMT_SAVE: return false;
+        case TL_STMT_LOAD: if (st->host_data || st->path[0]) return false; break;
+        case TL_STMT_SPARSE_LOAD: if (st->coo_rows || st->coo_cols) return false; break;
+        case TL_STMT_EQUATION: if (is_recursive(&st->eq)) return false; break;
+        default: break;
+        }
+    }
+    return true;
+}
+
+}  // namespace
+
+void tl::release_graphs(tl_ctx* c) {
+    for (auto& g : c->graphs)
+        if (g.exec) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(g.exec));
+    c->graphs.clear();
+}
+
+// Replays or captures this run; *done when the run's work is on the stream.
+static tl_status run_as_graph(tl_ctx* c, const tl_statement* s, int n, const std::vector<tl_equation>& eqs,
+                              bool* done) {
+    *done = false;
+    // the same statement array with the same bytes (a memcmp, not a hash: the
+    // statements are several KB each)
+    const size_t bytes = (size_t)n * sizeof(tl_statement);
+    std::vector<uint8_t> begin = snapshot(c);
+    GraphEntry* e = nullptr;
+    for (auto& g : c->graphs)
+        if (g.stmts_at == s && g.stmts.size() == bytes && memcmp(g.stmts.data(), s, bytes) == 0) e = &g;
+    if (!e) {
+        if (c->graphs.size() >= 8) {   // drop the least recently used
+            auto old = std::min_element(c->graphs.begin(), c->graphs.end(),
+                                        [](const GraphEntry& a, const GraphEntry& b) { return a.used < b.used; });
+            if (old->exec) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(old->exec));
+            c->graphs.erase(old);
+        }
+        c->graphs.emplace_back();
+        e = &c->graphs.back();
+        e->stmts_at = s;
+        e->stmts.assign(reinterpret_cast<const uint8_t*>(s), reinterpret_cast<const uint8_t*>(s) + bytes);
+    }
+    e->used = ++c->graph_clock;
+    if (e->failed) return TL_OK;
+    if (e->exec && e->begin == begin) {
+        TL_CK(c, cudaGraphLaunch(static_cast<cudaGraphExec_t>(e->exec), c->stream));
+        apply_snapshot(c, e->end);
+        c->launches += e->launches;
+        c->stats["program_graph_replay"].launches++;   // visible through tl_profile_read
+        *done = true;
+        return TL_OK;
+    }
+    if (e->last_begin != begin) {   // not repeated yet: run eagerly, remember the state
+        if (getenv("TL_GRAPH_DEBUG") && !e->last_begin.empty()) {
+            size_t i = 0;
+            while (i < begin.size() && i < e->last_begin.size() && begin[i] == e->last_begin[i]) ++i;
+            const size_t t = i < sizeof(CtxSnap) ? (size_t)-1 : (i - sizeof(CtxSnap)) / sizeof(TensorSnap);
+            fprintf(stderr, "tl graph: host state differs at byte %zu (%s %s), sizes %zu/%zu\n", i,
+                    t == (size_t)-1 ? "context" : "tensor",
+                    t == (size_t)-1 ? "" : reinterpret_cast<const TensorSnap*>(begin.data() + sizeof(CtxSnap) +
+                                                                           t * sizeof(TensorSnap))->name,
+                    begin.size(), e->last_begin.size());
+        }
+        e->last_begin = begin;
+        return TL_OK;
+    }
+    if (e->exec) {
+        cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(e->exec));
+        e->exec = nullptr;
+    }
+    const int64_t launches0 = c->launches;
+    if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed) != cudaSuccess) {
+        cudaGetLastError();
+        e->failed = true;
+        return TL_OK;
+    }
+    std::vector<tl_equation> rec;
+    const tl_status st = run_statements(c, s, n, eqs, &rec);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(c->stream, &g);
+    cudaGraphExec_t x = nullptr;
+    bool ok = st == TL_OK && ce == cudaSuccess && g && rec.empty();
+    if (ok && cudaGraphInstantiate(&x, g, 0) != cudaSuccess) ok = false;
+    if (g) cudaGraphDestroy(g);
+    if (!ok) {
+        // nothing ran: put the state back and run this program eagerly from now on
+        if (getenv("TL_GRAPH_DEBUG"))
+            fprintf(stderr, "tl graph: capture failed (status %d, %s, %zu recursive): %s\n", (int)st,
+                    cudaGetErrorString(ce), rec.size(), c->err.c_str());
+        cudaGetLastError();
+        if (x) cudaGraphExecDestroy(x);
+        apply_snapshot(c, begin);
+        c->launches = launches0;
+        c->err.clear();
+        e->failed = true;
+        return TL_OK;
+    }
+    e->exec = x;
+    e->begin = begin;
+    e->end = snapshot(c);
+    e->launches = c->launches - launches0;
+    TL_CK(c, cudaGraphLaunch(x, c->stream));
+    *done = true;
+    return TL_OK;
+}
+
 extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n) {
     if (!c || (n > 0 && !s)) return TL_ERR_INVALID;
     TL_CK(c, cudaSetDevice(c->device));
@@ -1077,31 +1305,9 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
         ~LazyReset() { c->lazy_eq = nullptr; }
     } lazy_reset{c};
     c->lazy_eq = lazy_step_equation(s, n);
-    for (int i = 0; i < n; ++i) {
-        const tl_statement* st = &s[i];
-        switch (st->kind) {
-        case TL_STMT_DOMAIN: case TL_STMT_QUERY: break;
-        case TL_STMT_EQUATION:
-            if (is_recursive(&st->eq)) rec.push_back(st->eq);
-            else {
-                // an element-wise relu right after a GEMM is written by its epilogue
-                const tl_equation* next = (i + 1 < n && s[i + 1].kind == TL_STMT_EQUATION &&
-                                           !is_recursive(&s[i + 1].eq)) ? &s[i + 1].eq : nullptr;
-                bool consumed = false;
-                TL_TRY(run_equation(c, &st->eq, next, &consumed));
-                if (consumed) ++i;
-            }
-            break;
-        case TL_STMT_SPARSE: TL_TRY(tl_sparse_decl(c, &st->sparse)); break;
-        case TL_STMT_SPARSE_LOAD: TL_TRY(run_sparse_load(c, st)); break;
-        case TL_STMT_BACKWARD:
-            TL_TRY(run_backward(c, st->name, st->params, st->n_params, eqs.data(), (int)eqs.size()));
-            break;
-        case TL_STMT_SAVE: TL_TRY(run_save(c, st)); break;
-        case TL_STMT_LOAD: TL_TRY(run_load(c, st)); break;
-        default: return fail(c, TL_ERR_INVALID, "unknown statement kind %d", st->kind);
-        }
-    }
+    bool replayed = false;
+    if (graphable(c, s, n)) TL_TRY(run_as_graph(c, s, n, eqs, &replayed));
+    if (!replayed) TL_TRY(run_statements(c, s, n, eqs, &rec));
     c->lazy_eq = nullptr;
     c->last_sweeps = 0;
     if (!rec.empty()) TL_TRY(run_fixpoint(c, rec.data(), (int)rec.size(), nullptr));

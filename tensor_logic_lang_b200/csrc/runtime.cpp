@@ -328,6 +328,7 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     c->tensors.clear();
     for (auto& p : c->pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
     for (auto e : c->event_pool) cudaEventDestroy(e);
+    release_graphs(c);
     comm_peer_release(c);
     if (c->comm) comm_destroy(c);
     for (int i = 0; i < 4; ++i) cudaFree(c->ws[i]);

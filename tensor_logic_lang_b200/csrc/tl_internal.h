@@ -84,6 +84,20 @@ struct Tensor {
     }
 };
 
+// A captured CUDA graph of one program run (tl_program_run): replayed while
+// the statements and the context's host state at the start of a run (tensor
+// storages, flags, workspaces) are the same as when it was captured.
+struct GraphEntry {
+    const void* stmts_at = nullptr;    // the caller's statement array
+    std::vector<uint8_t> stmts;        // and its bytes when captured
+    std::vector<uint8_t> begin, end;   // host state before / after the run
+    std::vector<uint8_t> last_begin;   // state seen by the last eager run
+    void* exec = nullptr;              // cudaGraphExec_t
+    int64_t launches = 0;
+    bool failed = false;               // capture not possible: always run eagerly
+    uint64_t used = 0;
+};
+
 struct KStat {
     int64_t launches = 0;
     double total_ms = 0, bytes = 0, flops = 0;
@@ -125,6 +139,9 @@ struct tl_ctx {
     size_t aux_cap = 0;
     int* h_flags = nullptr;     // pinned mirror
     void* fix_state = nullptr;  // control block of the one-launch closure fixpoint
+    // captured program runs (most recently used last)
+    std::vector<tl::GraphEntry> graphs;
+    uint64_t graph_clock = 0;
     // the equation of tl_program_run whose step(E) result may stay unwritten
     // until the closure fixpoint that reads it next
     const tl_equation* lazy_eq = nullptr;
@@ -288,6 +305,8 @@ uint64_t next_csr_stamp();
 // multi-GPU fixpoint flags over peer memory (comm.cpp); collective over all ranks
 tl_status comm_peer_setup(tl_ctx* c);
 void comm_peer_release(tl_ctx* c);
+// captured program runs (lower.cpp)
+void release_graphs(tl_ctx* c);
 
 // elementwise gradient rules
 // overwrite: out holds logical zeros that are not in memory yet (no memset

@@ -4,6 +4,7 @@ import ctypes as C
 import os
 import re
 import subprocess
+import sys
 
 import pytest
 
@@ -71,3 +72,17 @@ def test_library_has_no_oracle_dependency():
     assert "oracle" not in out
     syms = subprocess.run(["nm", "-D", abi.LIB_PATH], capture_output=True, text=True).stdout
     assert "or_program_run" not in syms
+
+
+def test_library_loads_the_nccl_torch_uses():
+    # the library must resolve libnccl.so.2 to the NCCL wheel torch links, also
+    # when it is loaded before torch (an older system NCCL would break torch)
+    nvidia_nccl = pytest.importorskip("nvidia.nccl")
+    want = os.path.realpath(os.path.join(list(nvidia_nccl.__path__)[0], "lib", "libnccl.so.2"))
+    code = ("from tensor_logic_lang_b200 import abi; abi.load_library()\n"
+            "import os\n"
+            "print(sorted({os.path.realpath(l.split()[-1]) for l in open('/proc/self/maps') if 'libnccl' in l}))\n"
+            "import torch\n")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd=REPO)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert want in out.stdout and out.stdout.count("libnccl") == 1, out.stdout

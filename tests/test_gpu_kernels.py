@@ -206,8 +206,12 @@ def test_closure_high_degree_nodes(ctx, oracle_lib):
     assert ctx.sweeps == sweeps == 2
 
 
-def test_closure_large_frontier(ctx, oracle_lib):
-    # rows whose first frontier and later frontiers outgrow the queue (spill set)
+@pytest.mark.parametrize("mode", ["default", "teams"])
+def test_closure_large_frontier(ctx, oracle_lib, monkeypatch, mode):
+    # rows whose first frontier and later frontiers outgrow the queue (spill
+    # set); "teams" hands rows past the lone-warp budget to whole blocks
+    if mode == "teams":
+        monkeypatch.setenv("TL_CLOSURE_TEAMS", "1")
     n, rng = 4096, np.random.default_rng(22)
     pairs = set()
     for u in range(8):
