@@ -438,6 +438,29 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+// Epilogue stores through the TMA: a 32 x 32 fp32 tile in shared memory (rows
+// of 128 bytes, 16-byte chunk j of row r at position j ^ (r & 7): the 128-byte
+// swizzle) written to the tensor map's box at {x, y}, plainly or added
+// element-wise in L2 (accumulation and split K).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     uint32_t r[16];
     asm volatile(
@@ -465,7 +488,8 @@ struct TcCfg {
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const __grid_constant__ TcEpi epi, int num_kb, int kb_per_split) {
+              const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+              const __grid_constant__ TcEpi epi, int num_kb, int kb_per_split, int tma_store) {
     using Cfg = TcCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -563,7 +587,46 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const bool ok = mbar_wait(accum_full, 0, epi.err);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int64_t row = (int64_t)m0 + q * 32 + lane;
-        if (ok && n_kb > 0 && split_k) {
+        if (ok && tma_store && (n_kb > 0 || !split_k)) {
+            // coalesced stores by the TMA: per 32-column chunk, this warp's 32
+            // rows go through a swizzled shared tile (the pipeline's stage
+            // memory is free now), two tiles in flight per warp
+            const bool add = split_k || epi.beta;
+            uint8_t* ebase = smem + (size_t)q * 16384;
+#pragma unroll 1
+            for (int ch = 0; ch < BN / 32; ++ch) {
+                uint8_t* sc = ebase + (ch & 1) * 8192;
+                uint8_t* sd = sc + 4096;
+                if (ch >= 2) {
+                    if (lane == 0) bulk_wait_read_1();   // the store of chunk ch - 2 has read this tile
+                    __syncwarp();
+                }
+                float v[32];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + ch * 32, v);
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + ch * 32 + 16, v + 16);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 o = make_float4(v[4 * j] * epi.mag, v[4 * j + 1] * epi.mag, v[4 * j + 2] * epi.mag,
+                                                 v[4 * j + 3] * epi.mag);
+                    const int off = lane * 128 + ((j ^ (lane & 7)) << 4);
+                    *reinterpret_cast<float4*>(sc + off) = o;
+                    if (epi.epi_relu)
+                        *reinterpret_cast<float4*>(sd + off) =
+                            make_float4(fmaxf(o.x, 0.f), fmaxf(o.y, 0.f), fmaxf(o.z, 0.f), fmaxf(o.w, 0.f));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    const int x = n0 + ch * 32, y = m0 + q * 32;
+                    if (add) tma_reduce_add_2d(&tmC, sc, x, y);
+                    else tma_store_2d(&tmC, sc, x, y);
+                    if (epi.epi_relu) tma_store_2d(&tmD, sd, x, y);
+                    bulk_commit();
+                }
+            }
+            if (lane == 0) bulk_wait_all();
+            __syncwarp();
+        } else if (ok && n_kb > 0 && split_k) {
             // partial tile of a split K range: add into C
 #pragma unroll 1
             for (int ch = 0; ch < BN / 16; ++ch) {
@@ -736,9 +799,24 @@ bool make_map(CUtensorMap* map, const float* base, int64_t x, int64_t y, int64_t
     return r == CUDA_SUCCESS;
 }
 
+// Store map of a row-major fp32 matrix (rows of `row_stride` floats): 32 x 32
+// boxes, 128-byte swizzle (the epilogue's shared tile layout).
+bool make_store_map(CUtensorMap* map, const float* base, int64_t cols, int64_t rows, int64_t row_stride) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(row_stride * 4)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, bool AM, bool BM>
-tl_status launch_tc_inst(tl_ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const TcEpi& e, int64_t M, int64_t N,
-                         int num_kb, int kb_per_split, int splits) {
+tl_status launch_tc_inst(tl_ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                         const CUtensorMap& md, int tma_store, const TcEpi& e, int64_t M, int64_t N, int num_kb,
+                         int kb_per_split, int splits) {
     using Cfg = TcCfg<BN>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -748,17 +826,20 @@ tl_status launch_tc_inst(tl_ctx* c, const CUtensorMap& ma, const CUtensorMap& mb
         attr_set = true;
     }
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + TC_BM - 1) / TC_BM), (unsigned)splits);
-    k_gemm_tc<BN, AM, BM><<<grid, TC_THREADS, Cfg::SMEM, c->stream>>>(ma, mb, e, num_kb, kb_per_split);
+    static_assert(Cfg::STAGES * Cfg::STAGE >= 4 * 16384, "epilogue tiles fit in the stage memory");
+    k_gemm_tc<BN, AM, BM><<<grid, TC_THREADS, Cfg::SMEM, c->stream>>>(ma, mb, mc, md, e, num_kb, kb_per_split,
+                                                                      tma_store);
     return TL_OK;
 }
 
 template <int BN>
-tl_status launch_tc_bn(tl_ctx* c, bool am, bool bm, const CUtensorMap& ma, const CUtensorMap& mb, const TcEpi& e,
-                       int64_t M, int64_t N, int num_kb, int kb_per_split, int splits) {
-    if (!am && !bm) return launch_tc_inst<BN, false, false>(c, ma, mb, e, M, N, num_kb, kb_per_split, splits);
-    if (am && !bm) return launch_tc_inst<BN, true, false>(c, ma, mb, e, M, N, num_kb, kb_per_split, splits);
-    if (!am && bm) return launch_tc_inst<BN, false, true>(c, ma, mb, e, M, N, num_kb, kb_per_split, splits);
-    return launch_tc_inst<BN, true, true>(c, ma, mb, e, M, N, num_kb, kb_per_split, splits);
+tl_status launch_tc_bn(tl_ctx* c, bool am, bool bm, const CUtensorMap& ma, const CUtensorMap& mb,
+                       const CUtensorMap& mc, const CUtensorMap& md, int ts, const TcEpi& e, int64_t M, int64_t N,
+                       int num_kb, int kb_per_split, int splits) {
+    if (!am && !bm) return launch_tc_inst<BN, false, false>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
+    if (am && !bm) return launch_tc_inst<BN, true, false>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
+    if (!am && bm) return launch_tc_inst<BN, false, true>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
+    return launch_tc_inst<BN, true, true>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
 }
 
 bool env_flag(const char* name) {
@@ -949,11 +1030,23 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     e.mag = split ? fabsf(p.scale) : p.scale;
     e.beta = p.beta; e.epi_relu = p.epi_relu;
     e.err = c->d_flags + 8;
+    // epilogue through the TMA when C (and the fused relu output D) are row-major
+    // with 16-byte aligned rows; a fused relu needs the plain store (it reads
+    // the final sum, which an accumulating reduce does not return)
+    CUtensorMap mc, md;
+    memset(&mc, 0, sizeof mc);
+    memset(&md, 0, sizeof md);
+    auto tma_ok = [](const float* base, int64_t sm, int64_t sn) {
+        return base && sn == 1 && sm > 0 && (sm * 4) % 16 == 0 && ((uintptr_t)base & 15) == 0;
+    };
+    int ts = !env_flag("TL_GEMM_NO_TMA_STORE") && tma_ok(p.C, p.scm, p.scn) &&
+             (!p.epi_relu || (tma_ok(p.D, p.sdm, p.sdn) && !p.beta && splits == 1));
+    if (ts) ts = make_store_map(&mc, p.C, p.N, p.M, p.scm) && (!p.epi_relu || make_store_map(&md, p.D, p.N, p.M, p.sdm));
     LaunchScope L(c, "gemm_tcgen05_tf32", (double)(p.M * p.K + p.K * p.N + p.M * p.N * (1 + p.beta)) * 4.0,
                   2.0 * p.M * p.N * p.K);
-    if (BN == 256) TL_TRY(launch_tc_bn<256>(c, pa.mn, pb.mn, ma, mb, e, p.M, p.N, num_kb, kb_per_split, splits));
-    else if (BN == 128) TL_TRY(launch_tc_bn<128>(c, pa.mn, pb.mn, ma, mb, e, p.M, p.N, num_kb, kb_per_split, splits));
-    else TL_TRY(launch_tc_bn<64>(c, pa.mn, pb.mn, ma, mb, e, p.M, p.N, num_kb, kb_per_split, splits));
+    if (BN == 256) TL_TRY(launch_tc_bn<256>(c, pa.mn, pb.mn, ma, mb, mc, md, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
+    else if (BN == 128) TL_TRY(launch_tc_bn<128>(c, pa.mn, pb.mn, ma, mb, mc, md, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
+    else TL_TRY(launch_tc_bn<64>(c, pa.mn, pb.mn, ma, mb, mc, md, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
     return L.done();
 }
 

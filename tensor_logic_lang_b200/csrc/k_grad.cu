@@ -75,6 +75,37 @@ __global__ void k_grad_elem4(int rule, float* __restrict__ out, const float* __r
     }
 }
 
+// s = sum_i a[i] * b[i] in f64 in one launch: every block adds its partial
+// sum into acc; the last block to finish writes out[0] = old + s (old = 0 for
+// a logically zero output) and puts acc and the counter back to zero.
+__global__ void __launch_bounds__(256) k_dot_scalar(const float* __restrict__ a, const float* __restrict__ b,
+                                                    int64_t n, float* out, int old_zero, double* acc,
+                                                    unsigned* done) {
+    double s = 0.0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        s += (double)a[i] * (double)b[i];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __shared__ double sh[8];
+    __shared__ bool last;
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += sh[w];
+        atomicAdd(acc, t);
+        __threadfence();
+        last = atomicAdd(done, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence();
+        const double total = *(volatile double*)acc;
+        out[0] = (float)((old_zero ? 0.0 : (double)out[0]) + total);
+        *acc = 0.0;
+        *done = 0u;
+    }
+}
+
 // sum_i dY[i] * Y[i] over the whole tensor, in f64
 __global__ void k_dot(const float* up, int64_t up_n, const float* y, int64_t y_n, double* acc) {
     double s = 0.0;
@@ -133,6 +164,18 @@ tl_status launch_grad_elem(tl_ctx* c, int rule, float* out, int64_t out_total, c
     if (overwrite) TL_CK(c, cudaMemsetAsync(out, 0, (size_t)out_total * sizeof(float), c->stream));
     LaunchScope L(c, "grad_elementwise", (double)n * 12.0, (double)n * 2.0);
     k_grad_elem<<<blocks_for(c, n), 256, 0, c->stream>>>(rule, out, out_total, up, up_total, x, x_total, y, y_total, n);
+    return L.done();
+}
+
+tl_status launch_dot_scalar(tl_ctx* c, const float* a, const float* b, int64_t n, float* out, int old_zero) {
+    if (n <= 0) return TL_OK;
+    // accumulator (double) and block counter live in the context's flag words
+    double* acc = reinterpret_cast<double*>(c->d_flags + 40);
+    unsigned* done = reinterpret_cast<unsigned*>(c->d_flags + 44);
+    int64_t blocks = (n + 2047) / 2048;
+    if (blocks > c->sm_count) blocks = c->sm_count;
+    LaunchScope L(c, "dot_scalar", (double)n * 8.0, (double)n * 2.0);
+    k_dot_scalar<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, c->stream>>>(a, b, n, out, old_zero, acc, done);
     return L.done();
 }
 

@@ -315,6 +315,44 @@ bool plain_2d(const tl_ref* r, const Tensor* t, const Analysis& a) {
     return true;
 }
 
+// A full contraction of two same-shaped tensors into a scalar,
+// `L = A[i,j] B[i,j]` (einsum.zig:20-254 with every index contracted): one
+// f64 dot product over the contiguous elements.  `=` with a contraction adds
+// into the old value, as `+=` does (einsum.zig:201-212).
+tl_status try_dot(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* lhs, bool* done) {
+    *done = false;
+    if (eq->accum != TL_ACC_ASSIGN && eq->accum != TL_ACC_ADD) return TL_OK;
+    if (a.n_free != 0 || !a.has_contraction || lhs->total != 1 || eq->n_refs != 2 || eq->n_code != 3) return TL_OK;
+    if (eq->code[0].op != TL_OP_REF || eq->code[1].op != TL_OP_REF || eq->code[2].op != TL_OP_PROD ||
+        eq->code[2].arg != 2 || eq->code[0].arg != 0 || eq->code[1].arg != 1)
+        return TL_OK;
+    Tensor* A = find_defined(c, eq->refs[0].tensor);
+    Tensor* B = find_defined(c, eq->refs[1].tensor);
+    if (!A || !B || A->rank < 1 || A->rank != B->rank || eq->refs[0].rank != A->rank || eq->refs[1].rank != B->rank)
+        return TL_OK;
+    if ((int)a.vars.size() != A->rank) return TL_OK;   // every variable is one of the tensors' axes
+    for (int k = 0; k < A->rank; ++k) {
+        const int v = ref_var(&eq->refs[0], k, a);
+        if (v < 0 || v != ref_var(&eq->refs[1], k, a) || a.vars[v].size != A->dims[k] || A->dims[k] != B->dims[k])
+            return TL_OK;
+    }
+    if ((A->shard == TL_SHARD_ROWS || B->shard == TL_SHARD_ROWS) && c->world > 1) return TL_OK;
+    tl_status st;
+    const float* ap = read_ptr(c, A, &st);
+    TL_TRY(st);
+    const float* bp = read_ptr(c, B, &st);
+    TL_TRY(st);
+    if (!ap || !bp) return TL_OK;   // an operand of zeros: the generic path keeps the old value
+    const bool old_zero = lhs->zero;
+    if (old_zero) TL_TRY(alloc_dense_public(c, lhs));
+    else TL_TRY(ensure_dense(c, lhs));
+    TL_TRY(launch_dot_scalar(c, ap, bp, A->total, lhs->dense, old_zero ? 1 : 0));
+    mark_written_dense(lhs);
+    lhs->boolean = false;
+    *done = true;
+    return TL_OK;
+}
+
 tl_status try_gemm(tl_ctx* c, const tl_equation* eq, const Analysis& a, Tensor* lhs, bool* done,
                    Tensor* fuse_relu = nullptr, bool* fused = nullptr) {
     *done = false;
@@ -686,6 +724,7 @@ static tl_status run_equation(tl_ctx* c, const tl_equation* eq, const tl_equatio
     if (done && fused && consumed_next) *consumed_next = true;
     if (!done) TL_TRY(try_sparse_chain(c, eq, a, lhs, &done));
     if (!done) TL_TRY(try_step_bits(c, eq, a, lhs, &done));
+    if (!done) TL_TRY(try_dot(c, eq, a, lhs, &done));
     if (done) return TL_OK;
 
     // generic loop nest

@@ -318,6 +318,8 @@ bool grad_elem_covers(int rule, int64_t out_total, int64_t up_total, int64_t x_t
 tl_status launch_grad_softmax(tl_ctx* c, float* out, int64_t out_total, const float* up,
                               int64_t up_total, const float* y, int64_t y_total);
 tl_status launch_fill(tl_ctx* c, float* p, int64_t n, float v);
+// out[0] = (old_zero ? 0 : out[0]) + sum a[i] b[i] (f64), one launch
+tl_status launch_dot_scalar(tl_ctx* c, const float* a, const float* b, int64_t n, float* out, int old_zero);
 tl_status launch_set1(tl_ctx* c, float* p, int64_t off, const GenericPlan& plan);
 
 // communication (comm.cpp)

@@ -101,6 +101,17 @@ def test_gemm_mn_major_descriptors(ctx, oracle_lib, case, monkeypatch):
     test_gemm(ctx, oracle_lib, case)
 
 
+STORE_CASES = [c for c in GEMM_CASES if c[0] * c[1] * c[2] >= (1 << 25) and c[1] >= 64]
+
+
+@pytest.mark.parametrize("case", STORE_CASES, ids=[f"{c[0]}x{c[1]}x{c[2]}-{c[3]}{c[4]}{c[5]}-{c[6]}" for c in STORE_CASES])
+def test_gemm_plain_store_epilogue(ctx, oracle_lib, case, monkeypatch):
+    """The tensor-core GEMMs with the epilogue's per-thread stores instead of
+    TMA stores (the path for unaligned or strided outputs)."""
+    monkeypatch.setenv("TL_GEMM_NO_TMA_STORE", "1")
+    test_gemm(ctx, oracle_lib, case)
+
+
 # ----------------------------------------------------------------------------- row-wise
 ROW_CASES = [(3, 10), (2048, 2048), (64, 1000), (5, 5000), (1024, 10), (7, 129)]
 
