@@ -27,6 +27,18 @@
 // needs a second sweep: on an edge set with u < v the first sweep closes
 // every row, as the reference's in-place z-ascending loop does, and the
 // second finds nothing pending (2 sweeps, as the reference).
+//
+// Rows of step(E) (the lazy start) take a shortcut: such a row, once closed,
+// is exactly E+(y), the nodes reachable from y in one or more steps, and
+// E+(y) is a subset of E+(x) for every y reached from x.  So when the search
+// from x reaches a node y whose row is local and closed already, the warp ORs
+// row y into row x instead of expanding y's successors, and queues none of
+// the bits it brings: they are closed under succ.  The first sweep takes the
+// rows in descending order, so on an edge set with u < v every successor's
+// row is closed before its predecessors' rows start, and a row costs a few
+// row ORs: R[x] = succ(x) | OR_{y in succ(x)} R[y].  A closed row publishes
+// its nonzero word range and then its pending word (release at GPU scope);
+// readers load the pending word, fence (acquire) and read the row through L2.
 #include <stdio.h>
 
 #include <algorithm>
@@ -39,11 +51,10 @@ namespace tl {
 namespace {
 
 constexpr int kFixQueue = 1024;   // queued bit positions per warp
-constexpr int kFixItems = 4;      // queued bits one lane expands per step
+constexpr int kFixItems = 4;      // queued bits one lane expands per step (1 in the lazy sweep)
 constexpr int kFixWarps = 8;      // most warps per block (the team of a heavy row)
 constexpr int kHeavyBudget = 2048; // with teams on: queued bits a lone warp expands before handing the row over
 static_assert((kFixQueue & (kFixQueue - 1)) == 0, "queue positions wrap with a mask");
-static_assert(kFixItems == 4, "the extra-successor pass selects among 4 items");
 
 struct FixState {
     unsigned long long next_row[2];   // row counters, by sweep parity
@@ -75,6 +86,8 @@ struct FixArgs {
     int64_t e_rows;
     int32_t* pending;
     int32_t* heavy;            // rows handed to teams (one slot per local row)
+    unsigned long long* closed;   // per local row: its closed word once closed in the lazy sweep, else 0
+    int shortcut;              // lazy rows OR closed rows in (and run in descending order)
     FixState* st;
     int team;                  // warps per block
     unsigned team_qmask;       // team queue positions - 1 (a power of two)
@@ -103,6 +116,36 @@ __device__ __forceinline__ unsigned long long load_acquire_sys(const unsigned lo
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ unsigned long long load_acquire_gpu(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void store_release_gpu(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// A closed row's word: bit 63 set, bits 32..62 the end and bits 0..31 the
+// first word of its nonzero 16-byte groups (0, 0 when the row is empty).
+constexpr unsigned long long kClosedBit = 1ull << 63;
+__device__ __forceinline__ unsigned long long closed_word(int lo, int hi) {
+    return kClosedBit | ((unsigned long long)(unsigned)hi << 32) | (unsigned)lo;
+}
+
+// Local row of global node y (row r holds node r * row_stride + row_offset), or -1.
+__device__ __forceinline__ int32_t local_row(int64_t rows, int64_t stride, int64_t offset, int32_t y) {
+    const int64_t d = (int64_t)y - offset;
+    if (d < 0) return -1;
+    int64_t l = d;
+    if (stride != 1) {
+        const uint32_t ud = (uint32_t)d, us = (uint32_t)stride;
+        if (ud % us) return -1;
+        l = ud / us;
+    }
+    return l < rows ? (int32_t)l : -1;
 }
 
 __device__ __forceinline__ int scan_incl(int v, int lane) {
@@ -176,9 +219,230 @@ __device__ __forceinline__ int harvest(uint32_t* spill, int64_t words, int64_t& 
     return stored;
 }
 
-// Closes every pending row taken from `next_row`; true if a row grew.
-// budget > 0: a row still open after that many queued bits is handed to the
-// block's team (the row stays unwritten and pending).
+// row |= the closed rows held by the lanes (at most one per lane: local row
+// ly, nonzero words [lo, hi)).  Each lane ORs its own words (16-byte groups
+// lane, lane + 32, ... of every 1024-word chunk) of the source rows into the
+// shared row, two source rows' loads in flight at a time: no index search and
+// no shared-memory atomics.
+__device__ __forceinline__ void or_closed_rows(const FixArgs& a, bool has, int32_t ly, int lo, int hi,
+                                               uint32_t* row, bool vec, int lane) {
+    const int words = (int)a.words;
+    unsigned m = __ballot_sync(0xffffffffu, has);
+    if (!vec) {
+        while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const uint32_t* srow = a.R + (int64_t)__shfl_sync(0xffffffffu, ly, src) * words;
+            const int l = max(__shfl_sync(0xffffffffu, lo, src), 0);
+            const int h = min(__shfl_sync(0xffffffffu, hi, src), words);
+            for (int w = l + lane; w < h; w += 32) row[w] |= __ldcg(srow + w);
+            __syncwarp();
+        }
+        return;
+    }
+    // source rows in pairs: (ly, lo, hi) of each
+    int n = __popc(m);
+    int32_t sl[2];
+    int sa[2], sb[2];
+    for (int base = 0; base < words; base += 1024) {
+        unsigned mm = m;
+        for (int done = 0; done < n; done += 2) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                sl[j] = -1;
+                sa[j] = 0;
+                sb[j] = 0;
+                if (mm) {
+                    const int src = __ffs(mm) - 1;
+                    mm &= mm - 1;
+                    sl[j] = __shfl_sync(0xffffffffu, ly, src);
+                    sa[j] = max(__shfl_sync(0xffffffffu, lo, src), 0);
+                    sb[j] = min(__shfl_sync(0xffffffffu, hi, src), words);
+                }
+            }
+            uint4 v[2][8];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint4* srow = reinterpret_cast<const uint4*>(a.R + (int64_t)max(sl[j], 0) * words);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int w = base + i * 128 + lane * 4;
+                    v[j][i] = (sl[j] >= 0 && w + 4 > sa[j] && w < sb[j]) ? __ldcg(srow + (w >> 2))
+                                                                        : make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint4 o = make_uint4(v[0][i].x | v[1][i].x, v[0][i].y | v[1][i].y, v[0][i].z | v[1][i].z,
+                                           v[0][i].w | v[1][i].w);
+                const int w = base + i * 128 + lane * 4;
+                if (o.x | o.y | o.z | o.w) {
+                    uint4 t = *reinterpret_cast<uint4*>(row + w);
+                    t.x |= o.x;
+                    t.y |= o.y;
+                    t.z |= o.z;
+                    t.w |= o.w;
+                    *reinterpret_cast<uint4*>(row + w) = t;
+                }
+            }
+        }
+    }
+}
+
+// The search state of one row.
+struct RowSearch {
+    int head, tail;   // queue positions (wrapping)
+    int64_t lo;       // lowest spill-set word that may hold a bit (words: none)
+    bool grew;        // a bit beyond the starting ones entered the row
+};
+
+// Expands the row's queued bits (and spill set) until both are empty.
+// own_first: queue slot 0 holds the row's own node (a lazy row), whose
+// successors are the starting bits and do not count as growth.  dp: a queued
+// node whose local row is closed (lazy sweep) is ORed in, not expanded.
+// budget > 0: returns false once more than that many bits were expanded (the
+// row goes to a team); true when the row is closed.
+template <int ITEMS>
+__device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool own_first, bool dp, int budget,
+                                           uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
+    const int64_t words = a.words;
+    const bool vec = (words & 3) == 0;
+    for (;;) {
+        if (budget && S.head > budget) return false;
+        if (S.head == S.tail) {
+            if (S.lo >= words) return true;
+            const int got = harvest(spill, words, S.lo, q, kFixQueue - 1, S.tail, kFixQueue, lane);
+            __syncwarp();
+            S.tail += got;
+            if (got == 0) return true;
+            continue;
+        }
+        const bool counts = !own_first || S.head != 0;
+        const int take = min(32 * ITEMS, S.tail - S.head);
+        const int nk = (take + 31) >> 5;
+        int4 A[ITEMS], B[ITEMS];
+        int32_t Y[ITEMS], L[ITEMS];
+        unsigned long long CW[ITEMS];
+#pragma unroll
+        for (int k = 0; k < ITEMS; ++k) {
+            A[k] = make_int4(-1, -1, -1, -1);
+            B[k] = make_int4(-1, -1, -1, -1);
+            Y[k] = -1;
+            L[k] = -1;
+            CW[k] = 0;
+            if (k < nk) {
+                const int idx = k * 32 + lane;
+                if (idx < take) {
+                    const int32_t y = (int32_t)q[(unsigned)(S.head + idx) & (kFixQueue - 1)];
+                    Y[k] = y;
+                    // the table entry is loaded with the closed word, not
+                    // after it: one round trip either way
+                    A[k] = __ldg(&a.succ[2 * (int64_t)y]);
+                    B[k] = __ldg(&a.succ[2 * (int64_t)y + 1]);
+                    if (dp) L[k] = local_row(a.rows, a.row_stride, a.row_offset, y);
+                }
+            }
+        }
+        if (dp) {
+            // closed words read with acquire: the reads of a closed row come
+            // after it (for the other lanes, through the warp barrier below)
+#pragma unroll
+            for (int k = 0; k < ITEMS; ++k)
+                if (L[k] >= 0) CW[k] = load_acquire_gpu(&a.closed[L[k]]);
+#pragma unroll
+            for (int k = 0; k < ITEMS; ++k) {
+                if (CW[k] & kClosedBit) Y[k] = -1;   // closed: ORed in below, not expanded
+                else L[k] = -1;
+            }
+        }
+        __syncwarp();   // the taken slots may be refilled from here on
+        S.head += take;
+        const int limit = S.head + kFixQueue;
+        unsigned long long fresh = 0;
+#pragma unroll
+        for (int k = 0; k < ITEMS; ++k) {
+            if (k < nk && Y[k] >= 0) {
+                const int32_t s[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if ((j < 7 || s[j] >= 0) && set_new(row, s[j])) fresh |= 1ull << (k * 8 + j);
+            }
+        }
+        const int cnt = __popcll(fresh);
+        const int pre = scan_incl(cnt, lane);
+        const int total = __shfl_sync(0xffffffffu, pre, 31);
+        int64_t slow = INT64_MAX;
+        if (fresh) {
+            int at = S.tail + pre - cnt;
+#pragma unroll
+            for (int k = 0; k < ITEMS; ++k) {
+                if (!((fresh >> (k * 8)) & 0xffull)) continue;
+                const int32_t s[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if ((fresh >> (k * 8 + j)) & 1ull) enqueue(q, kFixQueue - 1, spill, at++, limit, s[j], slow);
+            }
+        }
+        if (total) {
+            S.grew = S.grew || counts;
+            S.tail = min(S.tail + total, limit);
+        }
+        // successors past the table's 7 (slot 7 marked with -2), one per
+        // lane per round, items of a lane taken in turn
+        unsigned xm = 0;
+#pragma unroll
+        for (int k = 0; k < ITEMS; ++k)
+            if (k < nk && Y[k] >= 0 && B[k].w == -2) xm |= 1u << k;
+        if (__any_sync(0xffffffffu, xm)) {
+            int64_t e = 0, e_end = 0;
+            for (;;) {
+                if (e >= e_end && xm) {
+                    const int k = __ffs(xm) - 1;
+                    xm &= xm - 1;
+                    int32_t y = Y[0];
+#pragma unroll
+                    for (int kk = 1; kk < ITEMS; ++kk)
+                        if (k == kk) y = Y[kk];
+                    e = a.rowptr[y] + 7;
+                    e_end = a.rowptr[y + 1];
+                }
+                if (!__any_sync(0xffffffffu, e < e_end)) break;
+                bool f = false;
+                int32_t z = 0;
+                if (e < e_end) {
+                    z = a.colidx[e++];
+                    f = set_new(row, z);
+                }
+                const unsigned bal = __ballot_sync(0xffffffffu, f);
+                if (f) enqueue(q, kFixQueue - 1, spill, S.tail + __popc(bal & ((1u << lane) - 1u)), limit, z, slow);
+                if (bal) {
+                    S.grew = S.grew || counts;
+                    S.tail = min(S.tail + __popc(bal), limit);
+                }
+            }
+        }
+        S.lo = min(S.lo, warp_min64(slow));
+        __syncwarp();
+        if (dp) {
+            // closed rows reached this step: OR them in (their bits are
+            // closed under succ and are not queued); growth is judged by the
+            // caller from the row's final popcount
+#pragma unroll
+            for (int k = 0; k < ITEMS; ++k) {
+                const bool has = L[k] >= 0;
+                if (__any_sync(0xffffffffu, has))
+                    or_closed_rows(a, has, L[k], (int)(unsigned)CW[k], (int)((CW[k] >> 32) & 0x7fffffffu), row, vec,
+                                   lane);
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// Closes every pending row taken from `next_row` (grab rows per counter
+// step, ascending); true if a row grew.  Lazy rows start empty with their own
+// node queued.  budget > 0: a row still open after that many queued bits is
+// handed to the block's team (the row stays unwritten and pending).
 __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long* next_row, int grab, bool lazy,
                                            int budget, uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
@@ -199,8 +463,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
             const int64_t start_w = __shfl_sync(0xffffffffu, my_pend, src);
             uint32_t* grow = a.R + r * words;
 
-            int head = 0, tail = 0;
-            int64_t lo = words;
+            RowSearch S{0, 0, words, false};
             if (lazy) {
                 // the row is step(E)'s row: start empty with the row's own
                 // node queued; its successors (the starting bits) do not
@@ -208,7 +471,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
                 for (int64_t w = lane * 4; w < a.wpad; w += 128)
                     *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
                 if (lane == 0) q[0] = (uint32_t)(r * a.row_stride + a.row_offset);
-                tail = 1;
+                S.tail = 1;
                 __syncwarp();
             } else {
             // load the row; its set bits from the pending word on are the
@@ -256,134 +519,146 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
                 }
                 stored += total;
             }
-            tail = min(stored, kFixQueue);
-            lo = warp_min64(low);
-            if (lo > words) lo = words;
+            S.tail = min(stored, kFixQueue);
+            S.lo = warp_min64(low);
+            if (S.lo > words) S.lo = words;
             __syncwarp();
             }
 
-            bool grew = false, heavy = false;
-            for (;;) {
-                if (budget && head > budget) {
-                    // too much work for one warp: leave the row (unwritten,
-                    // still pending) to a team of warps after this phase
-                    heavy = true;
-                    break;
-                }
-                if (head == tail) {
-                    if (lo >= words) break;
-                    const int got = harvest(spill, words, lo, q, kFixQueue - 1, tail, kFixQueue, lane);
-                    __syncwarp();
-                    tail += got;
-                    if (got == 0) break;
-                    continue;
-                }
-                // growth counts except while expanding a lazy row's own node
-                const bool counts = !lazy || head != 0;
-                const int take = min(32 * kFixItems, tail - head);
-                const int nk = (take + 31) >> 5;
-                int4 A[kFixItems], B[kFixItems];
-                int32_t Y[kFixItems];
-#pragma unroll
-                for (int k = 0; k < kFixItems; ++k) {
-                    A[k] = make_int4(-1, -1, -1, -1);
-                    B[k] = make_int4(-1, -1, -1, -1);
-                    Y[k] = -1;
-                    if (k < nk) {
-                        const int idx = k * 32 + lane;
-                        if (idx < take) {
-                            const int32_t y = (int32_t)q[(unsigned)(head + idx) & (kFixQueue - 1)];
-                            Y[k] = y;
-                            A[k] = __ldg(&a.succ[2 * (int64_t)y]);
-                            B[k] = __ldg(&a.succ[2 * (int64_t)y + 1]);
-                        }
-                    }
-                }
-                __syncwarp();   // the taken slots may be refilled from here on
-                head += take;
-                const int limit = head + kFixQueue;
-                unsigned long long fresh = 0;
-#pragma unroll
-                for (int k = 0; k < kFixItems; ++k) {
-                    if (k < nk && Y[k] >= 0) {
-                        const int32_t s[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            if ((j < 7 || s[j] >= 0) && set_new(row, s[j])) fresh |= 1ull << (k * 8 + j);
-                    }
-                }
-                const int cnt = __popcll(fresh);
-                const int pre = scan_incl(cnt, lane);
-                const int total = __shfl_sync(0xffffffffu, pre, 31);
-                int64_t slow = INT64_MAX;
-                if (fresh) {
-                    int at = tail + pre - cnt;
-#pragma unroll
-                    for (int k = 0; k < kFixItems; ++k) {
-                        if (!((fresh >> (k * 8)) & 0xffull)) continue;
-                        const int32_t s[8] = {A[k].x, A[k].y, A[k].z, A[k].w, B[k].x, B[k].y, B[k].z, B[k].w};
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            if ((fresh >> (k * 8 + j)) & 1ull) enqueue(q, kFixQueue - 1, spill, at++, limit, s[j], slow);
-                    }
-                }
-                if (total) {
-                    grew = grew || counts;
-                    tail = min(tail + total, limit);
-                }
-                // successors past the table's 7 (slot 7 marked with -2), one
-                // per lane per round, items of a lane taken in turn
-                unsigned xm = 0;
-#pragma unroll
-                for (int k = 0; k < kFixItems; ++k)
-                    if (k < nk && Y[k] >= 0 && B[k].w == -2) xm |= 1u << k;
-                if (__any_sync(0xffffffffu, xm)) {
-                    int64_t e = 0, e_end = 0;
-                    for (;;) {
-                        if (e >= e_end && xm) {
-                            const int k = __ffs(xm) - 1;
-                            xm &= xm - 1;
-                            const int32_t y = k == 0 ? Y[0] : k == 1 ? Y[1] : k == 2 ? Y[2] : Y[3];
-                            e = a.rowptr[y] + 7;
-                            e_end = a.rowptr[y + 1];
-                        }
-                        if (!__any_sync(0xffffffffu, e < e_end)) break;
-                        bool f = false;
-                        int32_t z = 0;
-                        if (e < e_end) {
-                            z = a.colidx[e++];
-                            f = set_new(row, z);
-                        }
-                        const unsigned bal = __ballot_sync(0xffffffffu, f);
-                        if (f) enqueue(q, kFixQueue - 1, spill, tail + __popc(bal & ((1u << lane) - 1u)), limit, z, slow);
-                        if (bal) {
-                            grew = grew || counts;
-                            tail = min(tail + __popc(bal), limit);
-                        }
-                    }
-                }
-                lo = min(lo, warp_min64(slow));
-                __syncwarp();
-            }
-            if (heavy) {
+            if (!search_row<kFixItems>(a, S, lazy, false, budget, row, spill, q, lane)) {
+                // too much work for one warp: leave the row (unwritten, still
+                // pending) to a team of warps after this phase
                 if (lane == 0) a.heavy[atomicAdd(&a.st->n_heavy, 1)] = (int32_t)r;
                 for (int64_t w = lane * 4; w < a.wpad; w += 128)
                     *reinterpret_cast<uint4*>(spill + w) = make_uint4(0u, 0u, 0u, 0u);
                 __syncwarp();
                 continue;
             }
-            if (grew || lazy) {
+            if (S.grew || lazy) {
                 if (vec) {
                     for (int64_t w = lane * 4; w < words; w += 128)
                         *reinterpret_cast<uint4*>(grow + w) = *reinterpret_cast<const uint4*>(row + w);
                 } else {
                     for (int64_t w = lane; w < words; w += 32) grow[w] = row[w];
                 }
-                any = any || grew;
+                any = any || S.grew;
             }
             if (lane == 0) a.pending[r] = INT32_MAX;
             __syncwarp();
         }
+    }
+    return any;
+}
+
+// The lazy sweep with shortcuts: rows of step(E) taken one at a time in
+// descending order.  A row starts as succ(x) (from the successor table, the
+// CSR for the rest of a long list), every fresh successor queued; the search
+// then ORs in the successors whose rows are closed and expands the others.
+// The next row's index and table entry are fetched while this row runs.  A
+// row grew if it ends with more bits than succ(x) has.  Once written, the row
+// publishes its closed word (release at GPU scope) and its pending word.
+__device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long long* next_row, int budget,
+                                              uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
+    const int64_t words = a.words;
+    const bool vec = (words & 3) == 0;
+    const int32_t sentinel = (int32_t)(a.wpad * 32);
+    const int32_t* succ32 = reinterpret_cast<const int32_t*>(a.succ);
+    bool any = false;
+    unsigned long long nb = 0;
+    if (lane == 0) nb = atomicAdd(next_row, 1ull);
+    nb = __shfl_sync(0xffffffffu, nb, 0);
+    auto node_of = [&](unsigned long long i) { return (int64_t)(a.rows - 1 - (int64_t)i) * a.row_stride + a.row_offset; };
+    int32_t tnext = ((int64_t)nb < a.rows && lane < 8) ? __ldg(succ32 + 8 * node_of(nb) + lane) : -1;
+    // the row space starts empty; each row's write-back empties it again
+    for (int64_t w = lane * 4; w < a.wpad; w += 128)
+        *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
+    while ((int64_t)nb < a.rows) {
+        const int64_t r = a.rows - 1 - (int64_t)nb;
+        const int64_t gx = node_of(nb);
+        const int32_t tslot = tnext;
+        unsigned long long nb2 = 0;
+        if (lane == 0) nb2 = atomicAdd(next_row, 1ull);   // the row after this one
+
+        // the starting bits succ(x), each fresh one queued
+        RowSearch S{0, 0, words, false};
+        const bool more = __shfl_sync(0xffffffffu, tslot, 7) == -2;
+        const int32_t s0 = (lane < 8 && tslot >= 0 && tslot < sentinel) ? tslot : -1;
+        bool f = s0 >= 0 && set_new(row, s0);
+        unsigned bal = __ballot_sync(0xffffffffu, f);
+        if (f) q[__popc(bal & ((1u << lane) - 1u))] = (uint32_t)s0;
+        S.tail = __popc(bal);
+        int n_init = S.tail;
+        if (more) {
+            int64_t slow = INT64_MAX;
+            const int64_t e_end = a.rowptr[gx + 1];
+            for (int64_t e0 = a.rowptr[gx] + 7; e0 < e_end; e0 += 32) {
+                const int64_t e = e0 + lane;
+                const int32_t z = e < e_end ? a.colidx[e] : -1;
+                f = z >= 0 && set_new(row, z);
+                bal = __ballot_sync(0xffffffffu, f);
+                if (f) enqueue(q, kFixQueue - 1, spill, S.tail + __popc(bal & ((1u << lane) - 1u)), kFixQueue, z, slow);
+                S.tail = min(S.tail + __popc(bal), kFixQueue);
+                n_init += __popc(bal);
+            }
+            S.lo = min((int64_t)words, warp_min64(slow));
+        }
+        __syncwarp();
+
+        const bool done = search_row<1>(a, S, false, true, budget, row, spill, q, lane);
+        nb = __shfl_sync(0xffffffffu, nb2, 0);
+        tnext = ((int64_t)nb < a.rows && lane < 8) ? __ldg(succ32 + 8 * node_of(nb) + lane) : -1;
+        if (!done) {
+            if (lane == 0) a.heavy[atomicAdd(&a.st->n_heavy, 1)] = (int32_t)r;
+            for (int64_t w = lane * 4; w < a.wpad; w += 128) {
+                *reinterpret_cast<uint4*>(spill + w) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
+            }
+            __syncwarp();
+            continue;
+        }
+        // write the row back (emptying the row space); its nonzero range and popcount
+        uint32_t* grow = a.R + r * words;
+        int lo_w = INT32_MAX, hi_w = 0, pc = 0;
+        if (vec) {
+            for (int64_t w = lane * 4; w < words; w += 128) {
+                const uint4 t = *reinterpret_cast<const uint4*>(row + w);
+                *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(grow + w) = t;
+                const int c = __popc(t.x) + __popc(t.y) + __popc(t.z) + __popc(t.w);
+                if (c) {
+                    pc += c;
+                    lo_w = min(lo_w, (int)w);
+                    hi_w = (int)w + 4;
+                }
+            }
+        } else {
+            for (int64_t w = lane; w < words; w += 32) {
+                const uint32_t t = row[w];
+                row[w] = 0u;
+                grow[w] = t;
+                if (t) {
+                    pc += __popc(t);
+                    lo_w = min(lo_w, (int)w);
+                    hi_w = (int)w + 1;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            lo_w = min(lo_w, __shfl_xor_sync(0xffffffffu, lo_w, o));
+            hi_w = max(hi_w, __shfl_xor_sync(0xffffffffu, hi_w, o));
+            pc += __shfl_xor_sync(0xffffffffu, pc, o);
+        }
+        any = any || pc > n_init;
+        // every lane's stores of the row come before lane 0's release of the
+        // closed word (warp barrier, then a release store at GPU scope)
+        __syncwarp();
+        if (lane == 0) {
+            store_release_gpu(&a.closed[r], lo_w < hi_w ? closed_word(lo_w, hi_w) : closed_word(0, 0));
+            a.pending[r] = INT32_MAX;
+        }
+        __syncwarp();
     }
     return any;
 }
@@ -420,6 +695,7 @@ __device__ int exchange_changed(const FixArgs& a, int s, int c, int* ok) {
 // spill set and one large queue (every warp's queue space) are shared; each
 // step every lane takes up to kFixItems queued bits, and new bits are placed
 // with one shared-memory atomic per warp.  Returns true if the row grew.
+static_assert(kFixItems == 4, "the team's extra-successor pass selects among 4 items");
 __device__ bool team_close_row(const FixArgs& a, int64_t r, int64_t start_w, bool lazy, uint32_t* row,
                                uint32_t* spill, uint32_t* q) {
     __shared__ int s_head, s_tail, s_grew;
@@ -635,8 +911,11 @@ __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs
         for (int64_t w = lane * 4; w < a.wpad; w += 128)
             *reinterpret_cast<uint4*>(spill + w) = make_uint4(0u, 0u, 0u, 0u);
         __syncwarp();
-        bool grew = close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, lazy, a.team > 1 ? a.team_budget : 0,
-                               row, spill, q, lane);
+        const int budget = a.team > 1 ? a.team_budget : 0;
+        const bool grew = lazy && a.shortcut
+                              ? close_rows_dp(a, &a.st->next_row[s & 1], budget, row, spill, q, lane)
+                              : close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, lazy, budget, row, spill, q,
+                                           lane);
         if (lane == 0 && grew) *(volatile int*)&a.st->changed[s & 1] = 1;
         if (a.team > 1 && a.team_budget > 0) {
             if (!grid_barrier(a, ++gen, s, false)) return;
@@ -727,9 +1006,9 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         E->succ_sentinel = sentinel;
     }
 
-    // fixpoint-long state: pending word per row (0: expand everything), then
-    // the list of rows handed to teams in a sweep
-    const size_t aux_need = std::max<size_t>((size_t)rows * 8, 4096);
+    // fixpoint-long state: pending word per row (0: expand everything), the
+    // list of rows handed to teams in a sweep, closed rows' nonzero ranges
+    const size_t aux_need = std::max<size_t>((size_t)rows * 16, 4096);
     if (aux_need > c->aux_cap) {
         TL_CK(c, cudaStreamSynchronize(c->stream));
         cudaFree(c->aux);
@@ -741,7 +1020,10 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     static_assert(sizeof(FixState) <= 128, "control block and its pinned mirror");
     static_assert(kFixWarps * 32 <= 1024, "block size");
     if (!c->fix_state) TL_CK(c, cudaMalloc(&c->fix_state, 256));
-    if (rows > 0) TL_CK(c, cudaMemsetAsync(c->aux, 0, (size_t)rows * 4, c->stream));
+    if (rows > 0) {
+        TL_CK(c, cudaMemsetAsync(c->aux, 0, (size_t)rows * 4, c->stream));
+        TL_CK(c, cudaMemsetAsync((char*)c->aux + (size_t)rows * 8, 0, (size_t)rows * 8, c->stream));
+    }
     TL_CK(c, cudaMemsetAsync(c->fix_state, 0, sizeof(FixState), c->stream));
 
     // shape: with teams (TL_CLOSURE_TEAMS) the largest block that fits, so a
@@ -777,12 +1059,14 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.e_rows = E->csr_rows;
     a.pending = (int32_t*)c->aux;
     a.heavy = (int32_t*)c->aux + rows;
+    a.closed = reinterpret_cast<unsigned long long*>((int32_t*)c->aux + 2 * rows);
     a.team = wpb;
     a.team_qmask = (unsigned)(qt - 1);
     a.team_budget = teams ? kHeavyBudget : 0;
     a.st = (FixState*)c->fix_state;
     // rows that step(E) left unwritten start from E's successor lists
     a.lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp ? 1 : 0;
+    a.shortcut = 1;
     // local row r is global row r * world + rank of a row-sharded relation
     a.row_stride = 1;
     a.row_offset = 0;
