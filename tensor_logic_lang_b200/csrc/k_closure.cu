@@ -86,7 +86,8 @@ struct FixArgs {
     int64_t e_rows;
     int32_t* pending;
     int32_t* heavy;            // rows handed to teams (one slot per local row)
-    unsigned long long* closed;   // per local row: its closed word once closed in the lazy sweep, else 0
+    unsigned long long* closed;   // per local row: its closed word once closed in the lazy sweep
+    uint32_t epoch;               // this launch's epoch in the closed words
     int shortcut;              // lazy rows OR closed rows in (and run in descending order)
     FixState* st;
     int team;                  // warps per block
@@ -128,11 +129,14 @@ __device__ __forceinline__ void store_release_gpu(unsigned long long* p, unsigne
     asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// A closed row's word: bit 63 set, bits 32..62 the end and bits 0..31 the
-// first word of its nonzero 16-byte groups (0, 0 when the row is empty).
-constexpr unsigned long long kClosedBit = 1ull << 63;
-__device__ __forceinline__ unsigned long long closed_word(int lo, int hi) {
-    return kClosedBit | ((unsigned long long)(unsigned)hi << 32) | (unsigned)lo;
+// A closed row's word: bits 42..63 the launch's epoch (1 .. 2^22 - 1),
+// bits 21..41 the end and bits 0..20 the first word of its nonzero 16-byte
+// groups (0, 0 when the row is empty).  A word from another launch has
+// another epoch and reads as not closed, so no launch clears the array.
+constexpr int kClosedSpan = 21;                       // row widths below 2^21 words
+constexpr uint32_t kEpochMax = (1u << 22) - 1;
+__device__ __forceinline__ unsigned long long closed_word(uint32_t epoch, int lo, int hi) {
+    return ((unsigned long long)epoch << 42) | ((unsigned long long)(unsigned)hi << kClosedSpan) | (unsigned)lo;
 }
 
 // Local row of global node y (row r holds node r * row_stride + row_offset), or -1.
@@ -351,7 +355,7 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
                 if (L[k] >= 0) CW[k] = load_acquire_gpu(&a.closed[L[k]]);
 #pragma unroll
             for (int k = 0; k < ITEMS; ++k) {
-                if (CW[k] & kClosedBit) Y[k] = -1;   // closed: ORed in below, not expanded
+                if (L[k] >= 0 && (uint32_t)(CW[k] >> 42) == a.epoch) Y[k] = -1;   // closed: ORed in below
                 else L[k] = -1;
             }
         }
@@ -431,8 +435,8 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
             for (int k = 0; k < ITEMS; ++k) {
                 const bool has = L[k] >= 0;
                 if (__any_sync(0xffffffffu, has))
-                    or_closed_rows(a, has, L[k], (int)(unsigned)CW[k], (int)((CW[k] >> 32) & 0x7fffffffu), row, vec,
-                                   lane);
+                    or_closed_rows(a, has, L[k], (int)(CW[k] & ((1u << kClosedSpan) - 1u)),
+                                   (int)((CW[k] >> kClosedSpan) & ((1u << kClosedSpan) - 1u)), row, vec, lane);
             }
             __syncwarp();
         }
@@ -552,62 +556,99 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
 
 // The lazy sweep with shortcuts: rows of step(E) taken one at a time in
 // descending order.  A row starts as succ(x) (from the successor table, the
-// CSR for the rest of a long list), every fresh successor queued; the search
-// then ORs in the successors whose rows are closed and expands the others.
-// The next row's index and table entry are fetched while this row runs.  A
-// row grew if it ends with more bits than succ(x) has.  Once written, the row
-// publishes its closed word (release at GPU scope) and its pending word.
+// CSR for the rest of a long list); fresh successors whose rows are closed are
+// ORed in, the others are queued and the search expands them (ORing in the
+// closed rows it meets).  The rows are software-pipelined: while row r runs,
+// the warp already takes the next row's index, its table entry and its
+// successors' closed words, so a row starts with all of them in hand.  A
+// closed word read early may say "not closed" for a row that closes later;
+// that successor is then expanded instead, with the same result.  A row grew
+// if it ends with more bits than succ(x) has.  Once written, the row publishes
+// its closed word (release at GPU scope) and its pending word.
 __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long long* next_row, int budget,
                                               uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
     const bool vec = (words & 3) == 0;
     const int32_t sentinel = (int32_t)(a.wpad * 32);
     const int32_t* succ32 = reinterpret_cast<const int32_t*>(a.succ);
+    const unsigned lanes_below = (1u << lane) - 1u;
+    auto node_of = [&](unsigned long long i) { return (int64_t)(a.rows - 1 - (int64_t)i) * a.row_stride + a.row_offset; };
+    // successor slot `lane` (< 8) of row i's table entry, and its closed word
+    auto slot_of = [&](unsigned long long i) {
+        return ((int64_t)i < a.rows && lane < 8) ? __ldg(succ32 + 8 * node_of(i) + lane) : -1;
+    };
+    auto closed_of = [&](int32_t sl) {
+        const int32_t l = (sl >= 0 && sl < sentinel) ? local_row(a.rows, a.row_stride, a.row_offset, sl) : -1;
+        return l >= 0 ? load_acquire_gpu(&a.closed[l]) : 0ull;
+    };
     bool any = false;
     unsigned long long nb = 0;
     if (lane == 0) nb = atomicAdd(next_row, 1ull);
     nb = __shfl_sync(0xffffffffu, nb, 0);
-    auto node_of = [&](unsigned long long i) { return (int64_t)(a.rows - 1 - (int64_t)i) * a.row_stride + a.row_offset; };
-    int32_t tnext = ((int64_t)nb < a.rows && lane < 8) ? __ldg(succ32 + 8 * node_of(nb) + lane) : -1;
+    int32_t t_next = slot_of(nb);
+    unsigned long long cw_next = closed_of(t_next);
     // the row space starts empty; each row's write-back empties it again
     for (int64_t w = lane * 4; w < a.wpad; w += 128)
         *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
     __syncwarp();
+    // the written row's closed word, published once every lane's stores of
+    // the row are done (warp barrier, then a release store at GPU scope)
+    int64_t pub_r = -1;
+    unsigned long long pub_w = 0;
+    auto publish = [&]() {
+        __syncwarp();
+        if (lane == 0 && pub_r >= 0) {
+            store_release_gpu(&a.closed[pub_r], pub_w);
+            a.pending[pub_r] = INT32_MAX;
+        }
+        pub_r = -1;
+        __syncwarp();
+    };
     while ((int64_t)nb < a.rows) {
         const int64_t r = a.rows - 1 - (int64_t)nb;
         const int64_t gx = node_of(nb);
-        const int32_t tslot = tnext;
-        unsigned long long nb2 = 0;
-        if (lane == 0) nb2 = atomicAdd(next_row, 1ull);   // the row after this one
+        const int32_t tslot = t_next;
+        const unsigned long long cw = cw_next;
 
-        // the starting bits succ(x), each fresh one queued
+        // the starting bits succ(x)
         RowSearch S{0, 0, words, false};
         const bool more = __shfl_sync(0xffffffffu, tslot, 7) == -2;
         const int32_t s0 = (lane < 8 && tslot >= 0 && tslot < sentinel) ? tslot : -1;
-        bool f = s0 >= 0 && set_new(row, s0);
-        unsigned bal = __ballot_sync(0xffffffffu, f);
-        if (f) q[__popc(bal & ((1u << lane) - 1u))] = (uint32_t)s0;
-        S.tail = __popc(bal);
-        int n_init = S.tail;
+        const bool f = s0 >= 0 && set_new(row, s0);
+        const int32_t l0 = f ? local_row(a.rows, a.row_stride, a.row_offset, s0) : -1;
+        const unsigned fresh = __ballot_sync(0xffffffffu, f);
+        int n_init = __popc(fresh);
+        unsigned long long nb2 = 0;
+        if (lane == 0) nb2 = atomicAdd(next_row, 1ull);   // the row after this one
+        const bool closed = f && l0 >= 0 && (uint32_t)(cw >> 42) == a.epoch;
+        const unsigned open = __ballot_sync(0xffffffffu, f && !closed);
+        if (f && !closed) q[__popc(open & lanes_below)] = (uint32_t)s0;
+        S.tail = __popc(open);
         if (more) {
             int64_t slow = INT64_MAX;
             const int64_t e_end = a.rowptr[gx + 1];
             for (int64_t e0 = a.rowptr[gx] + 7; e0 < e_end; e0 += 32) {
                 const int64_t e = e0 + lane;
                 const int32_t z = e < e_end ? a.colidx[e] : -1;
-                f = z >= 0 && set_new(row, z);
-                bal = __ballot_sync(0xffffffffu, f);
-                if (f) enqueue(q, kFixQueue - 1, spill, S.tail + __popc(bal & ((1u << lane) - 1u)), kFixQueue, z, slow);
+                const bool fz = z >= 0 && set_new(row, z);
+                const unsigned bal = __ballot_sync(0xffffffffu, fz);
+                if (fz) enqueue(q, kFixQueue - 1, spill, S.tail + __popc(bal & lanes_below), kFixQueue, z, slow);
                 S.tail = min(S.tail + __popc(bal), kFixQueue);
                 n_init += __popc(bal);
             }
             S.lo = min((int64_t)words, warp_min64(slow));
         }
+        // the next row's index and table entry, in flight during the ORs
+        nb = __shfl_sync(0xffffffffu, nb2, 0);
+        t_next = slot_of(nb);
         __syncwarp();
+        or_closed_rows(a, closed, l0, (int)(cw & ((1u << kClosedSpan) - 1u)),
+                       (int)((cw >> kClosedSpan) & ((1u << kClosedSpan) - 1u)), row, vec, lane);
+        __syncwarp();
+        // its successors' closed words, in flight during the search and write-back
+        cw_next = closed_of(t_next);
 
         const bool done = search_row<1>(a, S, false, true, budget, row, spill, q, lane);
-        nb = __shfl_sync(0xffffffffu, nb2, 0);
-        tnext = ((int64_t)nb < a.rows && lane < 8) ? __ldg(succ32 + 8 * node_of(nb) + lane) : -1;
         if (!done) {
             if (lane == 0) a.heavy[atomicAdd(&a.st->n_heavy, 1)] = (int32_t)r;
             for (int64_t w = lane * 4; w < a.wpad; w += 128) {
@@ -651,14 +692,9 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
             pc += __shfl_xor_sync(0xffffffffu, pc, o);
         }
         any = any || pc > n_init;
-        // every lane's stores of the row come before lane 0's release of the
-        // closed word (warp barrier, then a release store at GPU scope)
-        __syncwarp();
-        if (lane == 0) {
-            store_release_gpu(&a.closed[r], lo_w < hi_w ? closed_word(lo_w, hi_w) : closed_word(0, 0));
-            a.pending[r] = INT32_MAX;
-        }
-        __syncwarp();
+        pub_r = r;
+        pub_w = lo_w < hi_w ? closed_word(a.epoch, lo_w, hi_w) : closed_word(a.epoch, 0, 0);
+        publish();
     }
     return any;
 }
@@ -980,9 +1016,12 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         TL_TRY(comm_peer_setup(c));
         if (c->peer_state != 1) return TL_OK;
     }
-    int coop = 0;
-    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
-    if (!coop) return TL_OK;
+    if (c->fix_coop < 0) {
+        int coop = 0;
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
+        c->fix_coop = coop ? 1 : 0;
+    }
+    if (!c->fix_coop) return TL_OK;
     *handled = true;
 
     // successor table, rebuilt when the CSR or the row width changed
@@ -1006,9 +1045,9 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         E->succ_sentinel = sentinel;
     }
 
-    // fixpoint-long state: pending word per row (0: expand everything), the
-    // list of rows handed to teams in a sweep, closed rows' nonzero ranges
-    const size_t aux_need = std::max<size_t>((size_t)rows * 16, 4096);
+    // fixpoint-long state: pending word per row (0: expand everything), then
+    // the list of rows handed to teams in a sweep
+    const size_t aux_need = std::max<size_t>((size_t)rows * 8, 4096);
     if (aux_need > c->aux_cap) {
         TL_CK(c, cudaStreamSynchronize(c->stream));
         cudaFree(c->aux);
@@ -1020,28 +1059,54 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     static_assert(sizeof(FixState) <= 128, "control block and its pinned mirror");
     static_assert(kFixWarps * 32 <= 1024, "block size");
     if (!c->fix_state) TL_CK(c, cudaMalloc(&c->fix_state, 256));
-    if (rows > 0) {
-        TL_CK(c, cudaMemsetAsync(c->aux, 0, (size_t)rows * 4, c->stream));
-        TL_CK(c, cudaMemsetAsync((char*)c->aux + (size_t)rows * 8, 0, (size_t)rows * 8, c->stream));
+    // rows that step(E) left unwritten start from E's successor lists; their
+    // sweep ORs in closed rows (closed words of this launch's epoch)
+    const bool lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp;
+    const bool shortcut = lazy && words < (int64_t(1) << kClosedSpan);
+    if (shortcut) {
+        const size_t need = std::max<size_t>((size_t)rows * 8, 256);
+        if (need > c->fix_closed_cap) {
+            TL_CK(c, cudaStreamSynchronize(c->stream));
+            cudaFree(c->fix_closed);
+            c->fix_closed = nullptr;
+            c->fix_closed_cap = 0;
+            TL_CK(c, cudaMalloc(&c->fix_closed, need));
+            c->fix_closed_cap = need;
+            c->fix_epoch = kEpochMax;   // forces the clear below
+        }
+        if (++c->fix_epoch > kEpochMax) {
+            TL_CK(c, cudaMemsetAsync(c->fix_closed, 0, c->fix_closed_cap, c->stream));
+            c->fix_epoch = 1;
+        }
     }
+    // the lazy sweep with shortcuts writes every row's pending word before any
+    // later sweep reads it; otherwise every row starts fully pending
+    if (rows > 0 && !shortcut) TL_CK(c, cudaMemsetAsync(c->aux, 0, (size_t)rows * 4, c->stream));
     TL_CK(c, cudaMemsetAsync(c->fix_state, 0, sizeof(FixState), c->stream));
 
     // shape: with teams (TL_CLOSURE_TEAMS) the largest block that fits, so a
     // heavy row gets the most warps; otherwise the split that keeps the most
     // warps resident
-    TL_CK(c, cudaFuncSetAttribute(k_closure_fix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
     const size_t per_warp = fix_smem_per_warp(words);
     const bool teams = getenv("TL_CLOSURE_TEAMS") != nullptr;
-    int wpb = 1, per_sm = 0;
-    for (int w = kFixWarps; w >= 1; w >>= 1) {
-        if (per_warp * w > kSmemCap) continue;
-        int b = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_closure_fix, 32 * w, per_warp * w);
-        if (b < 1) continue;
-        if (teams) { wpb = w; per_sm = b; break; }
-        if (b * w > per_sm * wpb) { wpb = w; per_sm = b; }
+    if (c->fix_shape_words != words || c->fix_shape_teams != (int)teams) {
+        TL_CK(c, cudaFuncSetAttribute(k_closure_fix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
+        int wpb = 1, per_sm = 0;
+        for (int w = kFixWarps; w >= 1; w >>= 1) {
+            if (per_warp * w > kSmemCap) continue;
+            int b = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_closure_fix, 32 * w, per_warp * w);
+            if (b < 1) continue;
+            if (teams) { wpb = w; per_sm = b; break; }
+            if (b * w > per_sm * wpb) { wpb = w; per_sm = b; }
+        }
+        if (per_sm < 1) return fail(c, TL_ERR_UNSUPPORTED, "closure fixpoint: no resident block fits");
+        c->fix_shape_words = words;
+        c->fix_shape_teams = (int)teams;
+        c->fix_wpb = wpb;
+        c->fix_per_sm = per_sm;
     }
-    if (per_sm < 1) return fail(c, TL_ERR_UNSUPPORTED, "closure fixpoint: no resident block fits");
+    const int wpb = c->fix_wpb, per_sm = c->fix_per_sm;
     // a team's queue: every warp's space except the row and spill set it works on
     const int64_t team_words = (int64_t)wpb * (int64_t)(per_warp / 4) - (2 * wpad + 4);
     int64_t qt = 1;
@@ -1059,14 +1124,14 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.e_rows = E->csr_rows;
     a.pending = (int32_t*)c->aux;
     a.heavy = (int32_t*)c->aux + rows;
-    a.closed = reinterpret_cast<unsigned long long*>((int32_t*)c->aux + 2 * rows);
     a.team = wpb;
     a.team_qmask = (unsigned)(qt - 1);
     a.team_budget = teams ? kHeavyBudget : 0;
     a.st = (FixState*)c->fix_state;
-    // rows that step(E) left unwritten start from E's successor lists
-    a.lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp ? 1 : 0;
-    a.shortcut = 1;
+    a.lazy = lazy ? 1 : 0;
+    a.shortcut = shortcut ? 1 : 0;
+    a.closed = static_cast<unsigned long long*>(c->fix_closed);
+    a.epoch = c->fix_epoch;
     // local row r is global row r * world + rank of a row-sharded relation
     a.row_stride = 1;
     a.row_offset = 0;

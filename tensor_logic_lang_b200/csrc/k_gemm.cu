@@ -1030,6 +1030,7 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     e.mag = split ? fabsf(p.scale) : p.scale;
     e.beta = p.beta; e.epi_relu = p.epi_relu;
     e.err = c->d_flags + 8;
+    c->flags_armed = true;
     // epilogue through the TMA when C (and the fused relu output D) are row-major
     // with 16-byte aligned rows; a fused relu needs the plain store (it reads
     // the final sum, which an accumulating reduce does not return)

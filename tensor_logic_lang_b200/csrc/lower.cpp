@@ -1245,6 +1245,7 @@ static tl_status run_as_graph(tl_ctx* c, const tl_statement* s, int n, const std
     if (e->failed) return TL_OK;
     if (e->exec && e->begin == begin) {
         TL_CK(c, cudaGraphLaunch(static_cast<cudaGraphExec_t>(e->exec), c->stream));
+        c->flags_armed = true;   // the graph may hold tensor-core GEMMs
         apply_snapshot(c, e->end);
         c->launches += e->launches;
         c->stats["program_graph_replay"].launches++;   // visible through tl_profile_read
@@ -1301,6 +1302,7 @@ static tl_status run_as_graph(tl_ctx* c, const tl_statement* s, int n, const std
     e->end = snapshot(c);
     e->launches = c->launches - launches0;
     TL_CK(c, cudaGraphLaunch(x, c->stream));
+    c->flags_armed = true;
     *done = true;
     return TL_OK;
 }

@@ -334,6 +334,7 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     for (int i = 0; i < 4; ++i) cudaFree(c->ws[i]);
     cudaFree(c->aux);
     cudaFree(c->fix_state);
+    cudaFree(c->fix_closed);
     cudaFree(c->d_flags);
     cudaFreeHost(c->h_flags);
     cudaStreamDestroy(c->stream);
@@ -346,6 +347,10 @@ extern "C" const char* tl_last_error(const tl_ctx* c) { return c ? c->err.c_str(
 namespace tl {
 // Device-side error words: [8] a tensor-core pipeline wait gave up.
 tl_status check_device_flags(tl_ctx* c) {
+    // only the tensor-core GEMM writes the error word: without one since the
+    // last read there is nothing to read (and no reason to wait for the stream)
+    if (!c->flags_armed) return TL_OK;
+    c->flags_armed = false;
     TL_CK(c, cudaMemcpyAsync(c->h_flags + 8, c->d_flags + 8, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     TL_CK(c, cudaStreamSynchronize(c->stream));
     if (c->h_flags[8] != 0) {

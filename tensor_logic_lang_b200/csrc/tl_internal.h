@@ -139,6 +139,17 @@ struct tl_ctx {
     size_t aux_cap = 0;
     int* h_flags = nullptr;     // pinned mirror
     void* fix_state = nullptr;  // control block of the one-launch closure fixpoint
+    // closed words of the lazy closure sweep: one per local row, tagged with
+    // the launch's epoch so no launch has to clear them
+    void* fix_closed = nullptr;
+    size_t fix_closed_cap = 0;
+    uint32_t fix_epoch = 0;
+    // launch shape of the closure fixpoint, computed once per row width
+    int fix_coop = -1;
+    int64_t fix_shape_words = -1;
+    int fix_shape_teams = -1, fix_wpb = 0, fix_per_sm = 0;
+    // a tensor-core GEMM was given the device error word since it was last read
+    bool flags_armed = false;
     // captured program runs (most recently used last)
     std::vector<tl::GraphEntry> graphs;
     uint64_t graph_clock = 0;
