@@ -5,9 +5,11 @@ Headline: the transitive-closure fixpoint at n = 32768 (a seeded random DAG,
 convergence.  One step = one full program run (base equation + every
 fixpoint sweep).  metric = fixpoint sweeps per second over the whole n x n
 relation; with --gpus N the Reach rows are dealt cyclically over N ranks
-(one process per GPU, NCCL all-reduce of the changed word each sweep).
-At N = 1 the line also carries the einsum configurations (MLP forward,
-attention, MLP training step with autodiff, 2-layer GNN) as TFLOP/s.
+(one process per GPU; the changed word of each sweep crosses GPUs, nothing
+else).  At N = 1 the line also carries the einsum configurations (MLP
+forward, attention, MLP training step with autodiff, 2-layer GNN) as TFLOP/s
+and the row-wise softmax / lnorm kernels as GB/s against measured HBM
+(--workload rowwise runs only those).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -57,13 +59,19 @@ class ClockSampler:
         self.proc = None
         self.lines = []
 
-    def start(self):
+    def start(self, ready_s=3.0):
+        """Starts sampling and waits (up to ready_s) for the first sample, so
+        nvidia-smi's own start-up, which stalls the driver for a moment, has
+        passed before the caller's warm-up and timed steps."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < ready_s and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
 
@@ -356,6 +364,49 @@ def run_einsum_configs(args, peaks):
     return out
 
 
+def run_rowwise_configs(args, peaks):
+    """softmax / lnorm over 32M-element matrices (128 MB fp32, past L2): the
+    row-wise kernel's device time from CUDA events, as GB/s of its algorithmic
+    bytes (each element read once and written once) against measured HBM."""
+    import torch
+
+    from tensor_logic_lang_b200 import configs, lang
+    from tensor_logic_lang_b200 import inputs as gen
+    from tensor_logic_lang_b200.runtime import Context
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda:0")
+
+    class One:
+        world, rank = 1, 0
+
+        def barrier(self):
+            pass
+    n = 32 * 1024 * 1024
+    # values in [-4, 4): the distribution does not change the traffic
+    x = gen.uniform(configs.SEED, "R.X", (n,)) * 8.0 - 4.0
+    out = {}
+    for rows, cols in ((32768, 1024), (8192, 4096)):
+        for op in ("softmax", "lnorm"):
+            src, _, _, algo_bytes = configs.rowwise(rows=rows, cols=cols, op=op)
+            ctx = Context(device=0)
+            ctx.run(lang.Program(src, inputs={"X": x.reshape(rows, cols)}))
+            p_res = lang.Program(src, inputs={"X": x.reshape(rows, cols)})
+            for k in range(p_res.n):
+                if p_res.stmts[k].kind == 6:
+                    p_res.stmts[k].host_data = None
+                    p_res.stmts[k].path = b""
+            time_steps(ctx, lambda: ctx.run(p_res), args.steps, args.warmup, One(), flush)
+            prof = profile_steps(ctx, lambda: ctx.run(p_res), args.steps, One(), flush)
+            kname = f"{op}_rows"
+            st = prof.get(kname, {"launches": 0, "total_ms": float("nan")})
+            per = st["total_ms"] / max(1, st["launches"])
+            gbs = algo_bytes / (per / 1e3) / 1e9
+            out[f"{op}_{rows}x{cols}"] = {"kernel": kname, "ms": round(per, 4), "achieved_gbs": round(gbs, 1),
+                                          "peak_gbs": peaks[0], "frac": round(gbs / peaks[0], 4),
+                                          "algo_bytes": algo_bytes}
+            ctx.close()
+    return out
+
+
 # ---------------------------------------------------------------------------- reference arm
 def literal_sample(seconds=12.0, threads=1):
     """Time the literal reference sweep on sample rows, `threads` rows at a time on
@@ -412,7 +463,7 @@ def main():
     ap.add_argument("--no-einsum", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
     ap.add_argument("--workload", default="all",
-                    choices=["all", "closure", "mlp_forward", "attention", "mlp_train", "gnn"],
+                    choices=["all", "closure", "mlp_forward", "attention", "mlp_train", "gnn", "rowwise"],
                     help="all = closure headline + einsum configs at N=1; one name runs only that one "
                          "(single-config profiling)")
     args = ap.parse_args()
@@ -425,6 +476,11 @@ def main():
     dist = Dist(world, rank, local)
     torch.cuda.set_device(local)
     peaks = load_peaks()
+    if args.workload == "rowwise":
+        if rank == 0:
+            print(json.dumps({"workload": "rowwise", "rowwise": run_rowwise_configs(args, peaks)}))
+        dist.close()
+        return 0
     if args.workload not in ("all", "closure"):
         einsum = run_einsum_configs(args, peaks)
         if rank == 0:
@@ -433,9 +489,11 @@ def main():
         return 0
     res = run_closure(args, dist, peaks)
     einsum = None
+    rowwise = None
     cpu = None
     if world == 1 and not args.no_einsum and args.workload == "all":
         einsum = run_einsum_configs(args, peaks)
+        rowwise = run_rowwise_configs(args, peaks)
     if rank == 0 and world == 1 and args.cpu_sample_s > 0:
         cores = os.cpu_count() or 1
         sps, rows_done, secs = literal_sample(seconds=args.cpu_sample_s, threads=cores)
@@ -457,6 +515,8 @@ def main():
         }
         if einsum:
             line["einsum"] = einsum
+        if rowwise:
+            line["rowwise"] = rowwise
         print(json.dumps(line))
     dist.close()
     return 0

@@ -139,6 +139,22 @@ Reach[x,z] max= step(Reach[x,y] Edge[y,z])
     return src, {}, {"Edge": (rows, cols, None)}, 0
 
 
+def rowwise(rows=65536, cols=1024, op="softmax", seed=SEED):
+    """Row-wise softmax or layer norm over the last axis of an r x c matrix
+    (src/codegen/softmax.zig:19-229, src/codegen/layernorm.zig:25-310); sized
+    well past L2 so the kernel streams from HBM.  The last element is the
+    algorithmic bytes (one read and one write of every element), not flops."""
+    src = f"""
+domain r: {rows}
+domain c: {cols}
+X[r,c] = 0
+load X "x.bin"
+Y[r,c.] = {op}(X[r,c])
+"""
+    data = {"X": gen.normal(seed, f"R.{op}.X", (rows, cols))}
+    return src, data, {}, 8 * rows * cols
+
+
 def program(builder, **kw):
     src, data, sparse, flops = builder(**kw)
     return Program(src, inputs=data, sparse_inputs=sparse), data, sparse, flops

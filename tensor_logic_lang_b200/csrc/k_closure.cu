@@ -86,8 +86,17 @@ struct FixArgs {
     int64_t e_rows;
     int32_t* pending;
     int32_t* heavy;            // rows handed to teams (one slot per local row)
-    unsigned long long* closed;   // per local row: its closed word once closed in the lazy sweep
+    unsigned long long* closed;   // per row of the lazy sweep's row space: its closed word once closed
     uint32_t epoch;               // this launch's epoch in the closed words
+    // the row space of the lazy sweep with shortcuts: dp_rows rows at dpR, row
+    // r holding node r * dp_stride + dp_offset.  It is the relation itself
+    // (the local rows); on a row-sharded multi-GPU context it is every row of
+    // the relation in a scratch buffer (dp_copy), each rank closing all of
+    // them and copying its own rows (global r = lr * row_stride + row_offset)
+    // into the relation.
+    uint32_t* dpR;
+    int64_t dp_rows, dp_stride, dp_offset;
+    int dp_copy;
     int shortcut;              // lazy rows OR closed rows in (and run in descending order)
     FixState* st;
     int team;                  // warps per block
@@ -236,7 +245,7 @@ __device__ __forceinline__ void or_closed_rows(const FixArgs& a, bool has, int32
         while (m) {
             const int src = __ffs(m) - 1;
             m &= m - 1;
-            const uint32_t* srow = a.R + (int64_t)__shfl_sync(0xffffffffu, ly, src) * words;
+            const uint32_t* srow = a.dpR + (int64_t)__shfl_sync(0xffffffffu, ly, src) * words;
             const int l = max(__shfl_sync(0xffffffffu, lo, src), 0);
             const int h = min(__shfl_sync(0xffffffffu, hi, src), words);
             for (int w = l + lane; w < h; w += 32) row[w] |= __ldcg(srow + w);
@@ -267,7 +276,7 @@ __device__ __forceinline__ void or_closed_rows(const FixArgs& a, bool has, int32
             uint4 v[2][8];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const uint4* srow = reinterpret_cast<const uint4*>(a.R + (int64_t)max(sl[j], 0) * words);
+                const uint4* srow = reinterpret_cast<const uint4*>(a.dpR + (int64_t)max(sl[j], 0) * words);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int w = base + i * 128 + lane * 4;
@@ -343,7 +352,7 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
                     // after it: one round trip either way
                     A[k] = __ldg(&a.succ[2 * (int64_t)y]);
                     B[k] = __ldg(&a.succ[2 * (int64_t)y + 1]);
-                    if (dp) L[k] = local_row(a.rows, a.row_stride, a.row_offset, y);
+                    if (dp) L[k] = local_row(a.dp_rows, a.dp_stride, a.dp_offset, y);
                 }
             }
         }
@@ -572,13 +581,13 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
     const int32_t sentinel = (int32_t)(a.wpad * 32);
     const int32_t* succ32 = reinterpret_cast<const int32_t*>(a.succ);
     const unsigned lanes_below = (1u << lane) - 1u;
-    auto node_of = [&](unsigned long long i) { return (int64_t)(a.rows - 1 - (int64_t)i) * a.row_stride + a.row_offset; };
+    auto node_of = [&](unsigned long long i) { return (int64_t)(a.dp_rows - 1 - (int64_t)i) * a.dp_stride + a.dp_offset; };
     // successor slot `lane` (< 8) of row i's table entry, and its closed word
     auto slot_of = [&](unsigned long long i) {
-        return ((int64_t)i < a.rows && lane < 8) ? __ldg(succ32 + 8 * node_of(i) + lane) : -1;
+        return ((int64_t)i < a.dp_rows && lane < 8) ? __ldg(succ32 + 8 * node_of(i) + lane) : -1;
     };
     auto closed_of = [&](int32_t sl) {
-        const int32_t l = (sl >= 0 && sl < sentinel) ? local_row(a.rows, a.row_stride, a.row_offset, sl) : -1;
+        const int32_t l = (sl >= 0 && sl < sentinel) ? local_row(a.dp_rows, a.dp_stride, a.dp_offset, sl) : -1;
         return l >= 0 ? load_acquire_gpu(&a.closed[l]) : 0ull;
     };
     bool any = false;
@@ -593,19 +602,19 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
     __syncwarp();
     // the written row's closed word, published once every lane's stores of
     // the row are done (warp barrier, then a release store at GPU scope)
-    int64_t pub_r = -1;
+    int64_t pub_r = -1, pub_p = -1;
     unsigned long long pub_w = 0;
     auto publish = [&]() {
         __syncwarp();
         if (lane == 0 && pub_r >= 0) {
             store_release_gpu(&a.closed[pub_r], pub_w);
-            a.pending[pub_r] = INT32_MAX;
+            if (pub_p >= 0) a.pending[pub_p] = INT32_MAX;
         }
         pub_r = -1;
         __syncwarp();
     };
-    while ((int64_t)nb < a.rows) {
-        const int64_t r = a.rows - 1 - (int64_t)nb;
+    while ((int64_t)nb < a.dp_rows) {
+        const int64_t r = a.dp_rows - 1 - (int64_t)nb;
         const int64_t gx = node_of(nb);
         const int32_t tslot = t_next;
         const unsigned long long cw = cw_next;
@@ -615,7 +624,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         const bool more = __shfl_sync(0xffffffffu, tslot, 7) == -2;
         const int32_t s0 = (lane < 8 && tslot >= 0 && tslot < sentinel) ? tslot : -1;
         const bool f = s0 >= 0 && set_new(row, s0);
-        const int32_t l0 = f ? local_row(a.rows, a.row_stride, a.row_offset, s0) : -1;
+        const int32_t l0 = f ? local_row(a.dp_rows, a.dp_stride, a.dp_offset, s0) : -1;
         const unsigned fresh = __ballot_sync(0xffffffffu, f);
         int n_init = __popc(fresh);
         unsigned long long nb2 = 0;
@@ -658,14 +667,24 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
             __syncwarp();
             continue;
         }
-        // write the row back (emptying the row space); its nonzero range and popcount
-        uint32_t* grow = a.R + r * words;
+        // write the row back (emptying the row space); its nonzero range and
+        // popcount.  A copied row space also gives this rank's own rows to the
+        // relation (its pending word marks the local row closed).
+        uint32_t* grow = a.dpR + r * words;
+        uint32_t* own = nullptr;
+        int64_t lr = r;
+        if (a.dp_copy) {
+            const int64_t d = r - a.row_offset;
+            lr = (d >= 0 && d % a.row_stride == 0 && d / a.row_stride < a.rows) ? d / a.row_stride : -1;
+            if (lr >= 0) own = a.R + lr * words;
+        }
         int lo_w = INT32_MAX, hi_w = 0, pc = 0;
         if (vec) {
             for (int64_t w = lane * 4; w < words; w += 128) {
                 const uint4 t = *reinterpret_cast<const uint4*>(row + w);
                 *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
                 *reinterpret_cast<uint4*>(grow + w) = t;
+                if (own) *reinterpret_cast<uint4*>(own + w) = t;
                 const int c = __popc(t.x) + __popc(t.y) + __popc(t.z) + __popc(t.w);
                 if (c) {
                     pc += c;
@@ -678,6 +697,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
                 const uint32_t t = row[w];
                 row[w] = 0u;
                 grow[w] = t;
+                if (own) own[w] = t;
                 if (t) {
                     pc += __popc(t);
                     lo_w = min(lo_w, (int)w);
@@ -685,14 +705,12 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
                 }
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            lo_w = min(lo_w, __shfl_xor_sync(0xffffffffu, lo_w, o));
-            hi_w = max(hi_w, __shfl_xor_sync(0xffffffffu, hi_w, o));
-            pc += __shfl_xor_sync(0xffffffffu, pc, o);
-        }
+        lo_w = __reduce_min_sync(0xffffffffu, lo_w);
+        hi_w = __reduce_max_sync(0xffffffffu, hi_w);
+        pc = __reduce_add_sync(0xffffffffu, pc);
         any = any || pc > n_init;
         pub_r = r;
+        pub_p = lr;
         pub_w = lo_w < hi_w ? closed_word(a.epoch, lo_w, hi_w) : closed_word(a.epoch, 0, 0);
         publish();
     }
@@ -949,7 +967,7 @@ __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs
         __syncwarp();
         const int budget = a.team > 1 ? a.team_budget : 0;
         const bool grew = lazy && a.shortcut
-                              ? close_rows_dp(a, &a.st->next_row[s & 1], budget, row, spill, q, lane)
+                              ? close_rows_dp(a, &a.st->next_row[s & 1], a.dp_copy ? 0 : budget, row, spill, q, lane)
                               : close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, lazy, budget, row, spill, q,
                                            lane);
         if (lane == 0 && grew) *(volatile int*)&a.st->changed[s & 1] = 1;
@@ -1063,8 +1081,20 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // sweep ORs in closed rows (closed words of this launch's epoch)
     const bool lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp;
     const bool shortcut = lazy && words < (int64_t(1) << kClosedSpan);
+    // row-sharded on several GPUs: the lazy sweep closes every row of the
+    // relation in a scratch copy (a row's shortcuts read rows of every
+    // rank's share) and each rank keeps its own rows; only the changed word
+    // crosses GPUs
+    const bool sharded = R->shard == TL_SHARD_ROWS && c->world > 1;
+    const int64_t dp_rows = shortcut && sharded ? R->dims[0] : rows;
+    uint32_t* dpR = R->bits;
+    if (shortcut && sharded) {
+        void* ws = nullptr;
+        TL_TRY(workspace(c, (size_t)std::max<int64_t>(dp_rows, 1) * words * 4, &ws, WS_FIXPOINT));
+        dpR = static_cast<uint32_t*>(ws);
+    }
     if (shortcut) {
-        const size_t need = std::max<size_t>((size_t)rows * 8, 256);
+        const size_t need = std::max<size_t>((size_t)dp_rows * 8, 256);
         if (need > c->fix_closed_cap) {
             TL_CK(c, cudaStreamSynchronize(c->stream));
             cudaFree(c->fix_closed);
@@ -1111,7 +1141,8 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     const int64_t team_words = (int64_t)wpb * (int64_t)(per_warp / 4) - (2 * wpad + 4);
     int64_t qt = 1;
     while (qt * 2 <= team_words) qt *= 2;
-    int64_t grid = std::min<int64_t>((int64_t)c->sm_count * per_sm, std::max<int64_t>((rows + wpb - 1) / wpb, 1));
+    int64_t grid = std::min<int64_t>((int64_t)c->sm_count * per_sm,
+                                     std::max<int64_t>((std::max(rows, dp_rows) + wpb - 1) / wpb, 1));
 
     FixArgs a{};
     a.R = R->bits;
@@ -1132,6 +1163,9 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.shortcut = shortcut ? 1 : 0;
     a.closed = static_cast<unsigned long long*>(c->fix_closed);
     a.epoch = c->fix_epoch;
+    a.dpR = dpR;
+    a.dp_rows = dp_rows;
+    a.dp_copy = shortcut && sharded ? 1 : 0;
     // local row r is global row r * world + rank of a row-sharded relation
     a.row_stride = 1;
     a.row_offset = 0;
@@ -1139,6 +1173,9 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         a.row_stride = c->world;
         a.row_offset = c->rank;
     }
+    // the copied row space holds every node's row at its own index
+    a.dp_stride = a.dp_copy ? 1 : a.row_stride;
+    a.dp_offset = a.dp_copy ? 0 : a.row_offset;
     a.max_sweeps = max_sweeps;
     a.nblocks = (unsigned)grid;
     a.world = c->world;

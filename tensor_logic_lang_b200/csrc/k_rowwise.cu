@@ -10,9 +10,12 @@
 // read once and written once: the kernel is HBM-bound.  Softmax subtracts the
 // row maximum before exponentiating; exp(x - m) / sum exp(x - m) equals the
 // reference's unshifted quotient wherever its f64 sum is finite, and keeps
-// fp32 from overflowing for inputs above 88.  Rows longer than 2048 use a
-// block per row and re-read the row from L2.
+// fp32 from overflowing for inputs above 88.  Contiguous rows of 2049 to 8192
+// values are held in a block's registers instead (one HBM read per value);
+// longer or strided rows use a block per row and re-read the row from L2.
 #include <math.h>
+
+#include <algorithm>
 
 #include "tl_internal.h"
 
@@ -132,6 +135,70 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
     return r;
 }
 
+// Contiguous, 16-byte aligned rows of 2049 .. 8192 values: a block per row,
+// the row held in registers (VPT values per thread, 128-bit loads), so each
+// value is read from HBM once and written once; two block reductions.
+template <int VPT>
+__global__ void __launch_bounds__(256) k_row_cta(const __grid_constant__ RowPlan p) {
+    __shared__ float sh[32];
+    constexpr int NV = VPT / 4;
+    const int64_t L = p.len;
+    for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
+        int64_t ib, ob;
+        row_bases(p, r, &ib, &ob);
+        float4 v[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int64_t e = ((int64_t)i * blockDim.x + threadIdx.x) * 4;
+            v[i] = e < L ? __ldg(reinterpret_cast<const float4*>(p.in + ib + e)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        auto valid = [&](int i) { return ((int64_t)i * blockDim.x + threadIdx.x) * 4 < L; };
+        if (!p.lnorm) {
+            float m = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < NV; ++i)
+                if (valid(i)) m = fmaxf(fmaxf(m, fmaxf(v[i].x, v[i].y)), fmaxf(v[i].z, v[i].w));
+            m = block_reduce(m, true, sh);
+            if (m == -INFINITY || m != m) m = 0.f;
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                if (valid(i)) {
+                    v[i] = make_float4(__expf(v[i].x - m), __expf(v[i].y - m), __expf(v[i].z - m), __expf(v[i].w - m));
+                    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+                }
+            }
+            const float inv = 1.0f / block_reduce(s, false, sh);
+#pragma unroll
+            for (int i = 0; i < NV; ++i) v[i] = make_float4(v[i].x * inv, v[i].y * inv, v[i].z * inv, v[i].w * inv);
+        } else {
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i)
+                if (valid(i)) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+            const float mean = block_reduce(s, false, sh) / (float)L;
+            float q = 0.f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+                if (valid(i)) {
+                    const float a = v[i].x - mean, b = v[i].y - mean, c2 = v[i].z - mean, d = v[i].w - mean;
+                    q += (a * a + b * b) + (c2 * c2 + d * d);
+                }
+            }
+            const float rs = rsqrtf(block_reduce(q, false, sh) / (float)L + 1.0e-5f);
+#pragma unroll
+            for (int i = 0; i < NV; ++i)
+                v[i] = make_float4((v[i].x - mean) * rs, (v[i].y - mean) * rs, (v[i].z - mean) * rs, (v[i].w - mean) * rs);
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int64_t e = ((int64_t)i * blockDim.x + threadIdx.x) * 4;
+            if (e < L) *reinterpret_cast<float4*>(p.out + ob + e) = v[i];
+        }
+        __syncthreads();   // sh is reused by the next row's reductions
+    }
+}
+
 // Any row length or stride: a block per row, several passes over the row.
 __global__ void __launch_bounds__(256) k_row_block(const __grid_constant__ RowPlan p) {
     __shared__ float sh[32];
@@ -210,7 +277,11 @@ tl_status launch_rowwise(tl_ctx* c, const RowPlan& p) {
     }
     const double bytes = (double)p.rows * p.len * 8.0;
     LaunchScope L(c, p.lnorm ? "lnorm_rows" : "softmax_rows", bytes, (double)p.rows * p.len * 4.0);
-    if (!inside || p.len > 2048) {
+    if (vec && p.len > 2048 && p.len <= 8192) {
+        const int64_t blocks = std::min<int64_t>(std::max<int64_t>(p.rows, 1), (int64_t)c->sm_count * 8);
+        if (p.len <= 4096) k_row_cta<16><<<(unsigned)blocks, 256, 0, c->stream>>>(q);
+        else k_row_cta<32><<<(unsigned)blocks, 256, 0, c->stream>>>(q);
+    } else if (!inside || p.len > 2048) {
         int64_t blocks = p.rows < (int64_t)c->sm_count * 16 ? p.rows : (int64_t)c->sm_count * 16;
         k_row_block<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, c->stream>>>(q);
     } else if (p.len <= 32) launch_warp<1>(c, q, false);

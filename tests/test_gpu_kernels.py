@@ -113,7 +113,10 @@ def test_gemm_plain_store_epilogue(ctx, oracle_lib, case, monkeypatch):
 
 
 # ----------------------------------------------------------------------------- row-wise
-ROW_CASES = [(3, 10), (2048, 2048), (64, 1000), (5, 5000), (1024, 10), (7, 129)]
+# (6, 2052) .. (3, 8192): rows held in a block's registers; (2, 8196): the
+# multi-pass block path
+ROW_CASES = [(3, 10), (2048, 2048), (64, 1000), (5, 5000), (1024, 10), (7, 129), (6, 2052), (9, 4096),
+             (3, 8192), (2, 8196)]
 
 
 @pytest.mark.parametrize("rows,cols", ROW_CASES)
