@@ -713,18 +713,22 @@ __device__ __forceinline__ float seg_op(int op, float x) {
 // Row-wise segment copy: for each source row i (stride src_rs, len elements,
 // contiguous) and segment s, dst[i * dst_rs + s * dst_ss + j] = op_s(x[j]).
 // Serves both orientations: K-major copies of K-contiguous sources (rows = R)
-// and MN-major copies of MN-contiguous sources (rows = K).  A 2-D grid (row
-// chunks x rows) needs no index division; 128-bit loads and stores when every
-// stride and base is 16-byte aligned.
+// and MN-major copies of MN-contiguous sources (rows = K).  A block's 256
+// threads cover 256 / tpr rows of tpr threads each (tpr a power of two sized
+// to the row, so short rows do not leave most threads idle); a 2-D grid (row
+// chunks x row groups) needs no index division; 128-bit loads and stores when
+// every stride and base is 16-byte aligned.
 __global__ void __launch_bounds__(256) k_prep_rows(const float* __restrict__ S, int64_t src_rs, int64_t rows,
                                                    int64_t len, int nseg, unsigned ops, float sgn,
-                                                   float* __restrict__ D, int64_t dst_rs, int64_t dst_ss, int vec) {
-    for (int64_t i = blockIdx.y; i < rows; i += gridDim.y) {
+                                                   float* __restrict__ D, int64_t dst_rs, int64_t dst_ss, int vec,
+                                                   int tpr_log2) {
+    const int tpr = 1 << tpr_log2, rpb = 256 >> tpr_log2;
+    const int t = threadIdx.x & (tpr - 1);
+    for (int64_t i = (int64_t)blockIdx.y * rpb + (threadIdx.x >> tpr_log2); i < rows; i += (int64_t)gridDim.y * rpb) {
         const float* src = S + i * src_rs;
         float* dst = D + i * dst_rs;
         if (vec) {
-            for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; j < len;
-                 j += (int64_t)gridDim.x * blockDim.x * 4) {
+            for (int64_t j = ((int64_t)blockIdx.x * tpr + t) * 4; j < len; j += (int64_t)gridDim.x * tpr * 4) {
                 float4 x = *reinterpret_cast<const float4*>(src + j);
                 x.x *= sgn; x.y *= sgn; x.z *= sgn; x.w *= sgn;
                 for (int s = 0; s < nseg; ++s) {
@@ -734,7 +738,7 @@ __global__ void __launch_bounds__(256) k_prep_rows(const float* __restrict__ S, 
                 }
             }
         } else {
-            for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < len; j += (int64_t)gridDim.x * blockDim.x) {
+            for (int64_t j = (int64_t)blockIdx.x * tpr + t; j < len; j += (int64_t)gridDim.x * tpr) {
                 const float x = src[j] * sgn;
                 for (int s = 0; s < nseg; ++s) dst[s * dst_ss + j] = seg_op((ops >> (4 * s)) & 15, x);
             }
@@ -867,10 +871,19 @@ static bool launch_skinny(tl_ctx* c, const GemmPlan& p, tl_status* st) {
         dim3 g((unsigned)((p.M + rows - 1) / rows), (unsigned)((p.K + kw - 1) / kw));
         if (g.x > 2147483647u || g.y > 65535u) return false;
         if (g.y > 1 && !p.beta) {
-            GemmPlan z = p;   // zero C (a K = 0 pass), then add the partial sums
-            z.K = 0;
-            *st = launch_simt(c, z);
-            if (*st != TL_OK) return true;
+            // zero C (a memset when dense, else a K = 0 pass), then add the partial sums
+            if (p.scn == 1 && p.scm == p.N) {
+                const cudaError_t e = cudaMemsetAsync(p.C, 0, (size_t)p.M * p.N * sizeof(float), c->stream);
+                if (e != cudaSuccess) {
+                    *st = cuda_fail(c, e, "cudaMemsetAsync");
+                    return true;
+                }
+            } else {
+                GemmPlan z = p;
+                z.K = 0;
+                *st = launch_simt(c, z);
+                if (*st != TL_OK) return true;
+            }
         }
         const int vec = !mcont && (p.sam & 3) == 0 && ((uintptr_t)p.A & 15) == 0 ? 1 : 0;
         LaunchScope L(c, "gemm_skinny_fp32", (double)(p.M * p.K + p.K * p.N + p.M * p.N * (1 + p.beta)) * 4.0,
@@ -922,12 +935,16 @@ static tl_status launch_simt(tl_ctx* c, const GemmPlan& p) {
                   2.0 * p.M * p.N * p.K);
     dim3 grid((unsigned)((p.N + bn - 1) / bn), (unsigned)((p.M + SB_M - 1) / SB_M), (unsigned)splits);
     if (splits > 1 && !p.beta) {
-        // zero C first (a K = 0 pass), then add the partial tiles
-        GemmPlan z = p;
-        z.K = 0;
-        dim3 g1(grid.x, grid.y, 1);
-        if (bn == 16) k_gemm_simt<16><<<g1, 256, 0, c->stream>>>(z, sgn, mag, 0);
-        else k_gemm_simt<64><<<g1, 256, 0, c->stream>>>(z, sgn, mag, 0);
+        // zero C first (a memset when dense, else a K = 0 pass), then add the partial tiles
+        if (p.scn == 1 && p.scm == p.N) {
+            TL_CK(c, cudaMemsetAsync(p.C, 0, (size_t)p.M * p.N * sizeof(float), c->stream));
+        } else {
+            GemmPlan z = p;
+            z.K = 0;
+            dim3 g1(grid.x, grid.y, 1);
+            if (bn == 16) k_gemm_simt<16><<<g1, 256, 0, c->stream>>>(z, sgn, mag, 0);
+            else k_gemm_simt<64><<<g1, 256, 0, c->stream>>>(z, sgn, mag, 0);
+        }
     }
     if (bn == 16) k_gemm_simt<16><<<grid, 256, 0, c->stream>>>(p, sgn, mag, splits > 1 ? chunk : p.K);
     else k_gemm_simt<64><<<grid, 256, 0, c->stream>>>(p, sgn, mag, splits > 1 ? chunk : p.K);
@@ -990,9 +1007,13 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
             const bool vec = (len & 3) == 0 && (src_rs & 3) == 0 && (q->ld & 3) == 0 && (dst_ss & 3) == 0 &&
                              ((uintptr_t)src & 15) == 0 && ((uintptr_t)q->dst & 15) == 0;
             const int64_t per_row = vec ? (len + 3) / 4 : len;
-            dim3 g((unsigned)std::min<int64_t>((per_row + 255) / 256, 64), (unsigned)std::min<int64_t>(rows, 65535));
+            int tl = 0;   // threads per row: the power of two that covers the row, at most 256
+            while ((1 << tl) < per_row && tl < 8) ++tl;
+            const int64_t rpb = 256 >> tl;
+            dim3 g((unsigned)std::min<int64_t>((per_row + 255) / 256, 64),
+                   (unsigned)std::min<int64_t>((rows + rpb - 1) / rpb, 65535));
             k_prep_rows<<<g, 256, 0, c->stream>>>(src, src_rs, rows, len, nseg, q->ops, q->sgn, q->dst, q->ld, dst_ss,
-                                                  vec ? 1 : 0);
+                                                  vec ? 1 : 0, tl);
         } else {
             dim3 g((unsigned)((q->R + 31) / 32), (unsigned)((p.K + 31) / 32));
             k_prep_transpose<<<g, dim3(32, 8), 0, c->stream>>>(src, q->s_r, q->s_k, q->R, p.K, nseg, q->ops, q->sgn,
@@ -1019,9 +1040,15 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     const int kb_per_split = (num_kb + splits - 1) / splits;
     splits = (num_kb + kb_per_split - 1) / kb_per_split;
     if (splits > 1 && !p.beta) {
-        GemmPlan z = p;   // zero C (a K = 0 pass honours its strides), then add partial tiles
-        z.K = 0;
-        TL_TRY(launch_simt(c, z));
+        // zero C, then add the partial tiles: a memset when C is one dense
+        // block, else a K = 0 pass (it honours C's strides)
+        if (p.scn == 1 && p.scm == p.N) {
+            TL_CK(c, cudaMemsetAsync(p.C, 0, (size_t)p.M * p.N * sizeof(float), c->stream));
+        } else {
+            GemmPlan z = p;
+            z.K = 0;
+            TL_TRY(launch_simt(c, z));
+        }
     }
     TcEpi e;
     e.C = p.C; e.scm = p.scm; e.scn = p.scn;

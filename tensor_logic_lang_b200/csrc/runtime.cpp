@@ -570,6 +570,21 @@ extern "C" tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* 
     if (t->dims[1] > INT32_MAX) return fail(c, TL_ERR_UNSUPPORTED, "sparse column count exceeds int32");
     const bool sharded = t->shard == TL_SHARD_ROWS && c->world > 1;
     const int64_t lrows = dense_rows(c, t);
+    // large uploads build the CSR on the device; the host build below takes
+    // the rest (few entries, or a local row of more than 32 entries)
+    bool on_device = false;
+    TL_TRY(csr_from_coo_gpu(c, t, nnz, rows, cols, vals, lrows, &on_device));
+    if (on_device) {
+        t->csr_rows = lrows;
+        t->zero = false;
+        t->defined = true;
+        t->csr_valid = true;
+        t->csr_stamp = next_csr_stamp();
+        t->boolean = t->csr_nonneg && t->csr_ones;
+        t->dense_valid = t->bits_valid = t->csc_valid = false;
+        return TL_OK;
+    }
+    // counting sort of the entries by (local) row, stable in input order
     std::vector<int64_t> rowptr(lrows + 2, 0);
     for (int64_t e = 0; e < nnz; ++e) {
         if (rows[e] < 0 || rows[e] >= t->dims[0] || cols[e] < 0 || cols[e] >= t->dims[1])
@@ -578,36 +593,77 @@ extern "C" tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* 
         rowptr[(sharded ? rows[e] / c->world : rows[e]) + 1]++;
     }
     for (int64_t r = 0; r < lrows; ++r) rowptr[r + 1] += rowptr[r];
-    std::vector<int64_t> fillp(rowptr.begin(), rowptr.end() - 1);
-    std::vector<int32_t> col(rowptr[lrows]);
-    std::vector<int64_t> order(rowptr[lrows]);
-    for (int64_t e = 0; e < nnz; ++e) {
-        if (sharded && rows[e] % c->world != c->rank) continue;
-        const int64_t lr = sharded ? rows[e] / c->world : rows[e];
-        order[fillp[lr]++] = e;
+    const int64_t count = rowptr[lrows];
+    // the columns (and values) scattered to their rows in input order, so the
+    // per-row pass below reads contiguous memory
+    std::vector<int32_t> gcol(std::max<int64_t>(count, 1));
+    std::vector<float> gval(vals ? std::max<int64_t>(count, 1) : 0);
+    {
+        std::vector<int64_t> fillp(rowptr.begin(), rowptr.end() - 1);
+        for (int64_t e = 0; e < nnz; ++e) {
+            if (sharded && rows[e] % c->world != c->rank) continue;
+            const int64_t at = fillp[sharded ? rows[e] / c->world : rows[e]]++;
+            gcol[at] = (int32_t)cols[e];
+            if (vals) gval[at] = (float)vals[e];
+        }
     }
-    // sort each row by column, keep the last of duplicates (stable by input order)
-    std::vector<int64_t> out_ptr(lrows + 1, 0);
-    std::vector<int32_t> out_col;
-    std::vector<float> out_val;
-    out_col.reserve(order.size());
-    out_val.reserve(order.size());
+    // the CSR is assembled in the pinned staging buffer and copied from there:
+    // row pointers, then columns, then values (16-byte aligned sections)
+    const size_t ptr_b = ((size_t)(lrows + 1) * 8 + 15) & ~size_t(15);
+    const size_t col_b = ((size_t)count * 4 + 15) & ~size_t(15);
+    float* stage = nullptr;
+    TL_TRY(staging(c, ptr_b + col_b + (size_t)count * 4 + 16, &stage));
+    TL_CK(c, cudaStreamSynchronize(c->stream));   // earlier copies out of the staging buffer
+    int64_t* out_ptr = reinterpret_cast<int64_t*>(stage);
+    int32_t* out_col = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(stage) + ptr_b);
+    float* out_val = reinterpret_cast<float*>(reinterpret_cast<char*>(stage) + ptr_b + col_b);
+    // each row sorted by column (stable, so among repeats of a column the last
+    // entry of the input comes last and is the one kept)
     bool nonneg = true, ones = true, pos = true;
+    int64_t n = 0;
+    out_ptr[0] = 0;
+    std::vector<std::pair<int32_t, float>> longrow;
     for (int64_t r = 0; r < lrows; ++r) {
-        auto b = order.begin() + rowptr[r], en = order.begin() + rowptr[r + 1];
-        std::stable_sort(b, en, [&](int64_t x, int64_t y) { return cols[x] < cols[y]; });
-        for (auto it = b; it != en; ++it) {
-            if (it + 1 != en && cols[*(it + 1)] == cols[*it]) continue;
-            const float v = vals ? (float)vals[*it] : 1.0f;
+        int32_t* bc = gcol.data() + rowptr[r];
+        float* bv = vals ? gval.data() + rowptr[r] : nullptr;
+        const int64_t len = rowptr[r + 1] - rowptr[r];
+        if (len <= 32) {
+            for (int64_t i = 1; i < len; ++i) {
+                const int32_t kc = bc[i];
+                const float kv = bv ? bv[i] : 1.0f;
+                int64_t j = i - 1;
+                while (j >= 0 && bc[j] > kc) {
+                    bc[j + 1] = bc[j];
+                    if (bv) bv[j + 1] = bv[j];
+                    --j;
+                }
+                bc[j + 1] = kc;
+                if (bv) bv[j + 1] = kv;
+            }
+        } else {
+            longrow.resize(len);
+            for (int64_t i = 0; i < len; ++i) longrow[i] = {bc[i], bv ? bv[i] : 1.0f};
+            std::stable_sort(longrow.begin(), longrow.end(),
+                             [](const std::pair<int32_t, float>& x, const std::pair<int32_t, float>& y) {
+                                 return x.first < y.first;
+                             });
+            for (int64_t i = 0; i < len; ++i) {
+                bc[i] = longrow[i].first;
+                if (bv) bv[i] = longrow[i].second;
+            }
+        }
+        for (int64_t i = 0; i < len; ++i) {
+            if (i + 1 < len && bc[i + 1] == bc[i]) continue;
+            const float v = bv ? bv[i] : 1.0f;
             nonneg = nonneg && v >= 0.0f;
             pos = pos && v > 0.0f;
             ones = ones && v == 1.0f;
-            out_col.push_back((int32_t)cols[*it]);
-            out_val.push_back(v);
+            out_col[n] = bc[i];
+            out_val[n] = v;
+            ++n;
         }
-        out_ptr[r + 1] = (int64_t)out_col.size();
+        out_ptr[r + 1] = n;
     }
-    const int64_t n = (int64_t)out_col.size();
     if (n > t->csr_cap || !t->rowptr || t->csr_rows != lrows) {
         cudaFree(t->rowptr); cudaFree(t->colidx); cudaFree(t->vals);
         t->rowptr = nullptr; t->colidx = nullptr; t->vals = nullptr;
@@ -617,12 +673,14 @@ extern "C" tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* 
         TL_CK(c, cudaMalloc(&t->vals, cap * sizeof(float)));
         t->csr_cap = cap;
     }
-    TL_CK(c, cudaMemcpyAsync(t->rowptr, out_ptr.data(), (lrows + 1) * 8, cudaMemcpyHostToDevice, c->stream));
+    // copies from pinned memory; waited for here, since the staging buffer is
+    // shared by every context of this host thread
+    TL_CK(c, cudaMemcpyAsync(t->rowptr, out_ptr, (lrows + 1) * 8, cudaMemcpyHostToDevice, c->stream));
     if (n) {
-        TL_CK(c, cudaMemcpyAsync(t->colidx, out_col.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
-        TL_CK(c, cudaMemcpyAsync(t->vals, out_val.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+        TL_CK(c, cudaMemcpyAsync(t->colidx, out_col, n * 4, cudaMemcpyHostToDevice, c->stream));
+        TL_CK(c, cudaMemcpyAsync(t->vals, out_val, n * 4, cudaMemcpyHostToDevice, c->stream));
     }
-    TL_CK(c, cudaStreamSynchronize(c->stream));  // the host vectors die here
+    TL_CK(c, cudaStreamSynchronize(c->stream));
     t->nnz = n;
     t->csr_rows = lrows;
     t->zero = false;

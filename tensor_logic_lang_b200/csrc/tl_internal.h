@@ -306,6 +306,10 @@ tl_status launch_dense_to_bits(tl_ctx* c, Tensor* t);
 tl_status launch_bits_to_dense(tl_ctx* c, Tensor* t);
 tl_status launch_dense_to_csr(tl_ctx* c, Tensor* t);
 tl_status launch_closure_right(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed, int sweep);
+// t's CSR built on the device from COO entries (k_csr.cu); *handled = false
+// when the host build has to take it
+tl_status csr_from_coo_gpu(tl_ctx* c, Tensor* t, int64_t nnz, const int64_t* rows, const int64_t* cols,
+                           const double* vals, int64_t lrows, bool* handled);
 tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed);
 // every right-form sweep of a fixpoint in one cooperative launch; *handled is
 // false when the shapes or the context do not allow it (the caller then runs

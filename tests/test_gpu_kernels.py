@@ -259,6 +259,30 @@ def test_closure_explicit_zero_edges(ctx, oracle_lib):
     np.testing.assert_array_equal(ctx.tensor("Reach"), ref.tensor("Reach"))
 
 
+@pytest.mark.parametrize("long_row", [False, True])
+def test_sparse_upload_device_build(ctx, oracle_lib, long_row):
+    # unsorted COO entries with repeated (row, column) pairs, the last value
+    # counting; zero and negative values; long_row puts more than 32 entries in
+    # one row, which sends the upload to the host build
+    n, m = 600, 5000
+    rng = np.random.default_rng(41)
+    rows = rng.integers(0, n, m)
+    cols = rng.integers(0, n, m)
+    if long_row:
+        rows[:200] = 7
+    rows = np.concatenate([rows, rows[:300]])
+    cols = np.concatenate([cols, cols[:300]])
+    vals = rng.normal(size=len(rows))
+    vals[::17] = 0.0
+    src = decl(i=n, j=n) + "sparse A[i, j]\nB[i,j] = A[i,j]\n"
+    ref = both(ctx, oracle_lib, src, sparse={"A": (rows, cols, vals)})
+    D = np.zeros((n, n))
+    for r, c, v in zip(rows, cols, vals):
+        D[r, c] = v   # in input order: the last entry of a pair stays
+    np.testing.assert_array_equal(ctx.tensor("B"), D.astype(np.float32).astype(np.float64))
+    np.testing.assert_allclose(ref.tensor("B"), D, rtol=1e-7, atol=0)
+
+
 def test_closure_one_launch_matches_per_sweep(ctx, oracle_lib, monkeypatch):
     # the one-launch fixpoint and the per-sweep launches give the same bits and sweeps
     n = 2048
