@@ -35,45 +35,71 @@ __global__ void k_coo_count(const int64_t* __restrict__ rows, const int64_t* __r
     }
 }
 
-// out[i] = sum of cnt[0 .. i) for i <= n (out[n] = the total), by one block:
-// each thread scans a contiguous chunk, the chunk totals are scanned in
-// shared memory.  Also the largest count into *max_out (when given).
+// out[i] = sum of cnt[0 .. i) for i <= n (out[n] = the total), by one block,
+// tile by tile: each thread loads 4 consecutive counts (one 16-byte load per
+// lane, a warp reads 512 contiguous bytes), a warp scan and a scan of the 32
+// warp totals give every thread its exclusive prefix, and a running carry
+// links the tiles.  Also the largest count into *max_out (when given).
 __global__ void __launch_bounds__(kScanThreads) k_scan_counts(const int* __restrict__ cnt, int64_t n,
                                                               int64_t* __restrict__ out, int* __restrict__ max_out) {
-    __shared__ int64_t part[kScanThreads];
-    __shared__ int mx[kScanThreads / 32];
-    const int t = threadIdx.x;
-    const int64_t chunk = (n + kScanThreads - 1) / kScanThreads;
-    const int64_t b = (int64_t)t * chunk, e = b + chunk < n ? b + chunk : n;
-    int64_t s = 0;
+    static_assert(kScanThreads == 1024, "one warp scans the 32 warp totals");
+    __shared__ int64_t wsum[32];
+    __shared__ int wmax[32];
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    constexpr int PER = 4;
+    int64_t carry = 0;
     int m = 0;
-    for (int64_t i = b; i < e; ++i) {
-        s += cnt[i];
-        m = max(m, cnt[i]);
-    }
-    part[t] = s;
+    for (int64_t base = 0; base < n; base += (int64_t)kScanThreads * PER) {
+        const int64_t i0 = base + (int64_t)t * PER;
+        int v[PER] = {0, 0, 0, 0};
+        if (i0 + PER <= n && ((reinterpret_cast<uintptr_t>(cnt + i0) & 15) == 0)) {
+            const int4 q = *reinterpret_cast<const int4*>(cnt + i0);
+            v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+        } else {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((t & 31) == 0) mx[t >> 5] = m;
-    __syncthreads();
-    // inclusive scan of the chunk totals (Hillis-Steele over shared memory)
-    for (int o = 1; o < kScanThreads; o <<= 1) {
-        const int64_t v = t >= o ? part[t - o] : 0;
-        __syncthreads();
-        part[t] += v;
-        __syncthreads();
-    }
-    int64_t run = t > 0 ? part[t - 1] : 0;
-    for (int64_t i = b; i < e; ++i) {
-        out[i] = run;
-        run += cnt[i];
-    }
-    if (t == kScanThreads - 1) out[n] = part[t];
-    if (max_out && t < 32) {
-        int v = t < kScanThreads / 32 ? mx[t] : 0;
+            for (int k = 0; k < PER; ++k) v[k] = i0 + k < n ? cnt[i0 + k] : 0;
+        }
+        const int64_t s = (int64_t)v[0] + v[1] + v[2] + v[3];
+        m = max(m, max(max(v[0], v[1]), max(v[2], v[3])));
+        int64_t x = s;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (t == 0) *max_out = v;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[w] = x;
+        __syncthreads();
+        if (w == 0) {
+            int64_t y = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int64_t z = __shfl_up_sync(0xffffffffu, y, o);
+                if (lane >= o) y += z;
+            }
+            wsum[lane] = y;
+        }
+        __syncthreads();
+        int64_t run = carry + (w > 0 ? wsum[w - 1] : 0) + (x - s);
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            if (i0 + k < n) out[i0 + k] = run;
+            run += v[k];
+        }
+        carry += wsum[31];
+        __syncthreads();   // wsum is rewritten by the next tile
+    }
+    if (t == 0) out[n] = carry;
+    if (max_out) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) wmax[w] = m;
+        __syncthreads();
+        if (w == 0) {
+            int v = wmax[lane];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (lane == 0) *max_out = v;
+        }
     }
 }
 
