@@ -34,6 +34,10 @@ sys.path.insert(0, REPO)
 N_CLOSURE = 32768
 DEG_CLOSURE = 4
 METRIC = "closure_fixpoint_iters_per_s"
+# DRAM bytes one launch of the one-launch fixpoint moves on this workload at
+# N = 1 (dram__bytes_read.sum + dram__bytes_write.sum of an ncu capture:
+# 2.3 MB read, 79.4 MB written; the rest of the rows stay in L2)
+CLOSURE_TRAFFIC_1GPU = 81.7e6
 UNIT = "sweeps/s"
 
 
@@ -287,7 +291,8 @@ def run_closure(args, dist, peaks):
     achieved = algo_bytes / (per_launch_ms / 1e3) / 1e9
     roof = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks[0],
             "unit": "GB/s", "frac": round(achieved / peaks[0], 4), "peak_source": peaks[2],
-            "traffic": None, "algo_bytes_per_launch": algo_bytes, "avg_launch_ms": per_launch_ms,
+            "traffic": CLOSURE_TRAFFIC_1GPU if dist.world == 1 and kname == "closure_fixpoint" else None,
+            "algo_bytes_per_launch": algo_bytes, "avg_launch_ms": per_launch_ms,
             "sweeps_per_launch": sweeps if kname == "closure_fixpoint" else 1,
             "share_of_step": round(st["total_ms"] / max(ms, 1e-9), 3),
             # the launch's phases from the device clock (rows of each sweep,
