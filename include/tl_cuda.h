@@ -236,6 +236,10 @@ tl_status tl_comm_unique_id(uint8_t id[128]);
 tl_status tl_program_run(tl_ctx* ctx, const tl_statement* stmts, int32_t n_stmts);
 
 /* Sweeps the last fixpoint of tl_program_run took (the reference's `iter`). */
+/* tl_program_run does not wait for a one-launch closure fixpoint on one     */
+/* GPU; this call (like tl_sync) waits for it and reads its sweep count.     */
+/* A failure of that launch (a bounded device wait that ran out) is          */
+/* reported by the next tl_sync or tl_program_run.                           */
 int32_t tl_last_sweeps(const tl_ctx* ctx);
 
 /* ------------------------------------------------------------------------ */

@@ -1020,9 +1020,11 @@ size_t fix_smem_per_warp(int64_t words) {
 
 }  // namespace
 
-tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweeps, int* sweeps_out,
+tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweeps, bool need_now, int* sweeps_out,
                                   bool* changed_out, bool* handled) {
     *handled = false;
+    // the previous launch's result first (its control block shares the pinned slot)
+    TL_TRY(fix_resolve(c));
     constexpr size_t kSmemCap = 200 * 1024;
     const int64_t words = R->bits_words, rows = R->bits_rows;
     const int64_t wpad = (words + 3) & ~int64_t(3);
@@ -1192,14 +1194,37 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
                                              per_warp * wpb, c->stream));
         TL_TRY(L.done());
     }
-    FixState h{};
+    // the control block comes back to pinned memory behind the launch; it is
+    // read at once only when the caller needs the sweep count, when profiling
+    // (the phase marks), or on several GPUs (the peer token count must be
+    // known before the next launch); otherwise when the context next syncs,
+    // asks for the sweep count or launches another fixpoint
     TL_CK(c, cudaMemcpyAsync(c->h_flags + 32, c->fix_state, sizeof(FixState), cudaMemcpyDeviceToHost, c->stream));
-    TL_CK(c, cudaStreamSynchronize(c->stream));
+    if (!c->fix_event) TL_CK(c, cudaEventCreateWithFlags(&c->fix_event, cudaEventDisableTiming));
+    TL_CK(c, cudaEventRecord(c->fix_event, c->stream));
+    c->fix_pending = true;
+    c->fix_prof = c->prof;
+    c->fix_sweep_bytes = sweep_bytes;
+    R->lazy_src = nullptr;   // every row is written now (or the status of the launch says why not)
+    *sweeps_out = -1;
+    *changed_out = false;
+    if (!need_now && !c->prof && c->world == 1) return TL_OK;
+    TL_TRY(fix_resolve(c));
+    *sweeps_out = c->last_sweeps;
+    *changed_out = c->fix_last_changed;
+    return TL_OK;
+}
+
+tl_status fix_resolve(tl_ctx* c) {
+    if (!c->fix_pending) return TL_OK;
+    c->fix_pending = false;
+    TL_CK(c, cudaEventSynchronize(c->fix_event));
+    FixState h{};
     memcpy(&h, c->h_flags + 32, sizeof(FixState));
     // algorithmic bytes of the launch: every sweep reads and writes the rows
-    if (c->prof && !c->pending.empty() && c->pending.back().name == "closure_fixpoint")
-        c->pending.back().bytes = sweep_bytes * std::max(h.sweeps, 1);
-    if (c->prof) {
+    if (c->fix_prof && !c->pending.empty() && c->pending.back().name == "closure_fixpoint")
+        c->pending.back().bytes = c->fix_sweep_bytes * std::max(h.sweeps, 1);
+    if (c->fix_prof) {
         // phases of the launch from the device's own clock: each sweep's row
         // work (until the last block is done) and its settling (barrier and,
         // on several GPUs, the wait for the other ranks)
@@ -1224,15 +1249,15 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         }
     }
     if (c->world > 1) c->peer_tokens += (unsigned long long)h.sweeps;
+    c->last_sweeps = h.sweeps;
+    c->fix_last_changed = h.last_changed != 0;
     if (h.err) {
         if (c->world > 1) c->peer_state = -1;   // ranks may disagree on the token count now
         return fail(c, h.err == 2 ? TL_ERR_COMM : TL_ERR_CUDA,
                     "closure fixpoint: %s wait ran out after %d sweeps", h.err == 2 ? "peer" : "grid barrier",
                     h.sweeps);
     }
-    R->lazy_src = nullptr;   // every row is written now
-    *sweeps_out = h.sweeps;
-    *changed_out = h.last_changed != 0;
+    if (c->fix_last_changed) fail(c, TL_OK, "fixpoint stopped at the %d-sweep cap", h.sweeps);
     return TL_OK;
 }
 

@@ -936,12 +936,12 @@ static tl_status run_fixpoint(tl_ctx* c, const tl_equation* eqs, int n, int32_t*
         // rows left unwritten by step(E) are built by the one-launch fixpoint
         if (!(R->bits_valid && R->lazy_src == E)) TL_TRY(ensure_bits(c, R));
         bool handled = false;
-        TL_TRY(launch_closure_fixpoint(c, R, E, max_sweeps, &sweeps, &changed, &handled));
+        // the sweep count (and the note at the cap) is set when the launch's
+        // result is read: now if the caller wants it, else at the next sync
+        TL_TRY(launch_closure_fixpoint(c, R, E, max_sweeps, sweeps_out != nullptr, &sweeps, &changed, &handled));
         if (handled) {
             mark_written_bits(R);
-            c->last_sweeps = sweeps;
             if (sweeps_out) *sweeps_out = sweeps;
-            if (changed) fail(c, TL_OK, "fixpoint stopped at the %d-sweep cap", sweeps);
             return TL_OK;
         }
     }
@@ -1310,6 +1310,7 @@ static tl_status run_as_graph(tl_ctx* c, const tl_statement* s, int n, const std
 extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n) {
     if (!c || (n > 0 && !s)) return TL_ERR_INVALID;
     TL_CK(c, cudaSetDevice(c->device));
+    TL_TRY(fix_resolve(c));   // an earlier run's fixpoint result, before last_sweeps is reset
     c->err.clear();
     c->query_out.clear();
     c->domains.clear();   // a program's domains are its own (llvm.zig:133-140)

@@ -335,6 +335,7 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     cudaFree(c->aux);
     cudaFree(c->fix_state);
     cudaFree(c->fix_closed);
+    if (c->fix_event) cudaEventDestroy(c->fix_event);
     cudaFree(c->d_flags);
     cudaFreeHost(c->h_flags);
     cudaStreamDestroy(c->stream);
@@ -366,10 +367,17 @@ extern "C" tl_status tl_sync(tl_ctx* c) {
     if (!c) return TL_ERR_INVALID;
     TL_CK(c, cudaStreamSynchronize(c->stream));
     TL_CK(c, cudaGetLastError());
+    TL_TRY(fix_resolve(c));
     return check_device_flags(c);
 }
 
-extern "C" int32_t tl_last_sweeps(const tl_ctx* c) { return c ? c->last_sweeps : 0; }
+extern "C" int32_t tl_last_sweeps(const tl_ctx* c) {
+    if (!c) return 0;
+    // a fixpoint result still in flight is read here (cached state of the context)
+    tl_ctx* m = const_cast<tl_ctx*>(c);
+    fix_resolve(m);
+    return m->last_sweeps;
+}
 extern "C" int64_t tl_launch_count(const tl_ctx* c) { return c ? c->launches : 0; }
 extern "C" void* tl_stream(const tl_ctx* c) { return c ? (void*)c->stream : nullptr; }
 

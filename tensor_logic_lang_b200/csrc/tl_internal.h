@@ -150,6 +150,10 @@ struct tl_ctx {
     int fix_shape_teams = -1, fix_wpb = 0, fix_per_sm = 0;
     // a tensor-core GEMM was given the device error word since it was last read
     bool flags_armed = false;
+    // a closure fixpoint whose control block has not been read yet (fix_resolve)
+    bool fix_pending = false, fix_prof = false, fix_last_changed = false;
+    double fix_sweep_bytes = 0;
+    cudaEvent_t fix_event = nullptr;
     // captured program runs (most recently used last)
     std::vector<tl::GraphEntry> graphs;
     uint64_t graph_clock = 0;
@@ -314,8 +318,12 @@ tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed);
 // every right-form sweep of a fixpoint in one cooperative launch; *handled is
 // false when the shapes or the context do not allow it (the caller then runs
 // one launch per sweep)
-tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweeps, int* sweeps_out,
+// One-launch closure fixpoint.  need_now: the sweep count is wanted at once;
+// otherwise, on one GPU, it may stay pending (sweeps_out = -1) until
+// fix_resolve, which the next sync, sweep-count query or fixpoint calls.
+tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweeps, bool need_now, int* sweeps_out,
                                   bool* changed_out, bool* handled);
+tl_status fix_resolve(tl_ctx* c);
 uint64_t next_csr_stamp();
 // multi-GPU fixpoint flags over peer memory (comm.cpp); collective over all ranks
 tl_status comm_peer_setup(tl_ctx* c);
