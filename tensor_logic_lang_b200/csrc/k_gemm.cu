@@ -131,10 +131,13 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const __grid_constant__ GemmP
 //
 // k_skinny_kcont, A's k contiguous: a block owns 32 rows (4 per warp) and a
 // 512-wide K range.  B's slice is staged n-major, so lane l reads column n at
-// k = 4l .. 4l+3 with one conflict-free 128-bit load shared by the warp's 4
-// rows; each lane keeps 8 128-bit loads of A in flight, and the warp reduces
-// its sums at the end.
-constexpr int SKC_RPW = 4, SKC_ROWS = 8 * SKC_RPW, SKC_K = 512;
+// k = 4l .. 4l+3 with one 128-bit load shared by the warp's 4 rows (rows of
+// the slice padded by 4 floats, so the staging stores spread over the banks);
+// each lane keeps 8 128-bit loads of A in flight, and the warp reduces its 64
+// sums (4 rows x 16 columns) with a transpose-reduction: 5 shuffle levels
+// that each halve the values a lane keeps (62 shuffles), after which lane l
+// holds sums 2l and 2l + 1.
+constexpr int SKC_RPW = 4, SKC_ROWS = 8 * SKC_RPW, SKC_K = 512, SKC_PAD = 4;
 // k_skinny_mcont, A's rows contiguous (a transposed activation): lane = row,
 // a block owns 32 rows and a 256-wide K range, warp w takes k = w, w + 8, ...
 // (32 loads in flight per lane), B's slice is staged k-major (broadcast
@@ -173,7 +176,7 @@ __device__ __forceinline__ void stage_b(const GemmPlan& p, int64_t k0, int kn, F
 }
 
 __global__ void __launch_bounds__(256) k_skinny_kcont(const __grid_constant__ GemmPlan p, int vec) {
-    __shared__ __align__(16) float Bt[16][SKC_K];
+    __shared__ __align__(16) float Bt[16][SKC_K + SKC_PAD];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t m0 = (int64_t)blockIdx.x * SKC_ROWS + w * SKC_RPW;
     const int64_t kc = (int64_t)blockIdx.y * SKC_K;
@@ -222,19 +225,28 @@ __global__ void __launch_bounds__(256) k_skinny_kcont(const __grid_constant__ Ge
             }
         }
     }
+    static_assert(SKC_RPW * 16 == 64, "the transpose-reduction takes 64 sums per lane");
+    float v[64];
 #pragma unroll
     for (int r = 0; r < SKC_RPW; ++r)
 #pragma unroll
-        for (int nn = 0; nn < 16; ++nn) {
-            if (nn >= p.N) break;
+        for (int nn = 0; nn < 16; ++nn) v[r * 16 + nn] = acc[r][nn];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc[r][nn] += __shfl_xor_sync(0xffffffffu, acc[r][nn], o);
+    for (int o = 16, cnt = 32; o >= 1; o >>= 1, cnt >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < cnt; ++i) {
+            const float send = upper ? v[i] : v[i + cnt];
+            const float keep = upper ? v[i + cnt] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
+    }
+    // lane l: sums 2l and 2l + 1 of the flattened (row, column) order
 #pragma unroll
-    for (int r = 0; r < SKC_RPW; ++r)
-#pragma unroll
-        for (int nn = 0; nn < 16; ++nn)
-            if (lane == nn) skinny_put(p, m0 + r, nn, acc[r][nn], gridDim.y > 1);
+    for (int j = 0; j < 2; ++j) {
+        const int idx = 2 * lane + j;
+        skinny_put(p, m0 + idx / 16, idx % 16, v[j], gridDim.y > 1);
+    }
 }
 
 __global__ void __launch_bounds__(256) k_skinny_mcont(const __grid_constant__ GemmPlan p) {
