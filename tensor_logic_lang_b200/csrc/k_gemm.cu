@@ -471,6 +471,7 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
@@ -779,6 +780,309 @@ __global__ void k_prep_transpose(const float* __restrict__ S, int64_t s_r, int64
     }
 }
 
+// ============================================================================
+// Attention block: S = scale Q K^T, A = softmax over keys, O = A V (d = 64)
+// ============================================================================
+// The three equations of an attention block (softmax.zig:19-229 between two
+// einsum contractions, einsum.zig:20-254) as two kernels, Scores and Attn
+// still written in full:
+//  * k_attn_tile, one CTA per (128 queries, 128 keys) tile: TMA brings the
+//    Q, K and V tiles into shared memory, where the softmax warps round them
+//    to TF32 (nearest) in place; one elected thread issues S = Q K^T with
+//    tcgen05.mma into TMEM; the four softmax warps read S back (a row per
+//    thread), store scale * S through the TMA, take the row maximum m and
+//    sum l of exp(S - m) over the tile's keys, and write P = exp(S - m)
+//    (TF32) into shared memory in the 128-byte-swizzled K-major layout the
+//    tensor cores read (over Q and K, done with by then); O_tile = P V goes
+//    into TMEM with a second tcgen05.mma and is stored unnormalised with m and
+//    l.  97 KB of shared memory: two CTAs per SM.
+//  * k_attn_combine, a warp per query row: m* = max of the tiles' m, l* = sum
+//    of exp(m - m*) l, O = sum of exp(m - m*) O_tile / l*, and the row of A =
+//    exp(S - m*) / l* from the stored scores.
+// The softmax subtracts the row maximum, as the row-wise kernel does; the
+// quotient equals the reference's exp(x) / sum exp(x) wherever its sum is
+// finite.
+constexpr int AT_ROWS = 128, AT_KEYS = 128, AT_D = 64, AT_THREADS = 192;
+constexpr int AT_Q = 0, AT_K = 32768, AT_V = 65536, AT_P = 0, AT_BAR = 98304;   // P over Q and K
+constexpr int AT_SMEM = AT_BAR + 256 + 1024;   // + barriers, + alignment slack
+constexpr uint32_t AT_TMEM_COLS = 256;          // S in columns 0..127, O in 128..191
+
+struct AttnArgs {
+    float* S;             // scores, row-major with row stride ls
+    int64_t ls;
+    int64_t n_q;          // queries (rows of Q, S, O)
+    float scale;          // the equation's literal factor on Q K^T
+    float* opart;         // [key tiles][n_q][64]: P V of each key tile, unnormalised
+    float* mpart;         // [key tiles][n_q]: row maximum of scale * S over the tile
+    float* lpart;         // [key tiles][n_q]: row sum of exp(scale * S - m) over the tile
+    int* err;             // a bounded pipeline wait ran out
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Every fp32 of [base, base + bytes) rounded to TF32 in place by nthreads threads.
+__device__ __forceinline__ void round_tf32_inplace(uint8_t* base, int bytes, int t, int nthreads) {
+    for (int off = t * 16; off < bytes; off += nthreads * 16) {
+        float4 v = *reinterpret_cast<float4*>(base + off);
+        v.x = tf32_rna(v.x); v.y = tf32_rna(v.y); v.z = tf32_rna(v.z); v.w = tf32_rna(v.w);
+        *reinterpret_cast<float4*>(base + off) = v;
+    }
+}
+
+__global__ void __launch_bounds__(AT_THREADS, 2)
+    k_attn_tile(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmS,
+                const __grid_constant__ AttnArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 0: Q, K landed  1: V landed  2: Q, K rounded  3: V rounded  4: S done  5: P written  6: O done
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + AT_BAR);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 8);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int m0 = blockIdx.x * AT_ROWS, n0 = blockIdx.y * AT_KEYS;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1); mbar_init(&bar[1], 1);
+        mbar_init(&bar[2], 128); mbar_init(&bar[3], 128);
+        mbar_init(&bar[4], 1); mbar_init(&bar[5], 128); mbar_init(&bar[6], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(AT_TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA: Q and K as two 32-wide K-major blocks each, V
+        // as four 32-key blocks of two 32 x 32 MN-major boxes ----------------
+        if (lane == 0) {
+            mbar_expect_tx(&bar[0], 4 * 16384);
+            tma_load_2d(smem + AT_Q, &tmQ, &bar[0], 0, m0);
+            tma_load_2d(smem + AT_Q + 16384, &tmQ, &bar[0], 32, m0);
+            tma_load_2d(smem + AT_K, &tmK, &bar[0], 0, n0);
+            tma_load_2d(smem + AT_K + 16384, &tmK, &bar[0], 32, n0);
+            mbar_expect_tx(&bar[1], 8 * 4096);
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+                    tma_load_2d(smem + AT_V + kb * 8192 + j * 4096, &tmV, &bar[1], 32 * j, n0 + 32 * kb);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        constexpr uint32_t idesc_s = (1u << 4) | (2u << 7) | (2u << 10)           // D f32, A, B tf32
+                                     | ((uint32_t)(AT_KEYS >> 3) << 17) | ((uint32_t)(AT_ROWS >> 4) << 24);
+        constexpr uint32_t idesc_o = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16)   // B MN-major
+                                     | ((uint32_t)(AT_D >> 3) << 17) | ((uint32_t)(AT_ROWS >> 4) << 24);
+        bool ok = mbar_wait(&bar[2], 0, a.err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (ok && lane == 0) {
+#pragma unroll
+            for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t ad = umma_desc(smem_u32(smem + AT_Q + kb * 16384) + kk * 32, 16, 1024, kLayoutSW128);
+                    const uint64_t bd = umma_desc(smem_u32(smem + AT_K + kb * 16384) + kk * 32, 16, 1024, kLayoutSW128);
+                    umma_tf32(tmem, ad, bd, idesc_s, (kb > 0 || kk > 0) ? 1u : 0u);
+                }
+            umma_commit(&bar[4]);
+        }
+        __syncwarp();
+        ok = ok && mbar_wait(&bar[3], 0, a.err) && mbar_wait(&bar[5], 0, a.err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (ok && lane == 0) {
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t ad = umma_desc(smem_u32(smem + AT_P + kb * 16384) + kk * 32, 16, 1024, kLayoutSW128);
+                    const uint64_t bd =
+                        umma_desc(smem_u32(smem + AT_V + kb * 8192) + kk * 1024, 4096, 512, kLayoutSW128Base32B);
+                    umma_tf32(tmem + AT_KEYS, ad, bd, idesc_o, (kb > 0 || kk > 0) ? 1u : 0u);
+                }
+            umma_commit(&bar[6]);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- softmax warps: a row per thread ----------------
+        const int t = threadIdx.x - 64;
+        const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int row = q * 32 + lane;          // row of the tile = TMEM lane
+        bool ok = mbar_wait(&bar[0], 0, a.err);
+        if (ok) round_tf32_inplace(smem + AT_Q, 4 * 16384, t, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(&bar[2]);
+        ok = ok && mbar_wait(&bar[1], 0, a.err);
+        if (ok) round_tf32_inplace(smem + AT_V, 8 * 4096, t, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(&bar[3]);
+        ok = ok && mbar_wait(&bar[4], 0, a.err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        float s[AT_KEYS];
+#pragma unroll
+        for (int ch = 0; ch < AT_KEYS / 16; ++ch) tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + ch * 16, s + 16 * ch);
+#pragma unroll
+        for (int i = 0; i < AT_KEYS; ++i) s[i] *= a.scale;
+        // the Scores tile through the TMA: this warp's 32 rows staged, 32
+        // columns per swizzled 4 KB tile, in the warp's own 16 KB of the P
+        // space (over Q and K, free once S is done); P goes there after the
+        // stores have read it
+        uint8_t* stage = smem + AT_P + q * 16384;
+#pragma unroll
+        for (int ch = 0; ch < AT_KEYS / 32; ++ch) {
+            uint8_t* sc = stage + ch * 4096;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<float4*>(sc + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                    make_float4(s[32 * ch + 4 * j], s[32 * ch + 4 * j + 1], s[32 * ch + 4 * j + 2], s[32 * ch + 4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && ok) {
+#pragma unroll
+            for (int ch = 0; ch < AT_KEYS / 32; ++ch) tma_store_2d(&tmS, stage + ch * 4096, n0 + ch * 32, m0 + q * 32);
+            bulk_commit();
+        }
+        // the tile's row statistics and P = exp(S - m), TF32, into the
+        // K-major swizzled operand layout: 32-key block kb, 16-byte chunk j
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < AT_KEYS; ++i) mx = fmaxf(mx, s[i]);
+        if (mx == -INFINITY || mx != mx) mx = 0.f;
+        float l = 0.f;
+#pragma unroll
+        for (int i = 0; i < AT_KEYS; ++i) {
+            s[i] = __expf(s[i] - mx);
+            l += s[i];
+        }
+        // every warp's Scores stores have read their staging tiles (a warp's
+        // staging space is one whole 32-key block of P, which holds P rows of
+        // all four warps)
+        if (lane == 0) bulk_wait_read_0();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+        for (int kb = 0; kb < AT_KEYS / 32; ++kb)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float* v = s + 32 * kb + 4 * j;
+                *reinterpret_cast<float4*>(smem + AT_P + kb * 16384 + row * 128 + ((j ^ (row & 7)) << 4)) =
+                    make_float4(tf32_rna(v[0]), tf32_rna(v[1]), tf32_rna(v[2]), tf32_rna(v[3]));
+            }
+        fence_proxy_async_smem();
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&bar[5]);
+        const int64_t prow = (int64_t)blockIdx.y * a.n_q + m0 + row;
+        a.mpart[prow] = mx;
+        a.lpart[prow] = l;
+        ok = ok && mbar_wait(&bar[6], 0, a.err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (lane == 0) bulk_wait_all();   // the Scores stores are done before the CTA exits
+        __syncwarp();
+        if (ok) {
+            float* op = a.opart + prow * AT_D;
+#pragma unroll
+            for (int ch = 0; ch < AT_D / 16; ++ch) {
+                float o[16];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + AT_KEYS + ch * 16, o);
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                    *reinterpret_cast<float4*>(op + ch * 16 + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(AT_TMEM_COLS));
+    }
+}
+
+// A warp per query row: the key tiles' statistics combined (m*, l*) and the
+// row of O (lane l: columns 2l, 2l + 1); m* and 1 / l* kept for the row of A.
+__global__ void __launch_bounds__(256)
+    k_attn_rows(const float* __restrict__ opart, const float* __restrict__ mpart, const float* __restrict__ lpart,
+                int n_kt, int64_t n_q, float2* __restrict__ stat, float* __restrict__ O, int64_t lo) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_q; r += warps) {
+        float m = -INFINITY, lt = 0.f;
+        for (int t = lane; t < n_kt; t += 32) {
+            const float mt = mpart[t * n_q + r];
+            const float l1 = lpart[t * n_q + r];
+            // running (m, l) of this lane's tiles
+            const float mn = fmaxf(m, mt);
+            lt = lt * __expf(m - mn) + l1 * __expf(mt - mn);
+            m = mn;
+        }
+        float mstar = m;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mstar = fmaxf(mstar, __shfl_xor_sync(0xffffffffu, mstar, o));
+        float l = m == -INFINITY ? 0.f : lt * __expf(m - mstar);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        const float inv = 1.0f / l;
+        // 8 tiles' loads in flight at a time
+        float o0 = 0.f, o1 = 0.f;
+        for (int t0 = 0; t0 < n_kt; t0 += 8) {
+            float w[8];
+            float2 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int t = t0 + u;
+                w[u] = t < n_kt ? mpart[t * n_q + r] : -INFINITY;
+                v[u] = t < n_kt ? *reinterpret_cast<const float2*>(opart + (t * n_q + r) * AT_D + 2 * lane)
+                                : make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float e = __expf(w[u] - mstar);
+                o0 = fmaf(e, v[u].x, o0);
+                o1 = fmaf(e, v[u].y, o1);
+            }
+        }
+        *reinterpret_cast<float2*>(O + r * lo + 2 * lane) = make_float2(o0 * inv, o1 * inv);
+        if (lane == 0) stat[r] = make_float2(mstar, inv);
+    }
+}
+
+// A = exp(S - m*) / l* over the whole matrix, 128-bit loads and stores
+// (n_k a multiple of 4): each thread keeps 4 loads in flight.
+__global__ void __launch_bounds__(256)
+    k_attn_probs(const float* __restrict__ S, const float2* __restrict__ stat, int64_t n_q, int64_t n_k,
+                 float* __restrict__ A) {
+    const int64_t per_row = n_k / 4, total = n_q * per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 4 * stride) {
+        float4 v[4];
+        float2 st[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t i = i0 + u * stride;
+            v[u] = i < total ? reinterpret_cast<const float4*>(S)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            st[u] = i < total ? stat[i / per_row] : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i < total)
+                reinterpret_cast<float4*>(A)[i] =
+                    make_float4(__expf(v[u].x - st[u].x) * st[u].y, __expf(v[u].y - st[u].x) * st[u].y,
+                                __expf(v[u].z - st[u].x) * st[u].y, __expf(v[u].w - st[u].x) * st[u].y);
+        }
+    }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -961,6 +1265,58 @@ static tl_status launch_simt(tl_ctx* c, const GemmPlan& p) {
     if (bn == 16) k_gemm_simt<16><<<grid, 256, 0, c->stream>>>(p, sgn, mag, splits > 1 ? chunk : p.K);
     else k_gemm_simt<64><<<grid, 256, 0, c->stream>>>(p, sgn, mag, splits > 1 ? chunk : p.K);
     return L.done();
+}
+
+// The attention block S = scale Q K^T, A = softmax over keys (the rows of S),
+// O = A V on row-major fp32 tensors with d = 64 and query / key counts that are
+// multiples of 128 (the caller checks the shapes); see k_attn_tile.
+tl_status launch_attention(tl_ctx* c, const AttnPlan& p) {
+    CUtensorMap mq, mk, mv, ms;
+    memset(&mq, 0, sizeof mq); memset(&mk, 0, sizeof mk); memset(&mv, 0, sizeof mv); memset(&ms, 0, sizeof ms);
+    bool ok = make_map(&mq, p.Q, AT_D, p.n_q, AT_D, AT_ROWS, false) && make_map(&mk, p.K, AT_D, p.n_k, AT_D, AT_KEYS, false) &&
+              make_map(&mv, p.V, AT_D, p.n_k, AT_D, 32, true) && make_store_map(&ms, p.S, p.n_k, p.n_q, p.n_k);
+    if (!ok) return fail(c, TL_ERR_CUDA, "attention: tensor maps");
+    const int n_kt = (int)(p.n_k / AT_KEYS);
+    const size_t part = (size_t)n_kt * p.n_q;
+    void* ws = nullptr;
+    TL_TRY(workspace(c, part * (AT_D + 2) * sizeof(float) + (size_t)p.n_q * sizeof(float2) + 16, &ws, WS_GEMM));
+    AttnArgs a;
+    a.S = p.S;
+    a.ls = p.n_k;
+    a.n_q = p.n_q;
+    a.scale = p.scale;
+    a.opart = static_cast<float*>(ws);
+    a.mpart = a.opart + part * AT_D;
+    a.lpart = a.mpart + part;
+    a.err = c->d_flags + 8;
+    c->flags_armed = true;
+    static int attr_dev[64] = {0};
+    if (c->device >= 0 && c->device < 64 && !attr_dev[c->device]) {
+        TL_CK(c, cudaFuncSetAttribute(k_attn_tile, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM));
+        attr_dev[c->device] = 1;
+    }
+    {
+        LaunchScope L(c, "attention_tile", (double)(3 * p.n_k * AT_D + p.n_q * AT_D) * 4.0 + (double)p.n_q * p.n_k * 4.0,
+                      4.0 * (double)p.n_q * p.n_k * AT_D);
+        k_attn_tile<<<dim3((unsigned)(p.n_q / AT_ROWS), (unsigned)n_kt), AT_THREADS, AT_SMEM, c->stream>>>(mq, mk, mv, ms, a);
+        TL_TRY(L.done());
+    }
+    // per-row (m*, 1 / l*) after the partials, 8-byte aligned
+    float2* stat = reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(a.lpart + part) + 7) & ~uintptr_t(7));
+    {
+        LaunchScope L(c, "attention_combine", (double)part * (AT_D + 2) * 4.0 + (double)p.n_q * AT_D * 4.0);
+        const int64_t blocks = std::min<int64_t>((p.n_q + 7) / 8, (int64_t)c->sm_count * 8);
+        k_attn_rows<<<(unsigned)blocks, 256, 0, c->stream>>>(a.opart, a.mpart, a.lpart, n_kt, p.n_q, stat, p.O, AT_D);
+        TL_TRY(L.done());
+    }
+    {
+        LaunchScope L(c, "attention_probs", (double)p.n_q * p.n_k * 8.0);
+        const int64_t quads = p.n_q * p.n_k / 4;
+        const int64_t blocks = std::min<int64_t>((quads + 1023) / 1024, (int64_t)c->sm_count * 16);
+        k_attn_probs<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, c->stream>>>(p.S, stat, p.n_q, p.n_k, p.A);
+        TL_TRY(L.done());
+    }
+    return TL_OK;
 }
 
 tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {

@@ -1077,6 +1077,113 @@ static const tl_equation* lazy_step_equation(const tl_statement* s, int n) {
     return nullptr;
 }
 
+// An attention block, three equations in a row (softmax.zig:19-229 between
+// two contractions, einsum.zig:20-254):
+//   S[q,k] = Q[q,d] K[k,d] (times or divided by a literal)
+//   A[q,k.] = softmax(S[q,k])
+//   O[q,d] = A[q,k] V[k,d]
+// on row-major fp32 tensors with d = 64 and q, k multiples of 128, S and O
+// written for the first time in this run and no sign test on S or O: run as
+// the tiled kernel and the combine kernel (launch_attention), which write S,
+// A and O in full.  Anything else takes the three equations one by one.
+static tl_status try_attention(tl_ctx* c, const tl_equation* e1, const tl_equation* e2, const tl_equation* e3,
+                               bool* done) {
+    *done = false;
+    if (getenv("TL_NO_FUSED_ATTENTION") || c->opts.precision != TL_PREC_TF32 || !tcgen05_available(c)) return TL_OK;
+    if (e1->accum != TL_ACC_ASSIGN || e2->accum != TL_ACC_ASSIGN || e3->accum != TL_ACC_ASSIGN) return TL_OK;
+    auto name_is = [](const tl_index& ix, const char* n) { return !strcmp(ix.name, n); };
+    auto plain = [](const tl_ref& r) {
+        if (r.rank != 2) return false;
+        for (int k = 0; k < 2; ++k)
+            if (r.idx[k].kind != TL_IX_NAME) return false;
+        return true;
+    };
+    // e2: A[q, k.] = softmax(S[q, k])
+    if (e2->n_refs != 1 || e2->n_code != 2 || e2->code[0].op != TL_OP_REF || e2->code[0].arg != 0 ||
+        e2->code[1].op != TL_OP_NL || e2->code[1].arg != TL_NL_SOFTMAX)
+        return TL_OK;
+    const tl_ref& rs2 = e2->refs[0];
+    if (!plain(rs2) || e2->lhs.rank != 2 || e2->lhs.idx[0].kind != TL_IX_NAME ||
+        (e2->lhs.idx[1].kind != TL_IX_NAME && e2->lhs.idx[1].kind != TL_IX_NORMALIZE))
+        return TL_OK;
+    const char* qn = rs2.idx[0].name;
+    const char* kn = rs2.idx[1].name;
+    if (!strcmp(qn, kn) || !name_is(e2->lhs.idx[0], qn) || !name_is(e2->lhs.idx[1], kn)) return TL_OK;
+    // e1: S[q, k] = Q[q, d] K[k, d] scale
+    GemmMatch m1, m3;
+    if (!match_product2(e1, &m1) || m1.relu_term || !plain(e1->lhs) || strcmp(e1->lhs.tensor, rs2.tensor) ||
+        !name_is(e1->lhs.idx[0], qn) || !name_is(e1->lhs.idx[1], kn))
+        return TL_OK;
+    const tl_ref* rq = &e1->refs[m1.ref_a];
+    const tl_ref* rk = &e1->refs[m1.ref_b];
+    if (!plain(*rq) || !plain(*rk)) return TL_OK;
+    if (name_is(rq->idx[0], kn)) std::swap(rq, rk);
+    if (!name_is(rq->idx[0], qn) || !name_is(rk->idx[0], kn)) return TL_OK;
+    const char* dn = rq->idx[1].name;
+    if (!name_is(rk->idx[1], dn) || !strcmp(dn, qn) || !strcmp(dn, kn)) return TL_OK;
+    // e3: O[q, d] = A[q, k] V[k, d]
+    if (!match_product2(e3, &m3) || m3.relu_term || m3.scale != 1.0f || !plain(e3->lhs) ||
+        !name_is(e3->lhs.idx[0], qn) || !name_is(e3->lhs.idx[1], dn))
+        return TL_OK;
+    const tl_ref* ra = &e3->refs[m3.ref_a];
+    const tl_ref* rv = &e3->refs[m3.ref_b];
+    if (strcmp(ra->tensor, e2->lhs.tensor)) std::swap(ra, rv);
+    if (!plain(*ra) || !plain(*rv) || strcmp(ra->tensor, e2->lhs.tensor) || !name_is(ra->idx[0], qn) ||
+        !name_is(ra->idx[1], kn) || !name_is(rv->idx[0], kn) || !name_is(rv->idx[1], dn))
+        return TL_OK;
+    // the tensors: inputs defined and dense, outputs distinct and fresh
+    const int64_t nq = domain_size(c, qn), nk = domain_size(c, kn), nd = domain_size(c, dn);
+    if (nd != 64 || nq < 128 || nk < 128 || nq % 128 || nk % 128 || nq >= INT32_MAX || nk >= INT32_MAX) return TL_OK;
+    const char* outs[3] = {e1->lhs.tensor, e2->lhs.tensor, e3->lhs.tensor};
+    const char* ins[3] = {rq->tensor, rk->tensor, rv->tensor};
+    for (int i = 0; i < 3; ++i) {
+        for (int j = 0; j < 3; ++j)
+            if (!strcmp(outs[i], ins[j]) || (i != j && !strcmp(outs[i], outs[j]))) return TL_OK;
+        if (std::find(c->sign_sensitive.begin(), c->sign_sensitive.end(), std::string(outs[i])) !=
+            c->sign_sensitive.end())
+            return TL_OK;
+    }
+    Tensor* tq = find_defined(c, rq->tensor);
+    Tensor* tk = find_defined(c, rk->tensor);
+    Tensor* tv = find_defined(c, rv->tensor);
+    auto shape_ok = [](const Tensor* t, int64_t r, int64_t cl) {
+        return t && t->rank == 2 && t->dims[0] == r && t->dims[1] == cl && t->shard != TL_SHARD_ROWS;
+    };
+    if (!shape_ok(tq, nq, 64) || !shape_ok(tk, nk, 64) || !shape_ok(tv, nk, 64)) return TL_OK;
+    Tensor* out[3];
+    for (int i = 0; i < 3; ++i) {
+        const tl_equation* e = i == 0 ? e1 : i == 1 ? e2 : e3;
+        out[i] = find_defined(c, outs[i]);
+        if (!out[i]) TL_TRY(allocate_tensor(c, e->lhs.tensor, e->lhs.idx, e->lhs.rank, &out[i]));
+    }
+    if (!shape_ok(out[0], nq, nk) || !shape_ok(out[1], nq, nk) || !shape_ok(out[2], nq, 64) || !out[0]->zero ||
+        !out[2]->zero)
+        return TL_OK;
+    tl_status st;
+    AttnPlan p;
+    p.Q = read_ptr(c, tq, &st); TL_TRY(st);
+    p.K = read_ptr(c, tk, &st); TL_TRY(st);
+    p.V = read_ptr(c, tv, &st); TL_TRY(st);
+    if (!p.Q || !p.K || !p.V) return TL_OK;   // a zero operand: the one-by-one path keeps its meaning
+    for (int i = 0; i < 3; ++i) TL_TRY(alloc_dense_public(c, out[i]));
+    p.S = out[0]->dense;
+    p.A = out[1]->dense;
+    p.O = out[2]->dense;
+    p.n_q = nq;
+    p.n_k = nk;
+    p.scale = m1.scale;
+    for (const void* ptr : {(const void*)p.Q, (const void*)p.K, (const void*)p.V, (const void*)p.S, (const void*)p.A,
+                            (const void*)p.O})
+        if ((uintptr_t)ptr & 15) return TL_OK;
+    TL_TRY(launch_attention(c, p));
+    for (int i = 0; i < 3; ++i) {
+        mark_written_dense(out[i]);
+        out[i]->boolean = false;
+    }
+    *done = true;
+    return TL_OK;
+}
+
 // The statements of a run in order (non-recursive equations, declarations,
 // loads, backward); recursive equations are collected into `rec`.
 static tl_status run_statements(tl_ctx* c, const tl_statement* s, int n, const std::vector<tl_equation>& eqs,
@@ -1088,6 +1195,19 @@ static tl_status run_statements(tl_ctx* c, const tl_statement* s, int n, const s
         case TL_STMT_EQUATION:
             if (is_recursive(&st->eq)) rec->push_back(st->eq);
             else {
+                // an attention block runs as one tiled pipeline
+                if (i + 2 < n && s[i + 1].kind == TL_STMT_EQUATION && s[i + 2].kind == TL_STMT_EQUATION &&
+                    !is_recursive(&s[i + 1].eq) && !is_recursive(&s[i + 2].eq)) {
+                    bool fused = false;
+                    TL_TRY(validate_code(c, &st->eq));
+                    TL_TRY(validate_code(c, &s[i + 1].eq));
+                    TL_TRY(validate_code(c, &s[i + 2].eq));
+                    TL_TRY(try_attention(c, &st->eq, &s[i + 1].eq, &s[i + 2].eq, &fused));
+                    if (fused) {
+                        i += 2;
+                        break;
+                    }
+                }
                 // an element-wise relu right after a GEMM is written by its epilogue
                 const tl_equation* next = (i + 1 < n && s[i + 1].kind == TL_STMT_EQUATION &&
                                            !is_recursive(&s[i + 1].eq)) ? &s[i + 1].eq : nullptr;

@@ -297,6 +297,15 @@ struct GemmPlan {
 };
 tl_status launch_gemm(tl_ctx* c, const GemmPlan& p);
 bool tcgen05_available(tl_ctx* c);
+// S = scale Q K^T, A = softmax over the rows of S, O = A V: row-major fp32,
+// Q, K, V and O with 64 columns, n_q and n_k multiples of 128 (k_gemm.cu)
+struct AttnPlan {
+    const float *Q, *K, *V;
+    float *S, *A, *O;
+    int64_t n_q, n_k;
+    float scale;
+};
+tl_status launch_attention(tl_ctx* c, const AttnPlan& p);
 
 // CSR SpMM out[v, j] (+)= sum_e val[e] * P[col[e], j]
 tl_status launch_spmm(tl_ctx* c, int64_t rows, const int64_t* rowptr, const int32_t* colidx,

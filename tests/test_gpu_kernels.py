@@ -311,3 +311,60 @@ def test_generic_recursive_dense(ctx, oracle_lib):
         "R[x,y] = step(E[x,y])\nR[x,z] max= step(R[x,y] E[y,z])\n"
     ref = both(ctx, oracle_lib, src, dict(E=E))
     np.testing.assert_array_equal(ctx.tensor("R"), ref.tensor("R"))
+
+
+# ----------------------------------------------------------------------------- attention block
+ATTN_CASES = [
+    # (queries, keys, d, scores expression, note).  The scores keep the 1/sqrt(d)
+    # scale: unscaled N(0, 1) inputs give scores of deviation 8, where the TF32
+    # rounding of Q and K alone moves the softmax past the 1e-3 tolerance (in
+    # the tiled pipeline and one equation at a time alike)
+    (256, 384, 64, "Q[q,d] K[k,d] / 8.0", "the tiled pipeline"),
+    (128, 128, 64, "Q[q,d] K[k,d] * 0.125", "one tile, a multiplied scale"),
+    (384, 256, 64, "K[k,d] Q[q,d] / 8.0", "operands swapped"),
+    (200, 256, 64, "Q[q,d] K[k,d] / 8.0", "queries not a multiple of 128: one by one"),
+    (256, 256, 32, "Q[q,d] K[k,d] / 8.0", "d = 32: one by one"),
+]
+
+
+@pytest.mark.parametrize("nq,nk,d,expr,note", ATTN_CASES)
+def test_attention_block(ctx, oracle_lib, nq, nk, d, expr, note):
+    Q = gen.normal(11, "Q", (nq, d))
+    K = gen.normal(12, "K", (nk, d))
+    V = gen.normal(13, "V", (nk, d))
+    src = decl(q=nq, k=nk, d=d) + inputs_src([("Q", "qd"), ("K", "kd"), ("V", "kd")]) + \
+        f"S[q,k] = {expr}\nA[q,k.] = softmax(S[q,k])\nO[q,d] = A[q,k] V[k,d]\n"
+    ref = both(ctx, oracle_lib, src, dict(Q=Q, K=K, V=V))
+    for n in ("S", "A", "O"):
+        assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, f"{n} ({note})")
+
+
+def test_attention_block_matches_one_by_one(ctx, monkeypatch):
+    # the tiled pipeline and the three equations run one by one agree; a
+    # second run of the same program (outputs no longer fresh) too
+    nq, nk, d = 256, 512, 64
+    data = dict(Q=gen.normal(21, "Q", (nq, d)), K=gen.normal(22, "K", (nk, d)), V=gen.normal(23, "V", (nk, d)))
+    src = decl(q=nq, k=nk, d=d) + inputs_src([("Q", "qd"), ("K", "kd"), ("V", "kd")]) + \
+        "Scores[q,k] = Q[q,d] K[k,d] / 8.0\nAttn[q,k.] = softmax(Scores[q,k])\nOut[q,d] = Attn[q,k] V[k,d]\n"
+    p = lang.Program(src, inputs=data)
+    ctx.run(p)
+    fused = {n: ctx.tensor(n) for n in ("Scores", "Attn", "Out")}
+    ctx.run(p)
+    for n in fused:
+        np.testing.assert_allclose(ctx.tensor(n), fused[n], rtol=0, atol=0)
+    monkeypatch.setenv("TL_NO_FUSED_ATTENTION", "1")
+    ctx.run(p)
+    for n in fused:
+        assert_close(fused[n], ctx.tensor(n), TOL_TF32, n)
+
+
+def test_attention_block_accumulating_scores(ctx, oracle_lib):
+    # S defined earlier in the run: `=` with a contraction adds into it, so
+    # the block runs one equation at a time
+    nq, nk, d = 128, 128, 64
+    data = dict(Q=gen.normal(31, "Q", (nq, d)), K=gen.normal(32, "K", (nk, d)), V=gen.normal(33, "V", (nk, d)))
+    src = decl(q=nq, k=nk, d=d) + inputs_src([("Q", "qd"), ("K", "kd"), ("V", "kd")]) + \
+        "S[q,k] = 0.5\nS[q,k] = Q[q,d] K[k,d] / 8.0\nA[q,k.] = softmax(S[q,k])\nO[q,d] = A[q,k] V[k,d]\n"
+    ref = both(ctx, oracle_lib, src, data)
+    for n in ("S", "A", "O"):
+        assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
