@@ -787,8 +787,8 @@ __global__ void k_prep_transpose(const float* __restrict__ S, int64_t s_r, int64
 // einsum contractions, einsum.zig:20-254) as two kernels, Scores and Attn
 // still written in full:
 //  * k_attn_tile, one CTA per (128 queries, 128 keys) tile: TMA brings the
-//    Q, K and V tiles into shared memory, where the softmax warps round them
-//    to TF32 (nearest) in place; one elected thread issues S = Q K^T with
+//    Q, K and V tiles into shared memory, where they are rounded to TF32
+//    (nearest) in place; one elected thread issues S = Q K^T with
 //    tcgen05.mma into TMEM; the four softmax warps read S back (a row per
 //    thread), store scale * S through the TMA, take the row maximum m and
 //    sum l of exp(S - m) over the tile's keys, and write P = exp(S - m)
@@ -845,7 +845,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
 
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1); mbar_init(&bar[1], 1);
-        mbar_init(&bar[2], 128); mbar_init(&bar[3], 128);
+        mbar_init(&bar[2], 160); mbar_init(&bar[3], 32);
         mbar_init(&bar[4], 1); mbar_init(&bar[5], 128); mbar_init(&bar[6], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
@@ -864,7 +864,9 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
 
     if (warp == 0) {
         // ---------------- TMA: Q and K as two 32-wide K-major blocks each, V
-        // as four 32-key blocks of two 32 x 32 MN-major boxes ----------------
+        // as four 32-key blocks of two 32 x 32 MN-major boxes; then this warp
+        // helps round Q and K, and rounds V alone (V is needed only by the
+        // second MMA, so its rounding stays off the softmax warps' path) -------
         if (lane == 0) {
             mbar_expect_tx(&bar[0], 4 * 16384);
             tma_load_2d(smem + AT_Q, &tmQ, &bar[0], 0, m0);
@@ -878,6 +880,15 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
                 for (int j = 0; j < 2; ++j)
                     tma_load_2d(smem + AT_V + kb * 8192 + j * 4096, &tmV, &bar[1], 32 * j, n0 + 32 * kb);
         }
+        __syncwarp();
+        bool ok = mbar_wait(&bar[0], 0, a.err);
+        if (ok) round_tf32_inplace(smem + AT_Q, 4 * 16384, 128 + lane, 160);
+        fence_proxy_async_smem();
+        mbar_arrive(&bar[2]);
+        ok = ok && mbar_wait(&bar[1], 0, a.err);
+        if (ok) round_tf32_inplace(smem + AT_V, 8 * 4096, lane, 32);
+        fence_proxy_async_smem();
+        mbar_arrive(&bar[3]);
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         constexpr uint32_t idesc_s = (1u << 4) | (2u << 7) | (2u << 10)           // D f32, A, B tf32
@@ -919,13 +930,9 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
         const int q = warp & 3;                 // TMEM lane quarter of this warp
         const int row = q * 32 + lane;          // row of the tile = TMEM lane
         bool ok = mbar_wait(&bar[0], 0, a.err);
-        if (ok) round_tf32_inplace(smem + AT_Q, 4 * 16384, t, 128);
+        if (ok) round_tf32_inplace(smem + AT_Q, 4 * 16384, t, 160);
         fence_proxy_async_smem();
         mbar_arrive(&bar[2]);
-        ok = ok && mbar_wait(&bar[1], 0, a.err);
-        if (ok) round_tf32_inplace(smem + AT_V, 8 * 4096, t, 128);
-        fence_proxy_async_smem();
-        mbar_arrive(&bar[3]);
         ok = ok && mbar_wait(&bar[4], 0, a.err);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         float s[AT_KEYS];
