@@ -305,6 +305,13 @@ tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* rows,
                            const int64_t* cols, const double* vals);
 /* Query print: "Name[total] = [v0 ... v19 ]\n" with %.4g (llvm.zig:461-480). */
 tl_status tl_query_format(tl_tensor* t, char* buf, int64_t buf_len);
+/* The text the last tl_program_run's queries printed, in statement order:
+ * what the reference's program writes to stdout (llvm.zig:309-318).  A query
+ * with a constant index prints "Name = %.6g\n", the backward-chaining value
+ * (backward.zig:568-600); any other query prints as tl_query_format.
+ * Copies at most buf_len - 1 bytes and a terminating 0; *needed (optional)
+ * receives the full length. */
+tl_status tl_program_output(tl_ctx* ctx, char* buf, int64_t buf_len, int64_t* needed);
 
 /* ------------------------------------------------------------------------ */
 /* Row sharding (closure and GNN message passing across the GPUs of a box). */

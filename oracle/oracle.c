@@ -39,6 +39,26 @@ typedef struct {
     int64_t dims[TL_MAX_RANK];
 } or_maxdims;
 
+/* A global the backward-chaining infrastructure allocates before main
+ * (llvm.zig:231-260, tensor.zig:157-220): the queried tensors and the
+ * left-hand sides their equations read. */
+#define MAX_BW 64
+#define BW_MAX_DEPTH 4096
+typedef struct {
+    char name[TL_NAME_LEN];
+    int32_t rank;
+    int64_t dims[TL_MAX_RANK];
+    int64_t strides[TL_MAX_RANK];
+    int64_t total;
+    int32_t compute;          /* queried with a constant index: @compute_T */
+    int32_t n_eq;
+    int32_t* eq_stmt;         /* statement indices of T's equations, program order */
+    double* memo;             /* @memo_T */
+    unsigned char* done;      /* @memo_T_computed */
+    int32_t detached;         /* a `sparse` re-declaration replaced the forward tensor */
+    double* snap;             /* what the global held at that point */
+} bw_global;
+
 struct or_ctx {
     int32_t max_sweeps;
     int32_t last_sweeps;
@@ -52,6 +72,11 @@ struct or_ctx {
     char* qout;
     size_t qlen, qcap;
     char err[256];
+    int32_t n_bw;
+    bw_global bw[MAX_BW];
+    const tl_statement* bw_stmts;
+    int32_t bw_depth;
+    int32_t bw_err;
 };
 
 /* ------------------------------------------------------------------------ */
@@ -850,6 +875,289 @@ static int gen_backward(or_ctx* c, const tl_statement* st, const tl_statement* a
 }
 
 /* ------------------------------------------------------------------------ */
+/* Backward chaining: constant-index queries (backward.zig:37-600)            */
+/* ------------------------------------------------------------------------ */
+
+/* isBackwardQuery (backward.zig:37-46): any constant index. */
+static int bw_is_query(const tl_ref* q) {
+    for (int k = 0; k < q->rank; ++k) if (q->idx[k].kind == TL_IX_CONST) return 1;
+    return 0;
+}
+
+static bw_global* bw_find(or_ctx* c, const char* name) {
+    for (int i = 0; i < c->n_bw; ++i) if (strcmp(c->bw[i].name, name) == 0) return &c->bw[i];
+    return NULL;
+}
+
+static void bw_reset(or_ctx* c) {
+    for (int i = 0; i < c->n_bw; ++i) {
+        free(c->bw[i].eq_stmt); free(c->bw[i].memo); free(c->bw[i].done); free(c->bw[i].snap);
+    }
+    memset(c->bw, 0, sizeof c->bw);
+    c->n_bw = 0;
+    c->bw_stmts = NULL;
+    c->bw_depth = 0;
+    c->bw_err = 0;
+}
+
+/* allocateTensorGlobal (tensor.zig:157-220): max dims when known, else per index. */
+static bw_global* bw_add(or_ctx* c, const tl_ref* lhs) {
+    bw_global* g = bw_find(c, lhs->tensor);
+    if (g) return g;
+    if (c->n_bw >= MAX_BW) return NULL;
+    g = &c->bw[c->n_bw++];
+    snprintf(g->name, TL_NAME_LEN, "%s", lhs->tensor);
+    const or_maxdims* m = NULL;
+    for (int i = 0; i < c->n_maxdims; ++i) if (strcmp(c->maxdims[i].name, lhs->tensor) == 0) m = &c->maxdims[i];
+    if (m) { g->rank = m->rank; for (int k = 0; k < m->rank; ++k) g->dims[k] = m->dims[k]; }
+    else {
+        g->rank = lhs->rank;
+        for (int k = 0; k < lhs->rank; ++k)
+            g->dims[k] = lhs->idx[k].kind == TL_IX_NORMALIZE ? 10 : index_extent(c, &lhs->idx[k]);
+    }
+    if (g->rank == 0) { g->rank = 1; g->dims[0] = 1; }
+    int64_t s = 1;
+    for (int k = g->rank - 1; k >= 0; --k) { g->strides[k] = s; s *= g->dims[k]; }
+    g->total = s;
+    return g;
+}
+
+static int name_in(const char (*names)[TL_NAME_LEN], int n, const char* name) {
+    for (int i = 0; i < n; ++i) if (strcmp(names[i], name) == 0) return 1;
+    return 0;
+}
+
+/* The globals and memo tables of llvm.zig:222-264 and genBackwardInfra
+ * (backward.zig:53-118): queried tensors' equations in program order, then
+ * the equation-defined tensors their right-hand sides read. */
+static int bw_prepare(or_ctx* c, const tl_statement* stmts, int n) {
+    static char queried[MAX_BW][TL_NAME_LEN], deps[MAX_BW * TL_MAX_REFS][TL_NAME_LEN];
+    int nq = 0, nd = 0;
+    bw_reset(c);
+    c->bw_stmts = stmts;
+    for (int s = 0; s < n; ++s)
+        if (stmts[s].kind == TL_STMT_QUERY && bw_is_query(&stmts[s].sparse) &&
+            !name_in(queried, nq, stmts[s].name) && nq < MAX_BW)
+            snprintf(queried[nq++], TL_NAME_LEN, "%s", stmts[s].name);
+    if (nq == 0) return TL_OK;
+    for (int s = 0; s < n; ++s) {
+        if (stmts[s].kind != TL_STMT_EQUATION || !name_in(queried, nq, stmts[s].eq.lhs.tensor)) continue;
+        bw_global* g = bw_add(c, &stmts[s].eq.lhs);
+        if (!g) return TL_ERR_TOO_LARGE;
+        g->compute = 1;
+        g->eq_stmt = (int32_t*)realloc(g->eq_stmt, sizeof(int32_t) * (size_t)(g->n_eq + 1));
+        g->eq_stmt[g->n_eq++] = s;
+        for (int r = 0; r < stmts[s].eq.n_refs; ++r)
+            if (!name_in(deps, nd, stmts[s].eq.refs[r].tensor) && nd < MAX_BW * TL_MAX_REFS)
+                snprintf(deps[nd++], TL_NAME_LEN, "%s", stmts[s].eq.refs[r].tensor);
+    }
+    for (int s = 0; s < n; ++s) {
+        if (stmts[s].kind != TL_STMT_EQUATION) continue;
+        const char* lhs = stmts[s].eq.lhs.tensor;
+        if (name_in(deps, nd, lhs) && !name_in(queried, nq, lhs) && !bw_add(c, &stmts[s].eq.lhs))
+            return TL_ERR_TOO_LARGE;
+    }
+    for (int i = 0; i < c->n_bw; ++i) {
+        bw_global* g = &c->bw[i];
+        if (!g->compute) continue;
+        g->memo = (double*)calloc((size_t)g->total, sizeof(double));
+        g->done = (unsigned char*)calloc((size_t)g->total, 1);
+        if (!g->memo || !g->done) return TL_ERR_OOM;
+    }
+    return TL_OK;
+}
+
+/* genSparseDecl re-allocates unconditionally (llvm.zig:482-516), so after a
+ * `sparse` declaration of a global the forward code writes a new buffer and
+ * the compute functions keep reading the global as it was. */
+static void bw_detach(or_ctx* c, const char* name) {
+    bw_global* g = bw_find(c, name);
+    if (!g || g->detached) return;
+    g->detached = 1;
+    g->snap = (double*)calloc((size_t)g->total, sizeof(double));
+    const or_tensor* t = find_tensor(c, name);
+    if (g->snap && t && t->total == g->total) memcpy(g->snap, t->data, (size_t)g->total * sizeof(double));
+}
+
+static double bw_call(or_ctx* c, bw_global* g, const int64_t* iv);
+
+/* A contracted equation's loop variables (collectContracted,
+ * backward.zig:253-282), in order of first appearance. */
+typedef struct {
+    int32_t n;
+    char names[MAX_VARS][TL_NAME_LEN];
+    int64_t sizes[MAX_VARS];
+    int64_t cur[MAX_VARS];
+} bw_loops;
+
+/* genBackwardTensorAccess (backward.zig:493-548). */
+static double bw_access(or_ctx* c, const tl_equation* eq, int r, const int64_t* params,
+                        const tl_ref* lhs, const bw_loops* lv) {
+    const tl_ref* ref = &eq->refs[r];
+    bw_global* g = bw_find(c, ref->tensor);
+    if (!g) return 0.0;                        /* not in the codegen's tensor map */
+    int64_t iv[TL_MAX_RANK];
+    for (int k = 0; k < ref->rank; ++k) {
+        const tl_index* ix = &ref->idx[k];
+        iv[k] = 0;
+        if (ix->kind == TL_IX_CONST) { iv[k] = ix->value; continue; }
+        if (ix->kind != TL_IX_NAME) continue;
+        int bound = -1;
+        for (int j = 0; j < lhs->rank; ++j)
+            if (lhs->idx[j].kind == TL_IX_NAME && strcmp(lhs->idx[j].name, ix->name) == 0) bound = j;
+        if (bound >= 0) { iv[k] = params[bound]; continue; }
+        for (int j = 0; j < lv->n; ++j)
+            if (strcmp(lv->names[j], ix->name) == 0) { iv[k] = lv->cur[j]; break; }
+    }
+    if (g->compute) {
+        if (ref->rank != g->rank) { c->bw_err = TL_ERR_UNSUPPORTED; return 0.0; }
+        return bw_call(c, g, iv);
+    }
+    /* computeLinearOffset (tensor.zig:131-154) over the global's strides */
+    int64_t off = 0;
+    int nk = ref->rank < g->rank ? ref->rank : g->rank;
+    for (int k = 0; k < nk; ++k) off += iv[k] * g->strides[k];
+    if (off < 0 || off >= g->total) return 0.0;
+    if (g->detached) return g->snap ? g->snap[off] : 0.0;
+    const or_tensor* t = find_tensor(c, g->name);
+    return (t && off < t->total) ? t->data[off] : 0.0;
+}
+
+/* genBackwardExpr (backward.zig:375-488) over the postfix program. */
+static double bw_eval(or_ctx* c, const tl_equation* eq, const int64_t* params, const bw_loops* lv) {
+    double st[TL_MAX_CODE];
+    int sp = 0;
+    for (int i = 0; i < eq->n_code && !c->bw_err; ++i) {
+        const tl_instr* in = &eq->code[i];
+        switch (in->op) {
+        case TL_OP_REF: st[sp++] = bw_access(c, eq, in->arg, params, &eq->lhs, lv); break;
+        case TL_OP_LIT: st[sp++] = in->value; break;
+        case TL_OP_PROD: {
+            int n = in->arg;
+            double acc = st[sp - n];
+            for (int k = 1; k < n; ++k) acc = acc * st[sp - n + k];
+            sp -= n;
+            st[sp++] = acc;
+            break;
+        }
+        case TL_OP_NEG: st[sp - 1] = -st[sp - 1]; break;
+        case TL_OP_NOT: st[sp - 1] = (st[sp - 1] == 0.0) ? 1.0 : 0.0; break;
+        case TL_OP_NL: {
+            double x = st[sp - 1], r;
+            switch (in->arg) {
+            case TL_NL_STEP: r = x > 0.0 ? 1.0 : 0.0; break;
+            case TL_NL_RELU: r = x > 0.0 ? x : 0.0; break;
+            case TL_NL_SIGMOID: r = 1.0 / (1.0 + exp(-x)); break;   /* no temperature */
+            case TL_NL_EXP: r = exp(x); break;
+            case TL_NL_LOG: r = log(x); break;
+            case TL_NL_SQRT: r = sqrt(x); break;
+            case TL_NL_ABS: r = fabs(x); break;
+            case TL_NL_SIN: r = sin(x); break;
+            case TL_NL_COS: r = cos(x); break;
+            case TL_NL_TANH: { double e = x * 2.0; e = exp(e); r = (e - 1.0) / (e + 1.0); break; }
+            default: r = 0.0 + x; break;
+            }
+            st[sp - 1] = r;
+            break;
+        }
+        default: {
+            double b = st[--sp];
+            double a = st[sp - 1];
+            switch (in->op) {
+            case TL_OP_SUB: st[sp - 1] = a - b; break;
+            case TL_OP_MUL: st[sp - 1] = a * b; break;
+            case TL_OP_DIV: st[sp - 1] = a / b; break;
+            default: st[sp - 1] = a + b; break;     /* add, and every other binary op */
+            }
+        }
+        }
+    }
+    return sp > 0 ? st[sp - 1] : 0.0;
+}
+
+/* genBackwardEquation + genContractedSum (backward.zig:222-371). */
+static double bw_equation(or_ctx* c, const tl_equation* eq, const int64_t* params) {
+    bw_loops lv;
+    lv.n = 0;
+    for (int r = 0; r < eq->n_refs; ++r)
+        for (int k = 0; k < eq->refs[r].rank; ++k) {
+            const tl_index* ix = &eq->refs[r].idx[k];
+            if (ix->kind != TL_IX_NAME) continue;
+            int bound = 0;
+            for (int j = 0; j < eq->lhs.rank; ++j)
+                if (eq->lhs.idx[j].kind == TL_IX_NAME && strcmp(eq->lhs.idx[j].name, ix->name) == 0) bound = 1;
+            if (bound) continue;
+            int at = -1;
+            for (int j = 0; j < lv.n; ++j) if (strcmp(lv.names[j], ix->name) == 0) at = j;
+            if (at < 0 && lv.n < MAX_VARS) {
+                at = lv.n++;
+                snprintf(lv.names[at], TL_NAME_LEN, "%s", ix->name);
+                lv.sizes[at] = domain_size(c, ix->name);
+            }
+        }
+    if (lv.n == 0) return bw_eval(c, eq, params, &lv);
+    double acc = 0.0;
+    for (int j = 0; j < lv.n; ++j) { lv.cur[j] = 0; if (lv.sizes[j] <= 0) return acc; }
+    for (;;) {
+        acc = acc + bw_eval(c, eq, params, &lv);
+        if (c->bw_err) return 0.0;
+        int j = lv.n - 1;                      /* the first loop is the outermost */
+        while (j >= 0 && ++lv.cur[j] >= lv.sizes[j]) lv.cur[j--] = 0;
+        if (j < 0) return acc;
+    }
+}
+
+/* @compute_T (genComputeFunction, backward.zig:119-220). */
+static double bw_call(or_ctx* c, bw_global* g, const int64_t* iv) {
+    int64_t off = 0;
+    for (int k = 0; k < g->rank; ++k) off += iv[k] * g->strides[k];
+    if (off < 0 || off >= g->total) return 0.0;   /* outside the memo table */
+    if (g->done[off]) return g->memo[off];
+    if (c->bw_depth >= BW_MAX_DEPTH) { c->bw_err = TL_ERR_TOO_LARGE; return 0.0; }
+    c->bw_depth++;
+    g->done[off] = 1;
+    g->memo[off] = 0.0;
+    double result = 0.0;
+    for (int e = 0; e < g->n_eq && !c->bw_err; ++e) {
+        const tl_equation* eq = &c->bw_stmts[g->eq_stmt[e]].eq;
+        double v = bw_equation(c, eq, iv);
+        switch (eq->accum) {
+        case TL_ACC_ADD: result = result + v; break;
+        case TL_ACC_MAX: result = (v > result) ? v : result; break;
+        case TL_ACC_MIN: result = (v < result) ? v : result; break;
+        case TL_ACC_MUL: result = result * v; break;
+        default: result = 0.0 + v; break;
+        }
+        g->memo[off] = result;
+    }
+    c->bw_depth--;
+    return result;
+}
+
+/* genBackwardQuery (backward.zig:568-600): "%s = %.6g\n". */
+static int bw_query(or_ctx* c, const tl_statement* st, double* out) {
+    bw_global* g = bw_find(c, st->name);
+    if (!g || !g->compute) {
+        snprintf(c->err, sizeof c->err, "%s: a constant-index query needs an equation defining it", st->name);
+        return TL_ERR_UNSUPPORTED;
+    }
+    if (st->sparse.rank != g->rank) {
+        snprintf(c->err, sizeof c->err, "%s: query has %d indices, tensor has %d", st->name, st->sparse.rank, g->rank);
+        return TL_ERR_UNSUPPORTED;
+    }
+    int64_t iv[TL_MAX_RANK];
+    for (int k = 0; k < st->sparse.rank; ++k)
+        iv[k] = st->sparse.idx[k].kind == TL_IX_CONST ? st->sparse.idx[k].value : 0;
+    c->bw_depth = 0;
+    *out = bw_call(c, g, iv);
+    if (c->bw_err) {
+        snprintf(c->err, sizeof c->err, "%s: backward query failed (%d)", st->name, c->bw_err);
+        return c->bw_err;
+    }
+    return TL_OK;
+}
+
+/* ------------------------------------------------------------------------ */
 /* Program (llvm.zig:131-336)                                                 */
 /* ------------------------------------------------------------------------ */
 static void qprintf(or_ctx* c, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
@@ -879,6 +1187,7 @@ or_ctx* or_create(int32_t max_sweeps) {
 void or_destroy(or_ctx* c) {
     if (!c) return;
     for (int i = 0; i < c->n_tensors; ++i) free(c->tensors[i].data);
+    bw_reset(c);
     free(c->qout);
     free(c);
 }
@@ -894,6 +1203,7 @@ static int run_statement(or_ctx* c, const tl_statement* st, const tl_statement* 
             idx[k].kind = TL_IX_NAME;
             snprintf(idx[k].name, TL_NAME_LEN, "%s", st->sparse.idx[k].name);
         }
+        bw_detach(c, st->sparse.tensor);
         return allocate_tensor(c, st->sparse.tensor, idx, st->sparse.rank) ? TL_OK : TL_ERR_OOM;
     }
     case TL_STMT_SPARSE_LOAD: {
@@ -938,6 +1248,8 @@ int32_t or_program_run(or_ctx* c, const tl_statement* stmts, int32_t n) {
         if (stmts[s].kind == TL_STMT_DOMAIN && stmts[s].size >= 0) put_domain(c, stmts[s].name, stmts[s].size);
     for (int s = 0; s < n; ++s)
         if (stmts[s].kind == TL_STMT_EQUATION) update_max_dims(c, &stmts[s].eq.lhs);
+    int brc = bw_prepare(c, stmts, n);
+    if (brc != TL_OK) return brc;
     /* non-recursive statements in source order (llvm.zig:287-301) */
     int n_rec = 0;
     for (int s = 0; s < n; ++s) {
@@ -964,6 +1276,13 @@ int32_t or_program_run(or_ctx* c, const tl_statement* stmts, int32_t n) {
     /* queries (llvm.zig:310-318, 461-480) */
     for (int s = 0; s < n; ++s) {
         if (stmts[s].kind != TL_STMT_QUERY) continue;
+        if (bw_is_query(&stmts[s].sparse)) {
+            double v;
+            int rc = bw_query(c, &stmts[s], &v);
+            if (rc != TL_OK) return rc;
+            qprintf(c, "%s = %.6g\n", stmts[s].name, v);
+            continue;
+        }
         or_tensor* t = find_tensor(c, stmts[s].name);
         if (!t) continue;
         qprintf(c, "%s[%zu] = [", t->name, (size_t)t->total);

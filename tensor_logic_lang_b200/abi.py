@@ -111,7 +111,7 @@ EXPORTS = [
     "tl_tensor_rank", "tl_tensor_dim", "tl_tensor_numel", "tl_tensor_upload",
     "tl_tensor_download", "tl_tensor_upload_f32", "tl_tensor_download_f32",
     "tl_tensor_download_bits", "tl_tensor_device_ptr", "tl_tensor_set", "tl_sparse_upload",
-    "tl_query_format", "tl_set_sharding", "tl_profile_enable", "tl_profile_read",
+    "tl_query_format", "tl_program_output", "tl_set_sharding", "tl_profile_enable", "tl_profile_read",
     "tl_profile_reset", "tl_launch_count", "tl_stream", "tl_closure_noalloc",
 ]
 
@@ -148,6 +148,7 @@ def _declare(lib):
         "tl_tensor_set": (C.c_int32, [vp, P(C.c_int64), C.c_double]),
         "tl_sparse_upload": (C.c_int32, [vp, C.c_int64, P(C.c_int64), P(C.c_int64), P(C.c_double)]),
         "tl_query_format": (C.c_int32, [vp, C.c_char_p, C.c_int64]),
+        "tl_program_output": (C.c_int32, [vp, C.c_char_p, C.c_int64, P(C.c_int64)]),
         "tl_set_sharding": (C.c_int32, [vp, C.c_char_p, C.c_int32]),
         "tl_profile_enable": (C.c_int32, [vp, C.c_int32]),
         "tl_profile_read": (C.c_int32, [vp, P(KernelStats), C.c_int32]),

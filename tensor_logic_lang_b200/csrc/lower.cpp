@@ -981,6 +981,7 @@ extern "C" tl_status tl_sparse_decl(tl_ctx* c, const tl_ref* decl) {
         idx[k].kind = TL_IX_NAME;
         snprintf(idx[k].name, TL_NAME_LEN, "%s", decl->idx[k].name);
     }
+    TL_TRY(bq_detach(c, decl->tensor));
     Tensor* t;
     TL_TRY(allocate_tensor(c, decl->tensor, idx, decl->rank, &t));
     t->is_sparse = true;
@@ -1427,6 +1428,12 @@ static tl_status run_as_graph(tl_ctx* c, const tl_statement* s, int n, const std
     return TL_OK;
 }
 
+static bool is_constant_query(const tl_ref& q) {
+    for (int k = 0; k < q.rank; ++k)
+        if (q.idx[k].kind == TL_IX_CONST) return true;
+    return false;
+}
+
 extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n) {
     if (!c || (n > 0 && !s)) return TL_ERR_INVALID;
     TL_CK(c, cudaSetDevice(c->device));
@@ -1443,6 +1450,12 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
     for (int i = 0; i < n; ++i)
         if (s[i].kind == TL_STMT_EQUATION) eqs.push_back(s[i].eq);
     TL_TRY(tl_declare_dims(c, eqs.data(), (int)eqs.size()));
+    // the globals of constant-index queries exist before the program runs
+    struct BqReset {
+        tl_ctx* c;
+        ~BqReset() { bq_release(c); }
+    } bq_reset{c};
+    TL_TRY(bq_prepare(c, s, n));
     // sign-sensitive tensors: step / comparison arguments, and relu arguments
     // when a backward pass will take relu's gradient step(x)
     bool has_backward = false;
@@ -1473,8 +1486,20 @@ extern "C" tl_status tl_program_run(tl_ctx* c, const tl_statement* s, int32_t n)
     c->lazy_eq = nullptr;
     c->last_sweeps = 0;
     if (!rec.empty()) TL_TRY(run_fixpoint(c, rec.data(), (int)rec.size(), nullptr));
+    // queries in statement order (llvm.zig:309-318): a constant-index query
+    // prints the backward-chaining value (backward.zig:568-600)
+    std::vector<double> backward_values;
+    TL_TRY(bq_run(c, s, n, &backward_values));
+    size_t next_backward = 0;
     for (int i = 0; i < n; ++i) {
         if (s[i].kind != TL_STMT_QUERY) continue;
+        if (next_backward < backward_values.size() && is_constant_query(s[i].sparse)) {
+            char line[64 + TL_NAME_LEN];
+            snprintf(line, sizeof line, "%s = %.6g\n", s[i].name, backward_values[next_backward++]);
+            c->query_out += line;
+            if (c->opts.verbose) fputs(line, stdout);
+            continue;
+        }
         Tensor* t = find_defined(c, s[i].name);
         if (!t) continue;
         std::vector<char> buf(64 + 20 * 32 + strlen(s[i].name));

@@ -146,7 +146,7 @@ tl_status new_tensor(tl_ctx* c, const std::string& name, int rank, const int64_t
     return TL_OK;
 }
 
-static int64_t index_extent(tl_ctx* c, const tl_index* ix) {
+int64_t index_extent(tl_ctx* c, const tl_index* ix) {
     switch (ix->kind) {
     case TL_IX_NAME: case TL_IX_NORMALIZE: case TL_IX_PRIMED: case TL_IX_ADD: case TL_IX_SUB:
         return domain_size(c, ix->name);
@@ -336,6 +336,7 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     cudaFree(c->fix_state);
     cudaFree(c->fix_closed);
     if (c->fix_event) cudaEventDestroy(c->fix_event);
+    bq_release(c);
     cudaFree(c->d_flags);
     cudaFreeHost(c->h_flags);
     cudaStreamDestroy(c->stream);
@@ -717,6 +718,13 @@ extern "C" tl_status tl_query_format(tl_tensor* t, char* buf, int64_t len) {
     for (int64_t i = 0; i < np; ++i) { snprintf(tmp, sizeof tmp, "%.4g ", v[i]); s += tmp; }
     s += "]\n";
     snprintf(buf, (size_t)len, "%s", s.c_str());
+    return TL_OK;
+}
+
+extern "C" tl_status tl_program_output(tl_ctx* c, char* buf, int64_t len, int64_t* needed) {
+    if (!c || (len > 0 && !buf) || len < 0) return TL_ERR_INVALID;
+    if (needed) *needed = (int64_t)c->query_out.size();
+    if (len > 0) snprintf(buf, (size_t)len, "%s", c->query_out.c_str());
     return TL_OK;
 }
 

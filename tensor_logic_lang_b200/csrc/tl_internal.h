@@ -109,6 +109,19 @@ struct PendingEvent {
     double bytes, flops;
 };
 
+// A global of the backward-chaining queries (llvm.zig:222-264): a tensor named
+// by a constant-index query (compute: it has a memo table and is evaluated by
+// recursion) or an equation-defined tensor such a tensor's equations read.
+struct BqHost {
+    std::string name;
+    int rank = 0;
+    int64_t dims[TL_MAX_RANK] = {0};
+    bool compute = false;
+    std::vector<int> eqs;      // statement indices of its equations, program order
+    bool detached = false;     // a `sparse` re-declaration replaced the forward tensor
+    float* snap = nullptr;     // device copy of what it held then (nullptr: zeros)
+};
+
 }  // namespace tl
 
 struct tl_tensor : tl::Tensor {};
@@ -154,6 +167,8 @@ struct tl_ctx {
     bool fix_pending = false, fix_prof = false, fix_last_changed = false;
     double fix_sweep_bytes = 0;
     cudaEvent_t fix_event = nullptr;
+    // globals of this run's constant-index queries
+    std::vector<tl::BqHost> bq;
     // captured program runs (most recently used last)
     std::vector<tl::GraphEntry> graphs;
     uint64_t graph_clock = 0;
@@ -370,5 +385,12 @@ Tensor* find_defined(tl_ctx* c, const std::string& name);
 tl_status allocate_tensor(tl_ctx* c, const char* name, const tl_index* idx, int n, Tensor** out);
 tl_status new_tensor(tl_ctx* c, const std::string& name, int rank, const int64_t* dims, Tensor** out);
 int64_t domain_size(tl_ctx* c, const char* name);
+int64_t index_extent(tl_ctx* c, const tl_index* ix);
+
+// backward-chaining queries (k_query.cu)
+tl_status bq_prepare(tl_ctx* c, const tl_statement* s, int n);
+tl_status bq_detach(tl_ctx* c, const char* name);
+tl_status bq_run(tl_ctx* c, const tl_statement* s, int n, std::vector<double>* out);
+void bq_release(tl_ctx* c);
 
 }  // namespace tl

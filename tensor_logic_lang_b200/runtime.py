@@ -145,6 +145,14 @@ class Context:
         self.check(self.lib.tl_query_format(t, buf, len(buf)), f"query {name}")
         return buf.value.decode()
 
+    def output(self):
+        """What the last program's queries printed (the reference's stdout)."""
+        need = C.c_int64()
+        self.check(self.lib.tl_program_output(self.h, None, 0, C.byref(need)), "program output")
+        buf = C.create_string_buffer(need.value + 1)
+        self.check(self.lib.tl_program_output(self.h, buf, len(buf), None), "program output")
+        return buf.value.decode()
+
     # ------------------------------------------------------------------ profiling
     def profile(self, on=True):
         self.check(self.lib.tl_profile_enable(self.h, 1 if on else 0), "profile")
