@@ -96,6 +96,8 @@ struct PeerRecord {
     int32_t ok;
     int32_t pad[3];
 };
+// a rank's slot array: words [2j, 2j + 1] for rank j's changed words (by sweep
+// parity), then at 2 * kMaxPeers the count of sweeps this context exchanged
 constexpr size_t kSlotBytes = 4096;
 }  // namespace
 

@@ -108,7 +108,9 @@ struct FixArgs {
     unsigned nblocks;
     int world, rank;
     unsigned long long* slots[kMaxPeers];   // every rank's slot array, [rank][parity]
-    unsigned long long token0;              // sweeps this context exchanged before
+    // sweeps this context exchanged before: a device word beside this rank's
+    // slots, advanced by the last sweep's settling thread
+    unsigned long long* token_base;
     unsigned long long timeout_ns;
 };
 
@@ -722,7 +724,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
 // every rank's word of this sweep.  The parity slots keep a rank that is one
 // sweep ahead from overwriting a word not read yet.  Returns the OR.
 __device__ int exchange_changed(const FixArgs& a, int s, int c, int* ok) {
-    const unsigned long long token = a.token0 + (unsigned long long)s + 1;
+    const unsigned long long token = *(volatile const unsigned long long*)a.token_base + (unsigned long long)s + 1;
     const unsigned long long v = (token << 1) | (c ? 1ull : 0ull);
     const int par = s & 1;
     for (int j = 0; j < a.world; ++j) store_release_sys(a.slots[j] + 2 * a.rank + par, v);
@@ -924,6 +926,8 @@ __device__ bool grid_barrier(const FixArgs& a, unsigned gen, int s, bool settle)
                 a.st->sweeps = s + 1;
                 a.st->last_changed = c;
                 a.st->go = (ok && c && s + 1 < a.max_sweeps) ? 1 : 0;
+                // the last sweep of the launch moves the token base past it
+                if (a.world > 1 && !a.st->go) *a.token_base += (unsigned long long)(s + 1);
                 if (s < kFixMarks) a.st->t_settled[s] = global_ns();
             }
             a.st->bar_count = 0;
@@ -1020,6 +1024,15 @@ size_t fix_smem_per_warp(int64_t words) {
 
 }  // namespace
 
+// TL_CLOSURE_SHARDED=local makes each rank close only its own rows, with
+// shortcuts through its own closed rows; the replicated sweep is the default
+// (the local one was slower at 2 and 4 GPUs, and slower at 4 than at 2, as
+// fewer successors are local).
+static bool sharded_sweep_replicates() {
+    const char* m = getenv("TL_CLOSURE_SHARDED");
+    return !(m && !strcmp(m, "local"));
+}
+
 tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweeps, bool need_now, int* sweeps_out,
                                   bool* changed_out, bool* handled) {
     *handled = false;
@@ -1083,14 +1096,17 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // sweep ORs in closed rows (closed words of this launch's epoch)
     const bool lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp;
     const bool shortcut = lazy && words < (int64_t(1) << kClosedSpan);
-    // row-sharded on several GPUs: the lazy sweep closes every row of the
-    // relation in a scratch copy (a row's shortcuts read rows of every
-    // rank's share) and each rank keeps its own rows; only the changed word
-    // crosses GPUs
+    // row-sharded on several GPUs, the lazy sweep runs one of two ways; only
+    // the changed word crosses GPUs in either.  Replicated: every rank closes
+    // every row of the relation in a scratch copy (a row's shortcuts read
+    // rows of every rank's share) and keeps its own rows.  Local: each rank
+    // closes only its own rows and takes shortcuts through its own closed
+    // rows, expanding the successors other ranks hold.
     const bool sharded = R->shard == TL_SHARD_ROWS && c->world > 1;
-    const int64_t dp_rows = shortcut && sharded ? R->dims[0] : rows;
+    const bool replicate = shortcut && sharded && sharded_sweep_replicates();
+    const int64_t dp_rows = replicate ? R->dims[0] : rows;
     uint32_t* dpR = R->bits;
-    if (shortcut && sharded) {
+    if (replicate) {
         void* ws = nullptr;
         TL_TRY(workspace(c, (size_t)std::max<int64_t>(dp_rows, 1) * words * 4, &ws, WS_FIXPOINT));
         dpR = static_cast<uint32_t*>(ws);
@@ -1167,7 +1183,7 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.epoch = c->fix_epoch;
     a.dpR = dpR;
     a.dp_rows = dp_rows;
-    a.dp_copy = shortcut && sharded ? 1 : 0;
+    a.dp_copy = replicate ? 1 : 0;
     // local row r is global row r * world + rank of a row-sharded relation
     a.row_stride = 1;
     a.row_offset = 0;
@@ -1183,7 +1199,7 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.world = c->world;
     a.rank = c->rank;
     for (int j = 0; j < kMaxPeers; ++j) a.slots[j] = c->peer_slots[j];
-    a.token0 = c->peer_tokens;
+    a.token_base = c->world > 1 ? static_cast<unsigned long long*>(c->peer_own) + 2 * kMaxPeers : nullptr;
     a.timeout_ns = (unsigned long long)std::max(c->opts.comm_timeout_ms, 1000) * 1000000ull;
 
     const double sweep_bytes = (double)rows * words * 8.0 + (double)nodes * 32.0;
@@ -1195,9 +1211,8 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         TL_TRY(L.done());
     }
     // the control block comes back to pinned memory behind the launch; it is
-    // read at once only when the caller needs the sweep count, when profiling
-    // (the phase marks), or on several GPUs (the peer token count must be
-    // known before the next launch); otherwise when the context next syncs,
+    // read at once only when the caller needs the sweep count or when
+    // profiling (the phase marks); otherwise when the context next syncs,
     // asks for the sweep count or launches another fixpoint
     TL_CK(c, cudaMemcpyAsync(c->h_flags + 32, c->fix_state, sizeof(FixState), cudaMemcpyDeviceToHost, c->stream));
     if (!c->fix_event) TL_CK(c, cudaEventCreateWithFlags(&c->fix_event, cudaEventDisableTiming));
@@ -1208,7 +1223,7 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     R->lazy_src = nullptr;   // every row is written now (or the status of the launch says why not)
     *sweeps_out = -1;
     *changed_out = false;
-    if (!need_now && !c->prof && c->world == 1) return TL_OK;
+    if (!need_now && !c->prof) return TL_OK;
     TL_TRY(fix_resolve(c));
     *sweeps_out = c->last_sweeps;
     *changed_out = c->fix_last_changed;
@@ -1248,7 +1263,6 @@ tl_status fix_resolve(tl_ctx* c) {
             prev = h.t_settled[s];
         }
     }
-    if (c->world > 1) c->peer_tokens += (unsigned long long)h.sweeps;
     c->last_sweeps = h.sweeps;
     c->fix_last_changed = h.last_changed != 0;
     if (h.err) {

@@ -1015,11 +1015,14 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
     }
 }
 
-// A warp per query row: the key tiles' statistics combined (m*, l*) and the
-// row of O (lane l: columns 2l, 2l + 1); m* and 1 / l* kept for the row of A.
+// A warp per query row: the key tiles' statistics combined (m*, l*), the row
+// of O (lane l: columns 2l, 2l + 1), then the row of A = exp(S - m*) / l*
+// from the scores the tile kernel stored (n_k a multiple of 4; 128-bit loads
+// and stores, 8 in flight per lane).
 __global__ void __launch_bounds__(256)
     k_attn_rows(const float* __restrict__ opart, const float* __restrict__ mpart, const float* __restrict__ lpart,
-                int n_kt, int64_t n_q, float2* __restrict__ stat, float* __restrict__ O, int64_t lo) {
+                int n_kt, int64_t n_q, float* __restrict__ O, int64_t lo, const float* __restrict__ S,
+                float* __restrict__ A, int64_t n_k) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_q; r += warps) {
@@ -1059,33 +1062,23 @@ __global__ void __launch_bounds__(256)
             }
         }
         *reinterpret_cast<float2*>(O + r * lo + 2 * lane) = make_float2(o0 * inv, o1 * inv);
-        if (lane == 0) stat[r] = make_float2(mstar, inv);
-    }
-}
-
-// A = exp(S - m*) / l* over the whole matrix, 128-bit loads and stores
-// (n_k a multiple of 4): each thread keeps 4 loads in flight.
-__global__ void __launch_bounds__(256)
-    k_attn_probs(const float* __restrict__ S, const float2* __restrict__ stat, int64_t n_q, int64_t n_k,
-                 float* __restrict__ A) {
-    const int64_t per_row = n_k / 4, total = n_q * per_row;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 4 * stride) {
-        float4 v[4];
-        float2 st[4];
+        const int64_t q4 = n_k / 4;
+        const float4* Sr = reinterpret_cast<const float4*>(S + r * n_k);
+        float4* Ar = reinterpret_cast<float4*>(A + r * n_k);
+        for (int64_t j0 = lane; j0 < q4; j0 += 32 * 8) {
+            float4 v[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int64_t i = i0 + u * stride;
-            v[u] = i < total ? reinterpret_cast<const float4*>(S)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-            st[u] = i < total ? stat[i / per_row] : make_float2(0.f, 0.f);
-        }
+            for (int u = 0; u < 8; ++u) {
+                const int64_t j = j0 + 32 * u;
+                v[u] = j < q4 ? Sr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int64_t i = i0 + u * stride;
-            if (i < total)
-                reinterpret_cast<float4*>(A)[i] =
-                    make_float4(__expf(v[u].x - st[u].x) * st[u].y, __expf(v[u].y - st[u].x) * st[u].y,
-                                __expf(v[u].z - st[u].x) * st[u].y, __expf(v[u].w - st[u].x) * st[u].y);
+            for (int u = 0; u < 8; ++u) {
+                const int64_t j = j0 + 32 * u;
+                if (j < q4)
+                    Ar[j] = make_float4(__expf(v[u].x - mstar) * inv, __expf(v[u].y - mstar) * inv,
+                                        __expf(v[u].z - mstar) * inv, __expf(v[u].w - mstar) * inv);
+            }
         }
     }
 }
@@ -1286,7 +1279,7 @@ tl_status launch_attention(tl_ctx* c, const AttnPlan& p) {
     const int n_kt = (int)(p.n_k / AT_KEYS);
     const size_t part = (size_t)n_kt * p.n_q;
     void* ws = nullptr;
-    TL_TRY(workspace(c, part * (AT_D + 2) * sizeof(float) + (size_t)p.n_q * sizeof(float2) + 16, &ws, WS_GEMM));
+    TL_TRY(workspace(c, part * (AT_D + 2) * sizeof(float), &ws, WS_GEMM));
     AttnArgs a;
     a.S = p.S;
     a.ls = p.n_k;
@@ -1308,19 +1301,12 @@ tl_status launch_attention(tl_ctx* c, const AttnPlan& p) {
         k_attn_tile<<<dim3((unsigned)(p.n_q / AT_ROWS), (unsigned)n_kt), AT_THREADS, AT_SMEM, c->stream>>>(mq, mk, mv, ms, a);
         TL_TRY(L.done());
     }
-    // per-row (m*, 1 / l*) after the partials, 8-byte aligned
-    float2* stat = reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(a.lpart + part) + 7) & ~uintptr_t(7));
     {
-        LaunchScope L(c, "attention_combine", (double)part * (AT_D + 2) * 4.0 + (double)p.n_q * AT_D * 4.0);
+        LaunchScope L(c, "attention_combine",
+                      (double)part * (AT_D + 2) * 4.0 + (double)p.n_q * AT_D * 4.0 + (double)p.n_q * p.n_k * 8.0);
         const int64_t blocks = std::min<int64_t>((p.n_q + 7) / 8, (int64_t)c->sm_count * 8);
-        k_attn_rows<<<(unsigned)blocks, 256, 0, c->stream>>>(a.opart, a.mpart, a.lpart, n_kt, p.n_q, stat, p.O, AT_D);
-        TL_TRY(L.done());
-    }
-    {
-        LaunchScope L(c, "attention_probs", (double)p.n_q * p.n_k * 8.0);
-        const int64_t quads = p.n_q * p.n_k / 4;
-        const int64_t blocks = std::min<int64_t>((quads + 1023) / 1024, (int64_t)c->sm_count * 16);
-        k_attn_probs<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, c->stream>>>(p.S, stat, p.n_q, p.n_k, p.A);
+        k_attn_rows<<<(unsigned)blocks, 256, 0, c->stream>>>(a.opart, a.mpart, a.lpart, n_kt, p.n_q, p.O, AT_D, p.S,
+                                                             p.A, p.n_k);
         TL_TRY(L.done());
     }
     return TL_OK;

@@ -503,6 +503,7 @@ static tl_status download_f32(tl_ctx* c, Tensor* t, float** st_out, int64_t* n_o
         TL_TRY(ensure_dense(c, t));
         TL_CK(c, cudaMemcpyAsync(st, t->dense, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
         TL_CK(c, cudaStreamSynchronize(c->stream));
+        TL_TRY(check_device_flags(c));   // values a timed-out pipeline left are not returned as valid
     }
     *st_out = st;
     *n_out = n;
@@ -536,7 +537,7 @@ extern "C" tl_status tl_tensor_download_bits(tl_tensor* t, uint32_t* host) {
     TL_TRY(ensure_bits(c, t));
     TL_CK(c, cudaMemcpyAsync(host, t->bits, t->bits_rows * t->bits_words * 4, cudaMemcpyDeviceToHost, c->stream));
     TL_CK(c, cudaStreamSynchronize(c->stream));
-    return TL_OK;
+    return check_device_flags(c);
 }
 
 extern "C" tl_status tl_tensor_device_ptr(tl_tensor* t, float** dptr) {

@@ -181,7 +181,6 @@ struct tl_ctx {
     int peer_state = 0;                              // 0 not tried, 1 ready, -1 unavailable
     unsigned long long* peer_slots[tl::kMaxPeers] = {};
     void* peer_own = nullptr;                        // this rank's slot array
-    unsigned long long peer_tokens = 0;              // sweeps exchanged so far
 
     // profiling
     bool prof = false;
