@@ -314,8 +314,8 @@ __global__ void __launch_bounds__(256) k_closure_left(const uint32_t* __restrict
     }
 }
 
-// out[v, :] (+)= sum_e vals[e] * P[col(e), :], one warp per row, 4 columns
-// per lane per step (128-bit loads of P rows).
+// out[v, :] (+)= sum_e vals[e] * P[col(e), :], one warp per row, 128-bit
+// loads of the gathered P rows (4 columns per lane and column half).
 __global__ void __launch_bounds__(256) k_spmm(int64_t rows, const int64_t* __restrict__ rowptr,
                                               const int32_t* __restrict__ colidx, const float* __restrict__ vals,
                                               const float* __restrict__ P, int64_t ldp, int64_t f, float* out,
@@ -326,19 +326,56 @@ __global__ void __launch_bounds__(256) k_spmm(int64_t rows, const int64_t* __res
     for (int64_t v = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); v < rows; v += warps) {
         const int64_t e0 = rowptr[v], e1 = rowptr[v + 1];
         if (vec) {
-            for (int64_t j = lane * 4; j < f; j += 128) {
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int64_t e = e0; e < e1; ++e) {
-                    int64_t u = colidx[e];
-                    if (col_world > 1) u = (u % col_world) * col_local + u / col_world;
-                    const float a = vals[e];
-                    const float4 pv = __ldg(reinterpret_cast<const float4*>(P + u * ldp + j));
-                    acc.x = fmaf(a, pv.x, acc.x); acc.y = fmaf(a, pv.y, acc.y);
-                    acc.z = fmaf(a, pv.z, acc.z); acc.w = fmaf(a, pv.w, acc.w);
+            // the row's column indices and values 32 at a time, one per lane,
+            // broadcast by shuffles; 4 nonzeros x 2 column halves (8 row
+            // gathers) in flight per lane.  Each element still sums its terms
+            // in nonzero order.
+            for (int64_t jb = 0; jb < f; jb += 256) {
+                const int64_t j0 = jb + lane * 4, j1 = j0 + 128;
+                const bool h0 = j0 < f, h1 = j1 < f;
+                float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+                for (int64_t eb = e0; eb < e1; eb += 32) {
+                    const int ne = (int)(e1 - eb < 32 ? e1 - eb : 32);
+                    long long u_l = 0;
+                    float w_l = 0.f;
+                    if (lane < ne) {
+                        int64_t u = colidx[eb + lane];
+                        if (col_world > 1) u = (u % col_world) * col_local + u / col_world;
+                        u_l = (long long)u;
+                        w_l = vals[eb + lane];
+                    }
+                    for (int k = 0; k < ne; k += 4) {
+                        float4 p0[4], p1[4];
+                        float w[4];
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const long long u = __shfl_sync(0xffffffffu, u_l, (k + t) & 31);
+                            w[t] = __shfl_sync(0xffffffffu, w_l, (k + t) & 31);
+                            const bool ok = k + t < ne;
+                            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+                            p0[t] = ok && h0 ? __ldg(reinterpret_cast<const float4*>(P + u * ldp + j0)) : z;
+                            p1[t] = ok && h1 ? __ldg(reinterpret_cast<const float4*>(P + u * ldp + j1)) : z;
+                        }
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            if (k + t >= ne) break;
+                            a0.x = fmaf(w[t], p0[t].x, a0.x); a0.y = fmaf(w[t], p0[t].y, a0.y);
+                            a0.z = fmaf(w[t], p0[t].z, a0.z); a0.w = fmaf(w[t], p0[t].w, a0.w);
+                            a1.x = fmaf(w[t], p1[t].x, a1.x); a1.y = fmaf(w[t], p1[t].y, a1.y);
+                            a1.z = fmaf(w[t], p1[t].z, a1.z); a1.w = fmaf(w[t], p1[t].w, a1.w);
+                        }
+                    }
                 }
-                float4* op = reinterpret_cast<float4*>(out + v * ldo + j);
-                if (beta) { const float4 o = *op; acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w; }
-                *op = acc;
+                if (h0) {
+                    float4* op = reinterpret_cast<float4*>(out + v * ldo + j0);
+                    if (beta) { const float4 o = *op; a0.x += o.x; a0.y += o.y; a0.z += o.z; a0.w += o.w; }
+                    *op = a0;
+                }
+                if (h1) {
+                    float4* op = reinterpret_cast<float4*>(out + v * ldo + j1);
+                    if (beta) { const float4 o = *op; a1.x += o.x; a1.y += o.y; a1.z += o.z; a1.w += o.w; }
+                    *op = a1;
+                }
             }
         } else {
             for (int64_t j = lane; j < f; j += 32) {
