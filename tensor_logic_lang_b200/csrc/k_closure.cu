@@ -631,7 +631,15 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         int n_init = __popc(fresh);
         unsigned long long nb2 = 0;
         if (lane == 0) nb2 = atomicAdd(next_row, 1ull);   // the row after this one
-        const bool closed = f && l0 >= 0 && (uint32_t)(cw >> 42) == a.epoch;
+        bool closed = f && l0 >= 0 && (uint32_t)(cw >> 42) == a.epoch;
+        // a successor that read as open when its word was fetched (a row
+        // earlier) has often closed since: read those words once more, so
+        // fewer successors are expanded
+        unsigned long long cw_now = cw;
+        if (__any_sync(0xffffffffu, f && l0 >= 0 && !closed) && f && l0 >= 0 && !closed) {
+            cw_now = load_acquire_gpu(&a.closed[l0]);
+            closed = (uint32_t)(cw_now >> 42) == a.epoch;
+        }
         const unsigned open = __ballot_sync(0xffffffffu, f && !closed);
         if (f && !closed) q[__popc(open & lanes_below)] = (uint32_t)s0;
         S.tail = __popc(open);
@@ -653,8 +661,8 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         nb = __shfl_sync(0xffffffffu, nb2, 0);
         t_next = slot_of(nb);
         __syncwarp();
-        or_closed_rows(a, closed, l0, (int)(cw & ((1u << kClosedSpan) - 1u)),
-                       (int)((cw >> kClosedSpan) & ((1u << kClosedSpan) - 1u)), row, vec, lane);
+        or_closed_rows(a, closed, l0, (int)(cw_now & ((1u << kClosedSpan) - 1u)),
+                       (int)((cw_now >> kClosedSpan) & ((1u << kClosedSpan) - 1u)), row, vec, lane);
         __syncwarp();
         // its successors' closed words, in flight during the search and write-back
         cw_next = closed_of(t_next);
