@@ -737,20 +737,39 @@ __global__ void __launch_bounds__(256) k_prep_rows(const float* __restrict__ S, 
                                                    int tpr_log2) {
     const int tpr = 1 << tpr_log2, rpb = 256 >> tpr_log2;
     const int t = threadIdx.x & (tpr - 1);
-    for (int64_t i = (int64_t)blockIdx.y * rpb + (threadIdx.x >> tpr_log2); i < rows; i += (int64_t)gridDim.y * rpb) {
-        const float* src = S + i * src_rs;
-        float* dst = D + i * dst_rs;
-        if (vec) {
+    const int64_t row_step = (int64_t)gridDim.y * rpb;
+    if (vec) {
+        // up to four rows per thread (as the grid leaves them), their loads
+        // issued before any store
+        for (int64_t i0 = (int64_t)blockIdx.y * rpb + (threadIdx.x >> tpr_log2); i0 < rows; i0 += 4 * row_step) {
             for (int64_t j = ((int64_t)blockIdx.x * tpr + t) * 4; j < len; j += (int64_t)gridDim.x * tpr * 4) {
-                float4 x = *reinterpret_cast<const float4*>(src + j);
-                x.x *= sgn; x.y *= sgn; x.z *= sgn; x.w *= sgn;
-                for (int s = 0; s < nseg; ++s) {
-                    const int op = (ops >> (4 * s)) & 15;
-                    *reinterpret_cast<float4*>(dst + s * dst_ss + j) =
-                        make_float4(seg_op(op, x.x), seg_op(op, x.y), seg_op(op, x.z), seg_op(op, x.w));
+                float4 x[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int64_t i = i0 + u * row_step;
+                    x[u] = i < rows ? *reinterpret_cast<const float4*>(S + i * src_rs + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int64_t i = i0 + u * row_step;
+                    if (i >= rows) break;
+                    float4 y = x[u];
+                    y.x *= sgn; y.y *= sgn; y.z *= sgn; y.w *= sgn;
+                    float* dst = D + i * dst_rs;
+                    for (int s = 0; s < nseg; ++s) {
+                        const int op = (ops >> (4 * s)) & 15;
+                        *reinterpret_cast<float4*>(dst + s * dst_ss + j) =
+                            make_float4(seg_op(op, y.x), seg_op(op, y.y), seg_op(op, y.z), seg_op(op, y.w));
+                    }
                 }
             }
-        } else {
+        }
+        return;
+    }
+    for (int64_t i = (int64_t)blockIdx.y * rpb + (threadIdx.x >> tpr_log2); i < rows; i += row_step) {
+        const float* src = S + i * src_rs;
+        float* dst = D + i * dst_rs;
+        {
             for (int64_t j = (int64_t)blockIdx.x * tpr + t; j < len; j += (int64_t)gridDim.x * tpr) {
                 const float x = src[j] * sgn;
                 for (int s = 0; s < nseg; ++s) dst[s * dst_ss + j] = seg_op((ops >> (4 * s)) & 15, x);
@@ -796,7 +815,7 @@ __global__ void k_prep_transpose(const float* __restrict__ S, int64_t s_r, int64
 //    tensor cores read (over Q and K, done with by then); O_tile = P V goes
 //    into TMEM with a second tcgen05.mma and is stored unnormalised with m and
 //    l.  97 KB of shared memory: two CTAs per SM.
-//  * k_attn_combine, a warp per query row: m* = max of the tiles' m, l* = sum
+//  * k_attn_rows, a warp per query row: m* = max of the tiles' m, l* = sum
 //    of exp(m - m*) l, O = sum of exp(m - m*) O_tile / l*, and the row of A =
 //    exp(S - m*) / l* from the stored scores.
 // The softmax subtracts the row maximum, as the row-wise kernel does; the
@@ -1371,8 +1390,13 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
             int tl = 0;   // threads per row: the power of two that covers the row, at most 256
             while ((1 << tl) < per_row && tl < 8) ++tl;
             const int64_t rpb = 256 >> tl;
-            dim3 g((unsigned)std::min<int64_t>((per_row + 255) / 256, 64),
-                   (unsigned)std::min<int64_t>((rows + rpb - 1) / rpb, 65535));
+            // the vector path takes four rows per thread when one row each
+            // would give at least four blocks per SM (a small operand keeps
+            // one row per thread, so enough blocks stay in flight)
+            const int64_t gx = std::min<int64_t>((per_row + 255) / 256, 64);
+            int64_t row_groups = (rows + rpb - 1) / rpb;
+            if (vec && gx * row_groups >= 4 * (int64_t)c->sm_count) row_groups = (rows + 4 * rpb - 1) / (4 * rpb);
+            dim3 g((unsigned)gx, (unsigned)std::min<int64_t>(row_groups, 65535));
             k_prep_rows<<<g, 256, 0, c->stream>>>(src, src_rs, rows, len, nseg, q->ops, q->sgn, q->dst, q->ld, dst_ss,
                                                   vec ? 1 : 0, tl);
         } else {
