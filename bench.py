@@ -126,7 +126,8 @@ class Dist:
 
             import torch
             import torch.distributed as td
-            torch.cuda.set_device(local)
+            if torch.cuda.is_available():
+                torch.cuda.set_device(local)
             td.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
             self.td = td
 
@@ -156,6 +157,14 @@ class Dist:
         t = torch.tensor([float(x)], dtype=torch.float64)
         self.td.all_reduce(t, op=self.td.ReduceOp.SUM)
         return float(t.item())
+
+    def gather(self, obj):
+        """Every rank's `obj` on rank 0 (in rank order); None elsewhere."""
+        if self.world == 1:
+            return [obj]
+        out = [None] * self.world if self.rank == 0 else None
+        self.td.gather_object(obj, out, dst=0)
+        return out
 
     def close(self):
         if self.world > 1:
@@ -319,10 +328,106 @@ def run_closure(args, dist, peaks):
     e2e = {"value": total_sweeps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
            "d2h_bytes_per_step": int(d2h)}
     reach_pairs = dist.sum(int(np.unpackbits(out_bits.view(np.uint8)).sum()))
-    res = dict(value=value, ms=ms_max, sweeps=sweeps, launches=launches, roofline=roof, clocks=clk, e2e=e2e,
-               reach_pairs=int(reach_pairs), nnz=nnz, kernels=prof)
     ctx.close()
+    parity = closure_parity(dist, out_bits, sweeps, rows, cols)
+    res = dict(value=value, ms=ms_max, sweeps=sweeps, launches=launches, roofline=roof, clocks=clk, e2e=e2e,
+               reach_pairs=int(reach_pairs), nnz=nnz, kernels=prof, parity=parity)
     return res
+
+
+def row_digests(bits):
+    import hashlib
+    return [hashlib.blake2b(r.tobytes(), digest_size=8).digest() for r in bits]
+
+
+def closure_parity(dist, out_bits, sweeps, rows, cols):
+    """Bit-exact check of the relation every rank computed (its cyclic share
+    of the rows, from the last end-to-end step) against the f64 oracle's
+    closure: rank 0 gathers one 8-byte digest per row and compares it with
+    the digest of the oracle's row, and the sweep counts.  The oracle is the
+    checker here, run after the timed and end-to-end regions."""
+    from tensor_logic_lang_b200 import inputs as gen
+    digests = dist.gather((row_digests(out_bits), sweeps))
+    if dist.rank != 0:
+        return None
+    from oracle import oracle
+    n = N_CLOSURE
+    t0 = time.perf_counter()
+    colptr, rowidx = gen.csr_from_coo(n, cols, rows)
+    R = np.zeros((n, n // 32), dtype=np.uint32)
+    np.bitwise_or.at(R, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
+    osw = oracle.closure_right(n, colptr, rowidx, R, threads=os.cpu_count() or 1)
+    want = row_digests(R)
+    world = len(digests)
+    bad = sum(1 for r, (dg, _) in enumerate(digests) for k, d in enumerate(dg) if d != want[k * world + r])
+    checked = sum(len(dg) for dg, _ in digests)
+    sw_ok = all(sw == osw for _, sw in digests)
+    return {"closure": "bit-exact" if bad == 0 and checked == n and sw_ok else "MISMATCH",
+            "rows_checked": checked, "rows_differing": bad, "sweeps": [sw for _, sw in digests],
+            "oracle_sweeps": osw, "oracle_s": round(time.perf_counter() - t0, 2),
+            "how": "blake2b digest of every row gathered from every rank vs the f64 oracle's closure_right"}
+
+
+# ---------------------------------------------------------------------------- GNN rows over ranks
+def run_gnn_sharded(args, dist, peaks):
+    """The 2-layer GNN (n=16384, f=256) with the node rows of Adj, H0, H1
+    and H2 dealt cyclically over the ranks: each rank computes P = relu-per-
+    term H W for its rows, one NCCL all-gather of P per layer, then the CSR
+    SpMM of its own output rows.  Device time per step (max over ranks), and
+    H1, H2 gathered to rank 0 and checked against the f64 oracle."""
+    import torch
+
+    from tensor_logic_lang_b200 import abi, configs, shard
+    from tensor_logic_lang_b200 import inputs as gen
+    from tensor_logic_lang_b200.runtime import Context, unique_id
+    nid = dist.bcast_bytes(unique_id() if dist.rank == 0 else None) if dist.world > 1 else None
+    ctx = Context(device=dist.local, rank=dist.rank, world_size=dist.world, nccl_id=nid)
+    if dist.world > 1:
+        for name in ("Adj", "H0", "H1", "H2"):
+            ctx.set_sharding(name, abi.SHARD_ROWS)
+    p, data, sparse, flops = configs.program(configs.gnn)
+    ctx.run(p)
+    p_res = configs.program(configs.gnn)[0]
+    for k in range(p_res.n):
+        st = p_res.stmts[k]
+        if st.kind == 6:
+            st.host_data = None
+            st.path = b""
+        if st.kind == 7:
+            st.coo_rows = None
+            st.coo_cols = None
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=f"cuda:{dist.local}")
+    ms, launches = time_steps(ctx, lambda: ctx.run(p_res), args.steps, args.warmup, dist, flush)
+    ms_max = dist.max(ms)
+    per = ms_max / args.steps
+    n = data["H0"].shape[0]
+    rows = shard.local_count(n, dist.rank, dist.world)
+    h1 = ctx.tensor("H1", rows=rows).astype(np.float32)
+    h2 = ctx.tensor("H2", rows=rows).astype(np.float32)
+    ctx.close()
+    got = dist.gather((h1, h2))
+    out = {"workload": "2-layer GNN n=16384 f=256, rows cyclic over the GPUs", "ms_per_step": round(per, 4),
+           "tflops": round(flops / (per / 1e3) / 1e12, 3), "algo_flops": flops,
+           "gpu_launches_per_step": launches / args.steps}
+    if dist.rank != 0:
+        return None
+    from oracle import oracle
+    t0 = time.perf_counter()
+    H1 = shard.assemble([g[0] for g in got], n)
+    H2 = shard.assemble([g[1] for g in got], n)
+    r_rows, r_cols, _ = sparse["Adj"]
+    rowptr, colidx = gen.csr_from_coo(n, r_rows, r_cols)
+    threads = os.cpu_count() or 1
+    r1 = oracle.gnn_layer(rowptr, colidx, data["H0"], data["W1"], threads=threads)
+    r2 = oracle.gnn_layer(rowptr, colidx, r1, data["W2"], threads=threads)
+
+    def rel(a, b):
+        return float(np.max(np.abs(a.astype(np.float64) - b)) / max(np.max(np.abs(b)), 1e-30))
+    e1, e2 = rel(H1, r1), rel(H2, r2)
+    out["parity"] = {"gnn": "within 1e-3" if max(e1, e2) <= 1e-3 else "MISMATCH", "tol": 1e-3,
+                     "rel_err_H1": e1, "rel_err_H2": e2, "oracle_s": round(time.perf_counter() - t0, 2),
+                     "how": "max|g-r|/max|r| of H1, H2 gathered from every rank vs the f64 oracle's gnn_layer"}
+    return out
 
 
 # ---------------------------------------------------------------------------- einsum configs
@@ -475,6 +580,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-einsum", action="store_true")
+    ap.add_argument("--no-gnn", action="store_true", help="skip the row-sharded GNN leg")
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
     ap.add_argument("--workload", default="all",
                     choices=["all", "closure", "mlp_forward", "attention", "mlp_train", "gnn", "rowwise"],
@@ -502,6 +608,7 @@ def main():
         dist.close()
         return 0
     res = run_closure(args, dist, peaks)
+    gnn = run_gnn_sharded(args, dist, peaks) if args.workload == "all" and not args.no_gnn else None
     einsum = None
     rowwise = None
     cpu = None
@@ -527,6 +634,10 @@ def main():
             "gpu_launches": int(res["launches"]), "roofline": res["roofline"], "cpu_baseline": cpu,
             "e2e": res["e2e"], "clocks": res["clocks"],
         }
+        if res["parity"]:
+            line["parity"] = res["parity"]
+        if gnn:
+            line["gnn_sharded"] = gnn
         if einsum:
             line["einsum"] = einsum
         if rowwise:

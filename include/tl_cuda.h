@@ -50,7 +50,10 @@ typedef int32_t tl_status;
 #define TL_ERR_OOM            2  /* device or host allocation failed          */
 #define TL_ERR_CUDA           3  /* a CUDA call or kernel failed              */
 #define TL_ERR_COMM           4  /* an NCCL call failed or timed out          */
-#define TL_ERR_NOT_CONVERGED  5  /* fixpoint hit its sweep cap (1000)         */
+#define TL_ERR_NOT_CONVERGED  5  /* reserved: a fixpoint that reaches its     */
+                                 /* sweep cap returns TL_OK with the cap as   */
+                                 /* its sweep count, as the reference stops   */
+                                 /* silently (fixpoint.zig:67-72)             */
 #define TL_ERR_UNSUPPORTED    6  /* form the backend does not lower           */
 #define TL_ERR_NOT_FOUND      7  /* unknown tensor name                       */
 #define TL_ERR_IO             8  /* save/load file error                      */
@@ -351,14 +354,14 @@ void* tl_stream(const tl_ctx* ctx);
 /* No counterpart in the reference.  For callers that must not allocate GPU */
 /* memory: a host application whose device memory belongs to its own pool   */
 /* or arena (a serving process under a fixed memory budget, a framework     */
-/* whose caching allocator owns the device), or a caller preparing work     */
-/* around stream capture, where cudaMalloc would synchronise the device or   */
-/* break the capture.  Such a caller cannot create a tl_ctx (tl_init         */
-/* allocates), so this entry point takes no context: every input and output */
-/* is caller-owned device memory, and the fixpoint's scratch (one word per   */
-/* row plus control words) lives in a fixed array inside the library, sized  */
-/* for at most TL_NOALLOC_MAX_ROWS rows (about 256 KiB, held by every GPU    */
-/* that loads the library until the process exits).                          */
+/* whose caching allocator must account for every byte on the device), so   */
+/* that a cudaMalloc behind the pool's back is not allowed.  Such a caller   */
+/* cannot create a tl_ctx (tl_init allocates), so this entry point takes no */
+/* context: every input and output is caller-owned device memory, and the   */
+/* fixpoint's scratch (one word per row plus control words) lives in a fixed */
+/* array inside the library, sized for at most TL_NOALLOC_MAX_ROWS rows      */
+/* (about 256 KiB, held by every GPU that loads the library until the        */
+/* process exits).                                                           */
 /*                                                                           */
 /* Computes Reach[x,z] max= step(Reach[x,y] Edge[y,z]) to its fixpoint, the  */
 /* same sweeps tl_fixpoint runs for this equation:                           */
@@ -370,13 +373,19 @@ void* tl_stream(const tl_ctx* ctx);
 /*   d_reach   in: the initial 0/1 relation, out: the fixpoint; n rows of    */
 /*             ceil(n/32) uint32 words, bit (z & 31) of word z >> 5 = [x,z]  */
 /*   max_sweeps  the sweep cap (0 = 1000, as fixpoint.zig:67-72)            */
-/*   stream    the cudaStream_t to run on (NULL = the default stream)        */
+/*   stream    the cudaStream_t to run on (NULL = the default stream); it    */
+/*             must belong to the current device (else TL_ERR_INVALID),      */
+/*             whose copy of the scratch array the call uses                 */
 /*   sweeps_out  receives the sweep count (may be NULL)                      */
-/* The first call on a device looks up the scratch array's device address    */
-/* (cudaGetSymbolAddress) and should happen before any stream capture.       */
-/* Every call shares the one array, so calls that overlap on the GPU (other  */
-/* streams, other host threads) race; serialise them.  The call returns      */
-/* after the fixpoint has converged (it reads the changed word each sweep).  */
+/* The call is synchronous: after every sweep it copies the changed word to  */
+/* the host and waits for the stream, so it returns with d_reach final, and  */
+/* it must not be called while the stream is capturing.  It returns TL_OK    */
+/* when a sweep changed nothing or when the cap was reached (then            */
+/* *sweeps_out == max_sweeps and the relation may not be closed, as the      */
+/* reference stops silently at its cap).  The first call on a device looks   */
+/* up the scratch array's device address (cudaGetSymbolAddress).  Every call */
+/* shares the one array, so calls that overlap on the GPU (other streams,    */
+/* other host threads) race; serialise them.                                 */
 /* ------------------------------------------------------------------------ */
 #define TL_NOALLOC_MAX_ROWS 65536
 tl_status tl_closure_noalloc(int64_t n, const int64_t* d_rowptr, const int32_t* d_colidx,

@@ -942,9 +942,13 @@ __device__ bool grid_barrier(const FixArgs& a, unsigned gen, int s, bool settle)
             __threadfence();
             atomicExch(&a.st->bar_gen, gen);
         } else {
+            // the settling block may itself wait up to timeout_ns for the
+            // other ranks: the blocks waiting for it allow twice that, so a
+            // peer wait that runs out is the one reported
             const unsigned long long t0 = global_ns();
+            const unsigned long long lim = a.world > 1 ? 2 * a.timeout_ns : a.timeout_ns;
             while (*(volatile unsigned*)&a.st->bar_gen < gen) {
-                if (global_ns() - t0 > a.timeout_ns) {
+                if (global_ns() - t0 > lim) {
                     atomicExch(&a.st->err, 1);
                     ok = 0;
                     break;

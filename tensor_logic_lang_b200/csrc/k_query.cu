@@ -18,7 +18,10 @@
 // by the plan's capacity and not by a thread stack.  All backward queries of a
 // program run in one launch, in statement order, sharing the memo tables the
 // way the reference's globals do.  The interpreter counts the steps it takes
-// and stops with an error status past a fixed budget; it has no waits.
+// and stops with an error status past a step budget or a time limit on
+// %globaltimer (defaults 2^31 steps and 4 s; TL_BQ_MAX_STEPS and TL_BQ_MAX_MS
+// set them per run), so a deep query cannot hold the GPU for minutes; it has
+// no waits.
 //
 // Arithmetic is f64 with the reference's operation order and no contraction
 // (__dadd_rn and friends); forward tensors are read from their fp32 device
@@ -37,6 +40,8 @@ namespace {
 constexpr int kBqVars = 16;
 constexpr int64_t kBqMaxFrames = int64_t(1) << 20;
 constexpr int64_t kBqMaxSteps = int64_t(1) << 31;
+constexpr int64_t kBqMaxMs = 4000;
+constexpr int64_t kBqClockEvery = 1024;   // steps between reads of %globaltimer
 constexpr double kBqMaxMemoBytes = 16.0 * (1 << 30);
 
 // one index of a tensor reference: a constant, a parameter of the function
@@ -93,9 +98,16 @@ struct BqArgs {
     double* memo;
     uint8_t* done;
     double* out;
-    int* status;                // 0 ok, 1 frame capacity, 2 step budget
+    int* status;                // 0 ok, 1 frame capacity, 2 step budget, 3 time limit
     int64_t max_steps;
+    unsigned long long max_ns;  // time limit of the launch
 };
+
+__device__ __forceinline__ unsigned long long bq_now_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 // genBackwardExpr's nonlinearities (backward.zig:419-457): sigmoid has no
 // temperature here, and every other function is the identity.
@@ -156,6 +168,7 @@ __global__ void __launch_bounds__(32) k_backward_query(BqArgs a) {
     if (threadIdx.x != 0) return;
     int status = 0;
     int64_t steps = 0;
+    const unsigned long long t0 = bq_now_ns();
     for (int q = 0; q < a.n_q && status == 0; ++q) {
         const BqQuery& Q = a.q[q];
         const BqGlobal& QG = a.g[Q.global];
@@ -209,6 +222,7 @@ __global__ void __launch_bounds__(32) k_backward_query(BqArgs a) {
                 continue;
             }
             if (++steps > a.max_steps) { status = 2; break; }
+            if (steps % kBqClockEvery == 0 && bq_now_ns() - t0 > a.max_ns) { status = 3; break; }
             const int pc = F->pc++;
             const int op = E.op[pc];
             switch (op) {
@@ -565,7 +579,13 @@ tl_status bq_run(tl_ctx* c, const tl_statement* s, int n, std::vector<double>* o
     a.done = (uint8_t*)(base + off_done);
     a.out = (double*)(base + off_o);
     a.status = (int*)(base + off_st);
-    a.max_steps = kBqMaxSteps;
+    // budgets of the launch (a test makes them tiny to see the error status)
+    const char* ms_env = getenv("TL_BQ_MAX_STEPS");
+    const char* mt_env = getenv("TL_BQ_MAX_MS");
+    const long long max_steps = ms_env ? atoll(ms_env) : 0;
+    const long long max_ms = mt_env ? atoll(mt_env) : 0;
+    a.max_steps = max_steps > 0 ? (int64_t)max_steps : kBqMaxSteps;
+    a.max_ns = (unsigned long long)(max_ms > 0 ? max_ms : kBqMaxMs) * 1000000ull;
     {
         LaunchScope L(c, "backward_query");
         k_backward_query<<<1, 32, 0, c->stream>>>(a);
@@ -577,7 +597,9 @@ tl_status bq_run(tl_ctx* c, const tl_statement* s, int n, std::vector<double>* o
     int status = 0;
     memcpy(&status, back.data() + (off_st - off_o), sizeof(int));
     if (status == 1) return fail(c, TL_ERR_TOO_LARGE, "backward query deeper than %lld frames", (long long)frames);
-    if (status == 2) return fail(c, TL_ERR_TOO_LARGE, "backward query above %lld steps", (long long)kBqMaxSteps);
+    if (status == 2) return fail(c, TL_ERR_TOO_LARGE, "backward query above %lld steps", (long long)a.max_steps);
+    if (status == 3)
+        return fail(c, TL_ERR_TOO_LARGE, "backward query ran past %.0f ms", (double)a.max_ns / 1e6);
     out->resize(queries.size());
     memcpy(out->data(), back.data(), queries.size() * sizeof(double));
     return TL_OK;

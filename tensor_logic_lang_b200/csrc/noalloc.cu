@@ -2,10 +2,16 @@
 // with its scratch in a fixed array inside the library instead of cudaMalloc.
 //
 // Who needs it: a caller whose GPU memory is owned by its own pool or arena
-// (a serving process with a fixed budget, a framework's caching allocator),
-// or one that prepares work around stream capture, where cudaMalloc would
-// synchronise the device or break the capture.  Such a caller cannot create
-// a tl_ctx (tl_init allocates), so this path takes no context at all.
+// (a serving process with a fixed budget, a framework's caching allocator
+// that must see every byte in use), which may not call cudaMalloc behind the
+// pool's back.  Such a caller cannot create a tl_ctx (tl_init allocates), so
+// this path takes no context at all.
+//
+// The call is synchronous: after every sweep it copies the changed word to
+// the host and waits for the stream, so it returns with the result final.
+// For the same reason it must not be called on a stream that is capturing.
+// `stream` must belong to the current device (checked): the scratch address
+// is the current device's.
 //
 // The scratch: one int32 "pending" word per row (the lowest 32-bit word of
 // the row that may hold a bit not yet expanded) and the sweep's control
@@ -64,12 +70,19 @@ extern "C" tl_status tl_closure_noalloc(int64_t n, const int64_t* d_rowptr, cons
     if (n == 0) return TL_OK;
     if (!d_rowptr || !d_colidx || !d_reach) return TL_ERR_INVALID;
     if (max_sweeps <= 0) max_sweeps = 1000;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (s) {
+        // the scratch address below is the current device's: a stream of
+        // another device would hand a kernel there a foreign address
+        int cur = 0, sdev = 0;
+        if (cudaGetDevice(&cur) != cudaSuccess || cudaStreamGetDevice(s, &sdev) != cudaSuccess) return TL_ERR_CUDA;
+        if (sdev != cur) return TL_ERR_INVALID;
+    }
     unsigned char* scratch = nullptr;
     if (scratch_for_current_device(&scratch) != cudaSuccess) return TL_ERR_CUDA;
     int* changed = reinterpret_cast<int*>(scratch);
     unsigned long long* counter = reinterpret_cast<unsigned long long*>(scratch + 64);
     int32_t* pending = reinterpret_cast<int32_t*>(scratch + kControlBytes);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int64_t words = (n + 31) / 32;
 
     // every row starts with all of its bits unexpanded

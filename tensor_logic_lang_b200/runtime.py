@@ -70,6 +70,10 @@ class Context:
     def sweeps(self):
         return self.lib.tl_last_sweeps(self.h)
 
+    def last_error(self):
+        """tl_last_error: the text of the last failure or note (the sweep cap)."""
+        return self.lib.tl_last_error(self.h).decode(errors="replace")
+
     @property
     def launches(self):
         return self.lib.tl_launch_count(self.h)

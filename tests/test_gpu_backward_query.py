@@ -100,3 +100,24 @@ def test_float_equations(ctx, oracle_lib, n, seed):
     assert [a for a, _ in g] == [a for a, _ in r]
     for (name, x), (_, y) in zip(g, r):
         assert abs(x - y) <= 1e-5 * abs(y) + 1e-6, (name, x, y)
+
+
+@pytest.mark.parametrize("env", [{"TL_BQ_MAX_STEPS": "50"}, {"TL_BQ_MAX_MS": "1", "TL_BQ_MAX_STEPS": "0"}],
+                         ids=["step_budget", "time_limit"])
+def test_budget_ends_the_interpreter_with_an_error(ctx, monkeypatch, env):
+    # the device interpreter stops at its step budget, or at its time limit
+    # on %globaltimer (read every 1024 steps), and the run reports
+    # TL_ERR_TOO_LARGE; the context stays usable afterwards.  The 400-node
+    # chain takes far more than 50 steps, and far more than 1 ms.
+    n = 400
+    edges = [(i, i + 1) for i in range(n - 1)]
+    src = bc.graph_program(n, edges, [(0, n - 1)] * 1 + [(k, n - 1) for k in range(0, 200, 10)], "left")
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    with pytest.raises(abi.TLError) as e:
+        ctx.run(lang.Program(src))
+    assert e.value.status == abi.TL_ERR_TOO_LARGE
+    for k in env:
+        monkeypatch.delenv(k)
+    ctx.run(lang.Program(bc.CHAIN))
+    assert ctx.output() == bc.CHAIN_OUT

@@ -1,7 +1,10 @@
 """Row-sharded closure and message passing on 2+ GPUs (one process per GPU,
-NCCL all-reduce of the changed word per sweep, NCCL all-gather of the
-per-node transform per layer), reassembled and checked against the f64
-oracle.  Skipped when the box has fewer than two GPUs."""
+changed word per sweep through peer memory or an NCCL all-reduce, NCCL
+all-gather of the per-node transform per layer), reassembled and checked
+against the f64 oracle; and the bounded waits of the sharded fixpoint when a
+rank skips a run.  Skipped when the box has fewer than two GPUs."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -88,3 +91,57 @@ def test_sharded_gnn(oracle_lib):
     r2 = oracle_lib.gnn_layer(rowptr, colidx, r1, d["W2"])
     assert_close(h1, r1, TOL_TF32, "H1")
     assert_close(h2, r2, TOL_TF32, "H2")
+
+
+def _skip_worker(rank, world, nid, mode, q, done):
+    # a rank that skips the second fixpoint: it stays alive, with none of its
+    # kernels or collectives in flight, until rank 0 has seen its wait run out
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if mode == "nccl":
+        os.environ["TL_NO_PEER_FLAGS"] = "1"
+    from tensor_logic_lang_b200 import abi as A
+    from tensor_logic_lang_b200.runtime import Context
+    ctx = Context(device=rank, rank=rank, world_size=world, nccl_id=nid, comm_timeout_ms=1000)
+    try:
+        ctx.set_sharding("Reach", A.SHARD_ROWS)
+        p, _, _, _ = configs.program(configs.closure, n=4096)
+        ctx.run(p)
+        ctx.sync()
+        first = ctx.sweeps
+        status = A.TL_OK
+        if rank == 0:
+            try:
+                ctx.run(p)
+                ctx.sync()
+            except A.TLError as e:
+                status = e.status
+            done.set()
+        else:
+            done.wait(120)
+        q.put((rank, first, status))
+    finally:
+        ctx.close()
+
+
+@pytest.mark.skipif(_world() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
+def test_skipped_rank_ends_the_wait_with_comm_error(mode):
+    # peer: the one-launch fixpoint's wait for the other rank's changed word
+    # (ld.acquire.sys on its own slot array) gives up after comm_timeout_ms of
+    # %globaltimer, every block returns, and tl_sync reports TL_ERR_COMM.
+    # nccl: the per-sweep all-reduce's host wait gives up after
+    # comm_timeout_ms, aborts the communicator and returns TL_ERR_COMM.
+    from tensor_logic_lang_b200.runtime import unique_id
+    nid = unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    done = ctx.Event()
+    procs = [ctx.Process(target=_skip_worker, args=(r, 2, nid, mode, q, done)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted([q.get(timeout=300) for _ in range(2)])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert out[0][1] == out[1][1] == 2                  # the first run converged on both ranks
+    assert out[0][2] == abi.TL_ERR_COMM and out[1][2] == abi.TL_OK

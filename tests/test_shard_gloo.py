@@ -95,3 +95,46 @@ def test_partition_helpers():
         layout[r * per: r * per + counts[r]] = shard.global_rows(n, r, world)
     for u in range(n):
         assert layout[shard.gathered_row(u, world, per)] == u
+
+
+def _parity_worker(rank, world, port, n, rows, cols, swap, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import bench
+    from oracle import oracle
+    bench.N_CLOSURE = n
+    dist = bench.Dist(world, rank, rank)
+    colptr, rowidx = gen.csr_from_coo(n, cols, rows)
+    full = _bits(n, rows, cols)
+    sweeps = oracle.closure_right(n, colptr, rowidx, full)
+    mine = np.ascontiguousarray(full[shard.global_rows(n, rank, world)])
+    if swap and rank == 1:
+        mine[[3, 4]] = mine[[4, 3]]          # two rows in the wrong places, same pair count
+    res = bench.closure_parity(dist, mine, sweeps, rows, cols)
+    if rank == 0:
+        q.put(res)
+    dist.close()
+
+
+@pytest.mark.parametrize("swap", [False, True], ids=["exact", "rows_swapped"])
+def test_bench_closure_parity_over_gloo(oracle_lib, swap):
+    # bench.py's N > 1 parity leg: per-row digests gathered from every rank
+    # and compared with the oracle's rows; a swap of two rows on one rank
+    # keeps the pair count but must read as a mismatch
+    n, world = 256, 2
+    rows, cols = gen.random_dag(n, 3, 22)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_parity_worker, args=(r, world, port, n, rows, cols, swap, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res["rows_checked"] == n
+    if swap:
+        assert res["closure"] == "MISMATCH" and res["rows_differing"] == 2
+    else:
+        assert res["closure"] == "bit-exact" and res["sweeps"] == [res["oracle_sweeps"]] * world
