@@ -183,6 +183,113 @@ tl_status comm_peer_setup(tl_ctx* c) {
     return st;
 }
 
+// ----------------------------------------------------------------------------
+// The symmetric buffer of the sharded closure: every rank allocates `bytes`,
+// zeroes it and exports it; the handles travel in one all-gather (which also
+// orders every rank's zeroing before any peer can read), and every rank maps
+// every other rank's buffer.  As with the flag slots, a second collective
+// makes every rank agree on whether all of them could.  A larger size later
+// unmaps the old buffers everywhere (a barrier between the unmapping and the
+// frees) and sets up again.
+// ----------------------------------------------------------------------------
+tl_status comm_barrier(tl_ctx* c) {
+    int* w = c->d_flags + 48;
+    TL_CK(c, cudaMemsetAsync(w, 0, sizeof(int), c->stream));
+    return comm_allreduce_max_int(c, w, 1);
+}
+
+void comm_sym_release(tl_ctx* c) {
+    for (int j = 0; j < kMaxPeers; ++j) {
+        if (c->sym_peer[j] && j != c->rank) cudaIpcCloseMemHandle(c->sym_peer[j]);
+        c->sym_peer[j] = nullptr;
+    }
+    if (c->sym_own) cudaFree(c->sym_own);
+    c->sym_own = nullptr;
+    c->sym_bytes = 0;
+    cudaGetLastError();
+}
+
+tl_status comm_sym_setup(tl_ctx* c, size_t bytes) {
+    if (c->sym_state == -1 || (c->sym_state == 1 && c->sym_bytes >= bytes)) return TL_OK;
+    if (!c->comm) return fail(c, TL_ERR_COMM, "no communicator");
+    if (c->sym_state == 1) {
+        // every rank grows at the same call: unmap the peers' buffers, wait
+        // until every rank has, then free this rank's
+        for (int j = 0; j < kMaxPeers; ++j) {
+            if (c->sym_peer[j] && j != c->rank) cudaIpcCloseMemHandle(c->sym_peer[j]);
+            c->sym_peer[j] = nullptr;
+        }
+        TL_TRY(comm_barrier(c));
+        comm_sym_release(c);
+    }
+    c->sym_state = -1;
+    const int world = c->world;
+    PeerRecord mine{};
+    mine.ok = world <= kMaxPeers && !getenv("TL_NO_PEER_ROWS");
+    if (mine.ok && cudaMalloc(&c->sym_own, bytes) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaMemsetAsync(c->sym_own, 0, bytes, c->stream) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaIpcGetMemHandle(&mine.handle, c->sym_own) != cudaSuccess) mine.ok = 0;
+    cudaGetLastError();
+    std::vector<PeerRecord> all(world);
+    PeerRecord* d = nullptr;
+    TL_CK(c, cudaMalloc(&d, sizeof(PeerRecord) * (world + 1)));
+    tl_status st = TL_OK;
+    int state = -1;
+    do {
+        if (cudaMemcpyAsync(d + world, &mine, sizeof mine, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+            st = fail(c, TL_ERR_CUDA, "peer rows set-up: copy");
+            break;
+        }
+        ncclResult_t r = ncclAllGather(d + world, d, sizeof(PeerRecord), ncclChar, (ncclComm_t)c->comm, c->stream);
+        if (r != ncclSuccess) {
+            st = nccl_fail(c, r, "ncclAllGather");
+            break;
+        }
+        if ((st = comm_wait(c)) != TL_OK) break;
+        if (cudaMemcpy(all.data(), d, sizeof(PeerRecord) * world, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            st = fail(c, TL_ERR_CUDA, "peer rows set-up: copy back");
+            break;
+        }
+        int ok = 1;
+        for (int j = 0; j < world; ++j) ok = ok && all[j].ok;
+        for (int j = 0; ok && j < world; ++j) {
+            if (j == c->rank) {
+                c->sym_peer[j] = c->sym_own;
+                continue;
+            }
+            void* p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, all[j].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+                break;
+            }
+            c->sym_peer[j] = p;
+        }
+        int* flag = reinterpret_cast<int*>(d + world);
+        const int bad = ok ? 0 : 1;
+        if (cudaMemcpyAsync(flag, &bad, sizeof bad, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+            st = fail(c, TL_ERR_CUDA, "peer rows set-up: copy");
+            break;
+        }
+        if ((st = comm_allreduce_max_int(c, flag, 1)) != TL_OK) break;
+        int any_bad = 1;
+        if (cudaMemcpy(&any_bad, flag, sizeof any_bad, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            st = fail(c, TL_ERR_CUDA, "peer rows set-up: copy back");
+            break;
+        }
+        state = any_bad ? -1 : 1;
+    } while (false);
+    cudaFree(d);
+    if (state == 1) {
+        c->sym_bytes = bytes;
+        c->sym_epoch = 0;
+    } else {
+        comm_sym_release(c);
+    }
+    c->sym_state = state;
+    return st;
+}
+
 }  // namespace tl
 
 extern "C" tl_status tl_comm_unique_id(uint8_t id_out[128]) {

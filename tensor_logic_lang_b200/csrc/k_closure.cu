@@ -97,6 +97,16 @@ struct FixArgs {
     uint32_t* dpR;
     int64_t dp_rows, dp_stride, dp_offset;
     int dp_copy;
+    // peer rows: the row space is this rank's own rows (dp_stride = world,
+    // dp_offset = rank), published for the other ranks in a buffer every
+    // rank maps (prows/pclosed[rank]) and also written to the relation; a
+    // successor y on rank y % world is read there at local row y / world
+    // (closed word with acquire at system scope, the row with plain loads
+    // over NVLink)
+    int peer_dp;
+    int64_t n_glob;                          // nodes of the relation (rows over all ranks)
+    unsigned long long* pclosed[kMaxPeers];
+    uint32_t* prows[kMaxPeers];
     int shortcut;              // lazy rows OR closed rows in (and run in descending order)
     FixState* st;
     int team;                  // warps per block
@@ -161,6 +171,31 @@ __device__ __forceinline__ int32_t local_row(int64_t rows, int64_t stride, int64
         l = ud / us;
     }
     return l < rows ? (int32_t)l : -1;
+}
+
+// Handle of node y's row in the lazy sweep's row space, or -1 when y has no
+// row there: the local row index, or with peer rows the node itself.
+template <bool PEER>
+__device__ __forceinline__ int32_t dp_handle(const FixArgs& a, int32_t y) {
+    if (PEER) return (y >= 0 && y < a.n_glob) ? y : -1;
+    return local_row(a.dp_rows, a.dp_stride, a.dp_offset, y);
+}
+
+// The closed word of row handle h, read with acquire (system scope for
+// another rank's word: its release was at system scope too).
+template <bool PEER>
+__device__ __forceinline__ unsigned long long dp_closed_load(const FixArgs& a, int32_t h) {
+    if (!PEER) return load_acquire_gpu(&a.closed[h]);
+    const uint32_t o = (uint32_t)h % (uint32_t)a.world, l = (uint32_t)h / (uint32_t)a.world;
+    return (int)o == a.rank ? load_acquire_gpu(a.pclosed[o] + l) : load_acquire_sys(a.pclosed[o] + l);
+}
+
+// The row of handle h (this rank's, or another rank's through peer memory).
+template <bool PEER>
+__device__ __forceinline__ const uint32_t* dp_row(const FixArgs& a, int32_t h) {
+    if (!PEER) return a.dpR + (int64_t)h * a.words;
+    const uint32_t o = (uint32_t)h % (uint32_t)a.world, l = (uint32_t)h / (uint32_t)a.world;
+    return a.prows[o] + (int64_t)l * a.words;
 }
 
 __device__ __forceinline__ int scan_incl(int v, int lane) {
@@ -239,6 +274,7 @@ __device__ __forceinline__ int harvest(uint32_t* spill, int64_t words, int64_t& 
 // lane, lane + 32, ... of every 1024-word chunk) of the source rows into the
 // shared row, two source rows' loads in flight at a time: no index search and
 // no shared-memory atomics.
+template <bool PEER>
 __device__ __forceinline__ void or_closed_rows(const FixArgs& a, bool has, int32_t ly, int lo, int hi,
                                                uint32_t* row, bool vec, int lane) {
     const int words = (int)a.words;
@@ -247,7 +283,7 @@ __device__ __forceinline__ void or_closed_rows(const FixArgs& a, bool has, int32
         while (m) {
             const int src = __ffs(m) - 1;
             m &= m - 1;
-            const uint32_t* srow = a.dpR + (int64_t)__shfl_sync(0xffffffffu, ly, src) * words;
+            const uint32_t* srow = dp_row<PEER>(a, __shfl_sync(0xffffffffu, ly, src));
             const int l = max(__shfl_sync(0xffffffffu, lo, src), 0);
             const int h = min(__shfl_sync(0xffffffffu, hi, src), words);
             for (int w = l + lane; w < h; w += 32) row[w] |= __ldcg(srow + w);
@@ -278,7 +314,7 @@ __device__ __forceinline__ void or_closed_rows(const FixArgs& a, bool has, int32
             uint4 v[2][8];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const uint4* srow = reinterpret_cast<const uint4*>(a.dpR + (int64_t)max(sl[j], 0) * words);
+                const uint4* srow = reinterpret_cast<const uint4*>(dp_row<PEER>(a, max(sl[j], 0)));
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int w = base + i * 128 + lane * 4;
@@ -317,7 +353,7 @@ struct RowSearch {
 // node whose local row is closed (lazy sweep) is ORed in, not expanded.
 // budget > 0: returns false once more than that many bits were expanded (the
 // row goes to a team); true when the row is closed.
-template <int ITEMS>
+template <int ITEMS, bool PEER>
 __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool own_first, bool dp, int budget,
                                            uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
@@ -354,7 +390,7 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
                     // after it: one round trip either way
                     A[k] = __ldg(&a.succ[2 * (int64_t)y]);
                     B[k] = __ldg(&a.succ[2 * (int64_t)y + 1]);
-                    if (dp) L[k] = local_row(a.dp_rows, a.dp_stride, a.dp_offset, y);
+                    if (dp) L[k] = dp_handle<PEER>(a, y);
                 }
             }
         }
@@ -363,7 +399,7 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
             // after it (for the other lanes, through the warp barrier below)
 #pragma unroll
             for (int k = 0; k < ITEMS; ++k)
-                if (L[k] >= 0) CW[k] = load_acquire_gpu(&a.closed[L[k]]);
+                if (L[k] >= 0) CW[k] = dp_closed_load<PEER>(a, L[k]);
 #pragma unroll
             for (int k = 0; k < ITEMS; ++k) {
                 if (L[k] >= 0 && (uint32_t)(CW[k] >> 42) == a.epoch) Y[k] = -1;   // closed: ORed in below
@@ -446,7 +482,7 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
             for (int k = 0; k < ITEMS; ++k) {
                 const bool has = L[k] >= 0;
                 if (__any_sync(0xffffffffu, has))
-                    or_closed_rows(a, has, L[k], (int)(CW[k] & ((1u << kClosedSpan) - 1u)),
+                    or_closed_rows<PEER>(a, has, L[k], (int)(CW[k] & ((1u << kClosedSpan) - 1u)),
                                    (int)((CW[k] >> kClosedSpan) & ((1u << kClosedSpan) - 1u)), row, vec, lane);
             }
             __syncwarp();
@@ -540,7 +576,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
             __syncwarp();
             }
 
-            if (!search_row<kFixItems>(a, S, lazy, false, budget, row, spill, q, lane)) {
+            if (!search_row<kFixItems, false>(a, S, lazy, false, budget, row, spill, q, lane)) {
                 // too much work for one warp: leave the row (unwritten, still
                 // pending) to a team of warps after this phase
                 if (lane == 0) a.heavy[atomicAdd(&a.st->n_heavy, 1)] = (int32_t)r;
@@ -576,6 +612,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
 // that successor is then expanded instead, with the same result.  A row grew
 // if it ends with more bits than succ(x) has.  Once written, the row publishes
 // its closed word (release at GPU scope) and its pending word.
+template <bool PEER>
 __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long long* next_row, int budget,
                                               uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
@@ -589,8 +626,8 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         return ((int64_t)i < a.dp_rows && lane < 8) ? __ldg(succ32 + 8 * node_of(i) + lane) : -1;
     };
     auto closed_of = [&](int32_t sl) {
-        const int32_t l = (sl >= 0 && sl < sentinel) ? local_row(a.dp_rows, a.dp_stride, a.dp_offset, sl) : -1;
-        return l >= 0 ? load_acquire_gpu(&a.closed[l]) : 0ull;
+        const int32_t l = (sl >= 0 && sl < sentinel) ? dp_handle<PEER>(a, sl) : -1;
+        return l >= 0 ? dp_closed_load<PEER>(a, l) : 0ull;
     };
     bool any = false;
     unsigned long long nb = 0;
@@ -609,7 +646,8 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
     auto publish = [&]() {
         __syncwarp();
         if (lane == 0 && pub_r >= 0) {
-            store_release_gpu(&a.closed[pub_r], pub_w);
+            if (PEER) store_release_sys(&a.closed[pub_r], pub_w);
+            else store_release_gpu(&a.closed[pub_r], pub_w);
             if (pub_p >= 0) a.pending[pub_p] = INT32_MAX;
         }
         pub_r = -1;
@@ -626,7 +664,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         const bool more = __shfl_sync(0xffffffffu, tslot, 7) == -2;
         const int32_t s0 = (lane < 8 && tslot >= 0 && tslot < sentinel) ? tslot : -1;
         const bool f = s0 >= 0 && set_new(row, s0);
-        const int32_t l0 = f ? local_row(a.dp_rows, a.dp_stride, a.dp_offset, s0) : -1;
+        const int32_t l0 = f ? dp_handle<PEER>(a, s0) : -1;
         const unsigned fresh = __ballot_sync(0xffffffffu, f);
         int n_init = __popc(fresh);
         unsigned long long nb2 = 0;
@@ -637,7 +675,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         // fewer successors are expanded
         unsigned long long cw_now = cw;
         if (__any_sync(0xffffffffu, f && l0 >= 0 && !closed) && f && l0 >= 0 && !closed) {
-            cw_now = load_acquire_gpu(&a.closed[l0]);
+            cw_now = dp_closed_load<PEER>(a, l0);
             closed = (uint32_t)(cw_now >> 42) == a.epoch;
         }
         const unsigned open = __ballot_sync(0xffffffffu, f && !closed);
@@ -661,13 +699,13 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         nb = __shfl_sync(0xffffffffu, nb2, 0);
         t_next = slot_of(nb);
         __syncwarp();
-        or_closed_rows(a, closed, l0, (int)(cw_now & ((1u << kClosedSpan) - 1u)),
+        or_closed_rows<PEER>(a, closed, l0, (int)(cw_now & ((1u << kClosedSpan) - 1u)),
                        (int)((cw_now >> kClosedSpan) & ((1u << kClosedSpan) - 1u)), row, vec, lane);
         __syncwarp();
         // its successors' closed words, in flight during the search and write-back
         cw_next = closed_of(t_next);
 
-        const bool done = search_row<1>(a, S, false, true, budget, row, spill, q, lane);
+        const bool done = search_row<1, PEER>(a, S, false, true, budget, row, spill, q, lane);
         if (!done) {
             if (lane == 0) a.heavy[atomicAdd(&a.st->n_heavy, 1)] = (int32_t)r;
             for (int64_t w = lane * 4; w < a.wpad; w += 128) {
@@ -687,6 +725,8 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
             const int64_t d = r - a.row_offset;
             lr = (d >= 0 && d % a.row_stride == 0 && d / a.row_stride < a.rows) ? d / a.row_stride : -1;
             if (lr >= 0) own = a.R + lr * words;
+        } else if (PEER) {
+            own = a.R + r * words;   // the published copy above, the relation here
         }
         int lo_w = INT32_MAX, hi_w = 0, pc = 0;
         if (vec) {
@@ -963,6 +1003,7 @@ __device__ bool grid_barrier(const FixArgs& a, unsigned gen, int s, bool settle)
     return ok_s != 0;
 }
 
+template <bool PEER>
 __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs a) {
     extern __shared__ __align__(16) uint32_t smem_fix[];
     __shared__ int s_idx;
@@ -983,7 +1024,8 @@ __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs
         __syncwarp();
         const int budget = a.team > 1 ? a.team_budget : 0;
         const bool grew = lazy && a.shortcut
-                              ? close_rows_dp(a, &a.st->next_row[s & 1], a.dp_copy ? 0 : budget, row, spill, q, lane)
+                              ? close_rows_dp<PEER>(a, &a.st->next_row[s & 1], a.dp_copy || PEER ? 0 : budget, row,
+                                              spill, q, lane)
                               : close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, lazy, budget, row, spill, q,
                                            lane);
         if (lane == 0 && grew) *(volatile int*)&a.st->changed[s & 1] = 1;
@@ -1036,13 +1078,18 @@ size_t fix_smem_per_warp(int64_t words) {
 
 }  // namespace
 
-// TL_CLOSURE_SHARDED=local makes each rank close only its own rows, with
-// shortcuts through its own closed rows; the replicated sweep is the default
-// (the local one was slower at 2 and 4 GPUs, and slower at 4 than at 2, as
-// fewer successors are local).
-static bool sharded_sweep_replicates() {
+// How a row-sharded relation runs its lazy sweep on several GPUs
+// (TL_CLOSURE_SHARDED): "peer" (default) — each rank closes its own rows and
+// takes shortcuts through every rank's closed rows, read over NVLink from a
+// buffer each rank publishes them in; "replicate" — every rank closes every
+// row in a scratch copy and keeps its own; "local" — each rank closes its
+// own rows with shortcuts through its own closed rows only.
+enum ShardedSweep { SWEEP_PEER, SWEEP_REPLICATE, SWEEP_LOCAL };
+static ShardedSweep sharded_sweep_mode() {
     const char* m = getenv("TL_CLOSURE_SHARDED");
-    return !(m && !strcmp(m, "local"));
+    if (m && !strcmp(m, "local")) return SWEEP_LOCAL;
+    if (m && !strcmp(m, "replicate")) return SWEEP_REPLICATE;
+    return SWEEP_PEER;
 }
 
 tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweeps, bool need_now, int* sweeps_out,
@@ -1115,7 +1162,17 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // closes only its own rows and takes shortcuts through its own closed
     // rows, expanding the successors other ranks hold.
     const bool sharded = R->shard == TL_SHARD_ROWS && c->world > 1;
-    const bool replicate = shortcut && sharded && sharded_sweep_replicates();
+    const ShardedSweep mode = sharded_sweep_mode();
+    const bool replicate = shortcut && sharded && mode == SWEEP_REPLICATE;
+    // peer rows: the published buffer holds, per rank, the closed words and
+    // then the rows of the largest share (every rank asks for the same size)
+    bool peer_rows = shortcut && sharded && mode == SWEEP_PEER;
+    const int64_t rows_max = (R->dims[0] + c->world - 1) / c->world;
+    const size_t sym_closed_bytes = ((size_t)rows_max * 8 + 255) & ~size_t(255);
+    if (peer_rows) {
+        TL_TRY(comm_sym_setup(c, sym_closed_bytes + (size_t)rows_max * words * 4));
+        peer_rows = c->sym_state == 1;   // the same on every rank
+    }
     const int64_t dp_rows = replicate ? R->dims[0] : rows;
     uint32_t* dpR = R->bits;
     if (replicate) {
@@ -1123,7 +1180,16 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         TL_TRY(workspace(c, (size_t)std::max<int64_t>(dp_rows, 1) * words * 4, &ws, WS_FIXPOINT));
         dpR = static_cast<uint32_t*>(ws);
     }
-    if (shortcut) {
+    if (peer_rows) {
+        // one epoch count per context, advanced on every rank at the same
+        // launch; at its wrap the closed words are cleared on every rank
+        // before any rank reads them again
+        if (++c->sym_epoch > kEpochMax) {
+            TL_CK(c, cudaMemsetAsync(c->sym_own, 0, sym_closed_bytes, c->stream));
+            TL_TRY(comm_barrier(c));
+            c->sym_epoch = 1;
+        }
+    } else if (shortcut) {
         const size_t need = std::max<size_t>((size_t)dp_rows * 8, 256);
         if (need > c->fix_closed_cap) {
             TL_CK(c, cudaStreamSynchronize(c->stream));
@@ -1150,12 +1216,16 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     const size_t per_warp = fix_smem_per_warp(words);
     const bool teams = getenv("TL_CLOSURE_TEAMS") != nullptr;
     if (c->fix_shape_words != words || c->fix_shape_teams != (int)teams) {
-        TL_CK(c, cudaFuncSetAttribute(k_closure_fix, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
+        TL_CK(c, cudaFuncSetAttribute(k_closure_fix<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
+        TL_CK(c, cudaFuncSetAttribute(k_closure_fix<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
         int wpb = 1, per_sm = 0;
         for (int w = kFixWarps; w >= 1; w >>= 1) {
             if (per_warp * w > kSmemCap) continue;
             int b = 0;
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_closure_fix, 32 * w, per_warp * w);
+            int b2 = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_closure_fix<false>, 32 * w, per_warp * w);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b2, k_closure_fix<true>, 32 * w, per_warp * w);
+            b = std::min(b, b2);   // one shape for both (every rank computes the same)
             if (b < 1) continue;
             if (teams) { wpb = w; per_sm = b; break; }
             if (b * w > per_sm * wpb) { wpb = w; per_sm = b; }
@@ -1193,6 +1263,17 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.shortcut = shortcut ? 1 : 0;
     a.closed = static_cast<unsigned long long*>(c->fix_closed);
     a.epoch = c->fix_epoch;
+    a.peer_dp = peer_rows ? 1 : 0;
+    a.n_glob = R->dims[0];
+    if (peer_rows) {
+        for (int j = 0; j < c->world; ++j) {
+            a.pclosed[j] = static_cast<unsigned long long*>(c->sym_peer[j]);
+            a.prows[j] = reinterpret_cast<uint32_t*>(static_cast<char*>(c->sym_peer[j]) + sym_closed_bytes);
+        }
+        a.closed = a.pclosed[c->rank];
+        a.epoch = c->sym_epoch;
+        dpR = a.prows[c->rank];
+    }
     a.dpR = dpR;
     a.dp_rows = dp_rows;
     a.dp_copy = replicate ? 1 : 0;
@@ -1218,7 +1299,8 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     {
         LaunchScope L(c, "closure_fixpoint", sweep_bytes);
         void* args[] = {&a};
-        TL_CK(c, cudaLaunchCooperativeKernel((const void*)k_closure_fix, dim3((unsigned)grid), dim3(32 * wpb), args,
+        const void* fn = peer_rows ? (const void*)k_closure_fix<true> : (const void*)k_closure_fix<false>;
+        TL_CK(c, cudaLaunchCooperativeKernel(fn, dim3((unsigned)grid), dim3(32 * wpb), args,
                                              per_warp * wpb, c->stream));
         TL_TRY(L.done());
     }

@@ -330,6 +330,7 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     for (auto e : c->event_pool) cudaEventDestroy(e);
     release_graphs(c);
     comm_peer_release(c);
+    comm_sym_release(c);
     if (c->comm) comm_destroy(c);
     for (int i = 0; i < 4; ++i) cudaFree(c->ws[i]);
     cudaFree(c->aux);

@@ -181,6 +181,14 @@ struct tl_ctx {
     int peer_state = 0;                              // 0 not tried, 1 ready, -1 unavailable
     unsigned long long* peer_slots[tl::kMaxPeers] = {};
     void* peer_own = nullptr;                        // this rank's slot array
+    // a buffer of one size on every rank, every rank's copy mapped into this
+    // process: the closed words and rows the sharded closure publishes for
+    // the other ranks' peer loads (comm_sym_setup)
+    int sym_state = 0;                               // 0 none, 1 ready, -1 unavailable
+    size_t sym_bytes = 0;
+    void* sym_own = nullptr;
+    void* sym_peer[tl::kMaxPeers] = {};
+    uint32_t sym_epoch = 0;                          // closed-word epoch of the sharded lazy sweep
 
     // profiling
     bool prof = false;
@@ -351,6 +359,11 @@ uint64_t next_csr_stamp();
 // multi-GPU fixpoint flags over peer memory (comm.cpp); collective over all ranks
 tl_status comm_peer_setup(tl_ctx* c);
 void comm_peer_release(tl_ctx* c);
+// the symmetric buffer (collective; every rank passes the same size): on
+// return sym_state is 1 on every rank or -1 on every rank
+tl_status comm_sym_setup(tl_ctx* c, size_t bytes);
+void comm_sym_release(tl_ctx* c);
+tl_status comm_barrier(tl_ctx* c);
 // captured program runs (lower.cpp)
 void release_graphs(tl_ctx* c);
 

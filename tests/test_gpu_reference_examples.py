@@ -51,3 +51,21 @@ def test_example_matches_oracle(ctx, case, tmp_path, monkeypatch):
         got = np.fromfile(tmp_path / path, dtype=np.float64)
         assert got.shape == (len(want),), path
         assert_close(got, want, TOL_FP32, path)
+
+
+def test_saved_files_load_back(ctx, oracle_lib, tmp_path, monkeypatch):
+    # fileio.tl saves W1; a second program loads the raw f64 file
+    # (llvm.zig:565-633 layout) into a fresh tensor and uses it
+    monkeypatch.chdir(tmp_path)
+    case = next(c for c in CASES if c["name"] == "fileio")
+    ctx.run(lang.Program(case["src"]))
+    src = ("domain i: 4\ndomain h: 3\nV[i,h] = 0\nload V \"w1.bin\"\nS[i] = V[i,h]\nT[h,i] = V[i,h]\nS?\n")
+    p = lang.Program(src)
+    ctx.run(p)
+    ref = oracle_lib.OracleRun(p)
+    want = np.asarray(case["expect_files"]["w1.bin"]).reshape(4, 3)
+    assert_close(ctx.tensor("V"), want, TOL_FP32, "V")
+    assert_close(ctx.tensor("S"), want.sum(axis=1), TOL_FP32, "S")
+    assert_close(ctx.tensor("T"), want.T, TOL_FP32, "T")
+    assert_close(ctx.tensor("S"), ref.tensor("S"), TOL_FP32, "S vs oracle")
+    assert ctx.output() == ref.queries
