@@ -35,9 +35,13 @@ N_CLOSURE = 32768
 DEG_CLOSURE = 4
 METRIC = "closure_fixpoint_iters_per_s"
 # DRAM bytes one launch of the one-launch fixpoint moves on this workload at
-# N = 1 (dram__bytes_read.sum + dram__bytes_write.sum of an ncu capture:
-# 2.3 MB read, 79.4 MB written; the rest of the rows stay in L2)
-CLOSURE_TRAFFIC_1GPU = 81.7e6
+# N = 1: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of
+# the current kernel (2.45 MB read, 78.79 MB written; the rest of the rows
+# are still in L2 when the kernel ends), measured with
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
+#       --clock-control none -k regex:k_closure_fix -s 2 -c 1
+#       python bench.py --workload closure --steps 1 --warmup 3 --cpu-sample-s 0
+CLOSURE_TRAFFIC_1GPU = 81.24e6
 UNIT = "sweeps/s"
 
 
@@ -307,7 +311,12 @@ def run_closure(args, dist, peaks):
             # the launch's phases from the device clock (rows of each sweep,
             # then its settling: grid barrier and, on several GPUs, the peer wait)
             "phases_ms": {k.split(".", 1)[1]: round(v["total_ms"] / max(1, v["launches"]), 4)
-                          for k, v in prof.items() if k.startswith("closure_fixpoint.")}}
+                          for k, v in prof.items() if k.startswith("closure_fixpoint.sweep")},
+            # per launch: closed rows the lazy sweep ORed in (this rank's:
+            # orl, other ranks': orr), nodes it expanded (exp), and the
+            # scheme it ran (1gpu, peer, repl, local or bfs: 1)
+            "lazy_sweep_counts": {k.split(".n_", 1)[1]: round(v["total_ms"] / max(1, v["launches"]), 1)
+                                  for k, v in prof.items() if k.startswith("closure_fixpoint.n_")}}
 
     # end to end: host COO -> CSR -> device, the fixpoint, full Reach bits back to the host
     e2e_total = 0.0
@@ -398,6 +407,7 @@ def run_gnn_sharded(args, dist, peaks):
             st.coo_cols = None
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=f"cuda:{dist.local}")
     ms, launches = time_steps(ctx, lambda: ctx.run(p_res), args.steps, args.warmup, dist, flush)
+    prof = profile_steps(ctx, lambda: ctx.run(p_res), args.steps, dist, flush)
     ms_max = dist.max(ms)
     per = ms_max / args.steps
     n = data["H0"].shape[0]
@@ -408,7 +418,8 @@ def run_gnn_sharded(args, dist, peaks):
     got = dist.gather((h1, h2))
     out = {"workload": "2-layer GNN n=16384 f=256, rows cyclic over the GPUs", "ms_per_step": round(per, 4),
            "tflops": round(flops / (per / 1e3) / 1e12, 3), "algo_flops": flops,
-           "gpu_launches_per_step": launches / args.steps}
+           "gpu_launches_per_step": launches / args.steps,
+           "kernels_ms_per_step_rank0": {k: round(v["total_ms"] / args.steps, 4) for k, v in prof.items()}}
     if dist.rank != 0:
         return None
     from oracle import oracle

@@ -198,37 +198,39 @@ tl_status comm_barrier(tl_ctx* c) {
     return comm_allreduce_max_int(c, w, 1);
 }
 
-void comm_sym_release(tl_ctx* c) {
+void comm_sym_release(tl_ctx* c, int slot) {
+    SymBuf& b = c->sym[slot];
     for (int j = 0; j < kMaxPeers; ++j) {
-        if (c->sym_peer[j] && j != c->rank) cudaIpcCloseMemHandle(c->sym_peer[j]);
-        c->sym_peer[j] = nullptr;
+        if (b.peer[j] && j != c->rank) cudaIpcCloseMemHandle(b.peer[j]);
+        b.peer[j] = nullptr;
     }
-    if (c->sym_own) cudaFree(c->sym_own);
-    c->sym_own = nullptr;
-    c->sym_bytes = 0;
+    if (b.own) cudaFree(b.own);
+    b.own = nullptr;
+    b.bytes = 0;
     cudaGetLastError();
 }
 
-tl_status comm_sym_setup(tl_ctx* c, size_t bytes) {
-    if (c->sym_state == -1 || (c->sym_state == 1 && c->sym_bytes >= bytes)) return TL_OK;
+tl_status comm_sym_setup(tl_ctx* c, int slot, size_t bytes) {
+    SymBuf& b = c->sym[slot];
+    if (b.state == -1 || (b.state == 1 && b.bytes >= bytes)) return TL_OK;
     if (!c->comm) return fail(c, TL_ERR_COMM, "no communicator");
-    if (c->sym_state == 1) {
+    if (b.state == 1) {
         // every rank grows at the same call: unmap the peers' buffers, wait
         // until every rank has, then free this rank's
         for (int j = 0; j < kMaxPeers; ++j) {
-            if (c->sym_peer[j] && j != c->rank) cudaIpcCloseMemHandle(c->sym_peer[j]);
-            c->sym_peer[j] = nullptr;
+            if (b.peer[j] && j != c->rank) cudaIpcCloseMemHandle(b.peer[j]);
+            b.peer[j] = nullptr;
         }
         TL_TRY(comm_barrier(c));
-        comm_sym_release(c);
+        comm_sym_release(c, slot);
     }
-    c->sym_state = -1;
+    b.state = -1;
     const int world = c->world;
     PeerRecord mine{};
     mine.ok = world <= kMaxPeers && !getenv("TL_NO_PEER_ROWS");
-    if (mine.ok && cudaMalloc(&c->sym_own, bytes) != cudaSuccess) mine.ok = 0;
-    if (mine.ok && cudaMemsetAsync(c->sym_own, 0, bytes, c->stream) != cudaSuccess) mine.ok = 0;
-    if (mine.ok && cudaIpcGetMemHandle(&mine.handle, c->sym_own) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaMalloc(&b.own, bytes) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaMemsetAsync(b.own, 0, bytes, c->stream) != cudaSuccess) mine.ok = 0;
+    if (mine.ok && cudaIpcGetMemHandle(&mine.handle, b.own) != cudaSuccess) mine.ok = 0;
     cudaGetLastError();
     std::vector<PeerRecord> all(world);
     PeerRecord* d = nullptr;
@@ -237,7 +239,7 @@ tl_status comm_sym_setup(tl_ctx* c, size_t bytes) {
     int state = -1;
     do {
         if (cudaMemcpyAsync(d + world, &mine, sizeof mine, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
-            st = fail(c, TL_ERR_CUDA, "peer rows set-up: copy");
+            st = fail(c, TL_ERR_CUDA, "peer buffer set-up: copy");
             break;
         }
         ncclResult_t r = ncclAllGather(d + world, d, sizeof(PeerRecord), ncclChar, (ncclComm_t)c->comm, c->stream);
@@ -247,14 +249,14 @@ tl_status comm_sym_setup(tl_ctx* c, size_t bytes) {
         }
         if ((st = comm_wait(c)) != TL_OK) break;
         if (cudaMemcpy(all.data(), d, sizeof(PeerRecord) * world, cudaMemcpyDeviceToHost) != cudaSuccess) {
-            st = fail(c, TL_ERR_CUDA, "peer rows set-up: copy back");
+            st = fail(c, TL_ERR_CUDA, "peer buffer set-up: copy back");
             break;
         }
         int ok = 1;
         for (int j = 0; j < world; ++j) ok = ok && all[j].ok;
         for (int j = 0; ok && j < world; ++j) {
             if (j == c->rank) {
-                c->sym_peer[j] = c->sym_own;
+                b.peer[j] = b.own;
                 continue;
             }
             void* p = nullptr;
@@ -263,30 +265,30 @@ tl_status comm_sym_setup(tl_ctx* c, size_t bytes) {
                 ok = 0;
                 break;
             }
-            c->sym_peer[j] = p;
+            b.peer[j] = p;
         }
         int* flag = reinterpret_cast<int*>(d + world);
         const int bad = ok ? 0 : 1;
         if (cudaMemcpyAsync(flag, &bad, sizeof bad, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
-            st = fail(c, TL_ERR_CUDA, "peer rows set-up: copy");
+            st = fail(c, TL_ERR_CUDA, "peer buffer set-up: copy");
             break;
         }
         if ((st = comm_allreduce_max_int(c, flag, 1)) != TL_OK) break;
         int any_bad = 1;
         if (cudaMemcpy(&any_bad, flag, sizeof any_bad, cudaMemcpyDeviceToHost) != cudaSuccess) {
-            st = fail(c, TL_ERR_CUDA, "peer rows set-up: copy back");
+            st = fail(c, TL_ERR_CUDA, "peer buffer set-up: copy back");
             break;
         }
         state = any_bad ? -1 : 1;
     } while (false);
     cudaFree(d);
     if (state == 1) {
-        c->sym_bytes = bytes;
-        c->sym_epoch = 0;
+        b.bytes = bytes;
+        if (slot == SYM_CLOSURE) c->sym_epoch = 0;
     } else {
-        comm_sym_release(c);
+        comm_sym_release(c, slot);
     }
-    c->sym_state = state;
+    b.state = state;
     return st;
 }
 

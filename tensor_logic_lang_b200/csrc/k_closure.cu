@@ -74,6 +74,9 @@ struct FixState {
     unsigned long long t_rows[2];
     unsigned long long t_team[2];
     unsigned long long t_settled[2];
+    // the lazy sweep's work, summed over warps: closed rows ORed in (this
+    // rank's, another rank's) and nodes whose successors were expanded
+    uint32_t n_or_local, n_or_remote, n_expanded;
 };
 constexpr int kFixMarks = 2;
 
@@ -345,6 +348,7 @@ struct RowSearch {
     int head, tail;   // queue positions (wrapping)
     int64_t lo;       // lowest spill-set word that may hold a bit (words: none)
     bool grew;        // a bit beyond the starting ones entered the row
+    uint32_t n_or_local = 0, n_or_remote = 0, n_expanded = 0;   // this lane's counts (lazy sweep)
 };
 
 // Expands the row's queued bits (and spill set) until both are empty.
@@ -402,9 +406,17 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
                 if (L[k] >= 0) CW[k] = dp_closed_load<PEER>(a, L[k]);
 #pragma unroll
             for (int k = 0; k < ITEMS; ++k) {
-                if (L[k] >= 0 && (uint32_t)(CW[k] >> 42) == a.epoch) Y[k] = -1;   // closed: ORed in below
-                else L[k] = -1;
+                if (L[k] >= 0 && (uint32_t)(CW[k] >> 42) == a.epoch) {
+                    if (PEER && (uint32_t)L[k] % (uint32_t)a.world != (uint32_t)a.rank) S.n_or_remote++;
+                    else S.n_or_local++;
+                    Y[k] = -1;   // closed: ORed in below
+                } else {
+                    L[k] = -1;
+                }
             }
+#pragma unroll
+            for (int k = 0; k < ITEMS; ++k)
+                if (Y[k] >= 0) S.n_expanded++;
         }
         __syncwarp();   // the taken slots may be refilled from here on
         S.head += take;
@@ -630,6 +642,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         return l >= 0 ? dp_closed_load<PEER>(a, l) : 0ull;
     };
     bool any = false;
+    uint32_t c_orl = 0, c_orr = 0, c_exp = 0;   // this lane's work counts
     unsigned long long nb = 0;
     if (lane == 0) nb = atomicAdd(next_row, 1ull);
     nb = __shfl_sync(0xffffffffu, nb, 0);
@@ -705,7 +718,14 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         // its successors' closed words, in flight during the search and write-back
         cw_next = closed_of(t_next);
 
+        if (closed) {
+            if (PEER && (uint32_t)l0 % (uint32_t)a.world != (uint32_t)a.rank) c_orr++;
+            else c_orl++;
+        }
         const bool done = search_row<1, PEER>(a, S, false, true, budget, row, spill, q, lane);
+        c_orl += S.n_or_local;
+        c_orr += S.n_or_remote;
+        c_exp += S.n_expanded;
         if (!done) {
             if (lane == 0) a.heavy[atomicAdd(&a.st->n_heavy, 1)] = (int32_t)r;
             for (int64_t w = lane * 4; w < a.wpad; w += 128) {
@@ -763,6 +783,14 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         pub_p = lr;
         pub_w = lo_w < hi_w ? closed_word(a.epoch, lo_w, hi_w) : closed_word(a.epoch, 0, 0);
         publish();
+    }
+    c_orl = __reduce_add_sync(0xffffffffu, c_orl);
+    c_orr = __reduce_add_sync(0xffffffffu, c_orr);
+    c_exp = __reduce_add_sync(0xffffffffu, c_exp);
+    if (lane == 0) {
+        atomicAdd(&a.st->n_or_local, c_orl);
+        atomicAdd(&a.st->n_or_remote, c_orr);
+        atomicAdd(&a.st->n_expanded, c_exp);
     }
     return any;
 }
@@ -1083,12 +1111,14 @@ size_t fix_smem_per_warp(int64_t words) {
 // takes shortcuts through every rank's closed rows, read over NVLink from a
 // buffer each rank publishes them in; "replicate" — every rank closes every
 // row in a scratch copy and keeps its own; "local" — each rank closes its
-// own rows with shortcuts through its own closed rows only.
-enum ShardedSweep { SWEEP_PEER, SWEEP_REPLICATE, SWEEP_LOCAL };
+// own rows with shortcuts through its own closed rows only; "bfs" — each
+// rank closes its own rows by a full breadth-first search, no shortcuts.
+enum ShardedSweep { SWEEP_PEER, SWEEP_REPLICATE, SWEEP_LOCAL, SWEEP_BFS };
 static ShardedSweep sharded_sweep_mode() {
     const char* m = getenv("TL_CLOSURE_SHARDED");
     if (m && !strcmp(m, "local")) return SWEEP_LOCAL;
     if (m && !strcmp(m, "replicate")) return SWEEP_REPLICATE;
+    if (m && !strcmp(m, "bfs")) return SWEEP_BFS;
     return SWEEP_PEER;
 }
 
@@ -1154,15 +1184,15 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // rows that step(E) left unwritten start from E's successor lists; their
     // sweep ORs in closed rows (closed words of this launch's epoch)
     const bool lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp;
-    const bool shortcut = lazy && words < (int64_t(1) << kClosedSpan);
+    const bool sharded = R->shard == TL_SHARD_ROWS && c->world > 1;
+    const ShardedSweep mode = sharded_sweep_mode();
+    const bool shortcut = lazy && words < (int64_t(1) << kClosedSpan) && !(sharded && mode == SWEEP_BFS);
     // row-sharded on several GPUs, the lazy sweep runs one of two ways; only
     // the changed word crosses GPUs in either.  Replicated: every rank closes
     // every row of the relation in a scratch copy (a row's shortcuts read
     // rows of every rank's share) and keeps its own rows.  Local: each rank
     // closes only its own rows and takes shortcuts through its own closed
     // rows, expanding the successors other ranks hold.
-    const bool sharded = R->shard == TL_SHARD_ROWS && c->world > 1;
-    const ShardedSweep mode = sharded_sweep_mode();
     const bool replicate = shortcut && sharded && mode == SWEEP_REPLICATE;
     // peer rows: the published buffer holds, per rank, the closed words and
     // then the rows of the largest share (every rank asks for the same size)
@@ -1170,8 +1200,8 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     const int64_t rows_max = (R->dims[0] + c->world - 1) / c->world;
     const size_t sym_closed_bytes = ((size_t)rows_max * 8 + 255) & ~size_t(255);
     if (peer_rows) {
-        TL_TRY(comm_sym_setup(c, sym_closed_bytes + (size_t)rows_max * words * 4));
-        peer_rows = c->sym_state == 1;   // the same on every rank
+        TL_TRY(comm_sym_setup(c, SYM_CLOSURE, sym_closed_bytes + (size_t)rows_max * words * 4));
+        peer_rows = c->sym[SYM_CLOSURE].state == 1;   // the same on every rank
     }
     const int64_t dp_rows = replicate ? R->dims[0] : rows;
     uint32_t* dpR = R->bits;
@@ -1185,7 +1215,7 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         // launch; at its wrap the closed words are cleared on every rank
         // before any rank reads them again
         if (++c->sym_epoch > kEpochMax) {
-            TL_CK(c, cudaMemsetAsync(c->sym_own, 0, sym_closed_bytes, c->stream));
+            TL_CK(c, cudaMemsetAsync(c->sym[SYM_CLOSURE].own, 0, sym_closed_bytes, c->stream));
             TL_TRY(comm_barrier(c));
             c->sym_epoch = 1;
         }
@@ -1264,11 +1294,12 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.closed = static_cast<unsigned long long*>(c->fix_closed);
     a.epoch = c->fix_epoch;
     a.peer_dp = peer_rows ? 1 : 0;
+    c->fix_mode = !sharded ? 0 : peer_rows ? 1 : replicate ? 2 : shortcut ? 3 : 4;
     a.n_glob = R->dims[0];
     if (peer_rows) {
         for (int j = 0; j < c->world; ++j) {
-            a.pclosed[j] = static_cast<unsigned long long*>(c->sym_peer[j]);
-            a.prows[j] = reinterpret_cast<uint32_t*>(static_cast<char*>(c->sym_peer[j]) + sym_closed_bytes);
+            a.pclosed[j] = static_cast<unsigned long long*>(c->sym[SYM_CLOSURE].peer[j]);
+            a.prows[j] = reinterpret_cast<uint32_t*>(static_cast<char*>(c->sym[SYM_CLOSURE].peer[j]) + sym_closed_bytes);
         }
         a.closed = a.pclosed[c->rank];
         a.epoch = c->sym_epoch;
@@ -1356,6 +1387,19 @@ tl_status fix_resolve(tl_ctx* c) {
             add("settle", s, h.t_team[s], h.t_settled[s]);
             prev = h.t_settled[s];
         }
+    }
+    if (c->fix_prof) {
+        // the lazy sweep's work and the way its shortcuts were read
+        auto count = [&](const char* what, double v) {
+            KStat& k = c->stats[std::string("closure_fixpoint.n_") + what];
+            k.launches++;
+            k.total_ms += v;   // a count, summed over launches
+        };
+        count("orl", h.n_or_local);    // closed rows of this rank ORed in
+        count("orr", h.n_or_remote);   // closed rows of other ranks ORed in
+        count("exp", h.n_expanded);    // nodes expanded
+        count(c->fix_mode == 1 ? "peer" : c->fix_mode == 2 ? "repl" : c->fix_mode == 3 ? "local" :
+              c->fix_mode == 4 ? "bfs" : "1gpu", 1);   // the scheme
     }
     c->last_sweeps = h.sweeps;
     c->fix_last_changed = h.last_changed != 0;

@@ -366,6 +366,9 @@ struct TcEpi {
     float mag;
     int beta, epi_relu;
     int* err;
+    float* fan[kMaxPeers];                  // peer copies of C (GemmPlan::fan)
+    unsigned long long* fan_cnt[kMaxPeers];
+    int fan_n;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -636,6 +639,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (epi.epi_relu) tma_store_2d(&tmD, sd, x, y);
                     bulk_commit();
                 }
+                if (epi.fan_n) {
+                    // the same 32 x 32 chunk into every peer's copy: the warp
+                    // reads the staged tile back four rows at a time, so each
+                    // store instruction writes four 128-byte row pieces
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = i * 4 + (lane >> 3), c4 = lane & 7;
+                        const int64_t grow = (int64_t)m0 + q * 32 + r;
+                        if (grow >= epi.M) continue;
+                        const float4 v = *reinterpret_cast<const float4*>(sc + r * 128 + ((c4 ^ (r & 7)) << 4));
+                        const int64_t off = grow * epi.scm + (int64_t)n0 + ch * 32 + c4 * 4;
+#pragma unroll
+                        for (int j = 0; j < kMaxPeers; ++j)
+                            if (epi.fan[j]) *reinterpret_cast<float4*>(epi.fan[j] + off) = v;
+                    }
+                }
             }
             if (lane == 0) bulk_wait_all();
             __syncwarp();
@@ -693,6 +712,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::TMEM_COLS));
+    }
+    if (epi.fan_n && threadIdx.x == 0) {
+        // every warp's peer stores of this tile happen before the barrier
+        // above; the fence and the release make them visible to a rank that
+        // reads its counter with acquire at system scope
+        __threadfence_system();
+#pragma unroll 1
+        for (int j = 0; j < kMaxPeers; ++j)
+            if (epi.fan_cnt[j])
+                asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(epi.fan_cnt[j]), "l"(1ull) : "memory");
     }
 }
 
@@ -1188,6 +1217,24 @@ bool env_flag(const char* name) {
 
 }  // namespace
 
+// Map for row gathers of a row-major fp32 matrix (`rows` rows of `cols`
+// floats, rows `row_stride` floats apart): a box of one row of `cols`
+// floats, no swizzle, for cp.async.bulk.tensor ... tile::gather4 (four rows
+// of given indices per copy).
+bool make_gather_map(CUtensorMap* map, const float* base, int64_t cols, int64_t rows, int64_t row_stride) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc || cols > 256 || (cols * 4) % 16 || (row_stride * 4) % 16 || ((uintptr_t)base & 15)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(row_stride * 4)};
+    cuuint32_t box[2] = {(cuuint32_t)cols, 1};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int64_t gemm_fan_tiles(int64_t M, int64_t N) { return ((M + TC_BM - 1) / TC_BM) * ((N + 63) / 64); }
+
 bool tcgen05_available(tl_ctx* c) {
     int major = 0, minor = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, c->device);
@@ -1345,6 +1392,9 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     const double macs = (double)p.M * p.N * p.K;
     bool tc = c->opts.precision == TL_PREC_TF32 && tcgen05_available(c) && p.M >= 128 && p.N >= 64 && p.K >= 32 &&
               macs >= (double)(1 << 25);
+    if (p.fan_n && (!tc || p.beta || p.epi_relu || p.N % 64))
+        return fail(c, TL_ERR_UNSUPPORTED, "fanned-out GEMM needs the tensor-core path (M %lld, N %lld)",
+                    (long long)p.M, (long long)p.N);
     if (!tc) return launch_simt(c, p);
 
     // Every tensor-core operand is copied once into the workspace, rounded to
@@ -1408,7 +1458,9 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     }
     // the maps span Ke; TMA reads zeros past it (the K tail of the last block)
     CUtensorMap ma, mb;
-    const int BN = p.N >= 256 && (p.N % 256 == 0 || p.N >= 1024) ? 256 : (p.N >= 128 ? 128 : 64);
+    // a fanned-out GEMM takes 64-wide tiles: more CTAs for the few rows of a
+    // shard, and a tile count every rank can compute (gemm_fan_tiles)
+    const int BN = p.fan_n ? 64 : p.N >= 256 && (p.N % 256 == 0 || p.N >= 1024) ? 256 : (p.N >= 128 ? 128 : 64);
     bool ok = pa.mn ? make_map(&ma, pa.dst, p.M, Ke, pa.ld, 32, true) : make_map(&ma, pa.dst, Ke, p.M, pa.ld, TC_BM, false);
     ok = ok && (pb.mn ? make_map(&mb, pb.dst, p.N, Ke, pb.ld, 32, true) : make_map(&mb, pb.dst, Ke, p.N, pb.ld, BN, false));
     if (!ok) return launch_simt(c, p);
@@ -1418,7 +1470,7 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     // idle SMs of a grid that is already half a wave or more
     const int64_t tiles = ((p.N + BN - 1) / BN) * ((p.M + TC_BM - 1) / TC_BM);
     int splits = 1;
-    if (!p.epi_relu && tiles * 2 <= c->sm_count && num_kb >= 8) {
+    if (!p.epi_relu && !p.fan_n && tiles * 2 <= c->sm_count && num_kb >= 8) {
         splits = (int)std::min<int64_t>((c->sm_count + tiles - 1) / tiles, num_kb / 4);
         if (splits < 1) splits = 1;
     }
@@ -1443,6 +1495,11 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     e.beta = p.beta; e.epi_relu = p.epi_relu;
     e.err = c->d_flags + 8;
     c->flags_armed = true;
+    for (int j = 0; j < kMaxPeers; ++j) {
+        e.fan[j] = p.fan_n ? p.fan[j] : nullptr;
+        e.fan_cnt[j] = p.fan_n ? p.fan_cnt[j] : nullptr;
+    }
+    e.fan_n = p.fan_n;
     // epilogue through the TMA when C (and the fused relu output D) are row-major
     // with 16-byte aligned rows; a fused relu needs the plain store (it reads
     // the final sum, which an accumulating reduce does not return)
@@ -1455,6 +1512,7 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     int ts = !env_flag("TL_GEMM_NO_TMA_STORE") && tma_ok(p.C, p.scm, p.scn) &&
              (!p.epi_relu || (tma_ok(p.D, p.sdm, p.sdn) && !p.beta && splits == 1));
     if (ts) ts = make_store_map(&mc, p.C, p.N, p.M, p.scm) && (!p.epi_relu || make_store_map(&md, p.D, p.N, p.M, p.sdm));
+    if (p.fan_n && !ts) return fail(c, TL_ERR_UNSUPPORTED, "fanned-out GEMM needs the TMA-store epilogue");
     LaunchScope L(c, "gemm_tcgen05_tf32", (double)(p.M * p.K + p.K * p.N + p.M * p.N * (1 + p.beta)) * 4.0,
                   2.0 * p.M * p.N * p.K);
     if (BN == 256) TL_TRY(launch_tc_bn<256>(c, pa.mn, pb.mn, ma, mb, mc, md, ts, e, p.M, p.N, num_kb, kb_per_split, splits));

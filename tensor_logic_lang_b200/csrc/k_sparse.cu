@@ -20,6 +20,9 @@
 // records whether any row gained a bit.
 #include <vector>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "tl_internal.h"
 
 namespace tl {
@@ -316,10 +319,52 @@ __global__ void __launch_bounds__(256) k_closure_left(const uint32_t* __restrict
 
 // out[v, :] (+)= sum_e vals[e] * P[col(e), :], one warp per row, 128-bit
 // loads of the gathered P rows (4 columns per lane and column half).
+// A block waits until every other rank's fanned-out tiles of P have landed
+// (their counters in this rank's array reach w.need), then the block's
+// reads (plain or by the TMA) may start.  False if the wait ran out: the
+// error word is set to 2 and the block does nothing.
+__device__ __forceinline__ bool spmm_wait_peers(const SpWait& w, int* err) {
+    __shared__ int ok_s;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        if (w.cnt) {
+            unsigned long long t0;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+            for (int j = 0; j < kMaxPeers && ok; ++j) {
+                if (!w.need[j]) continue;
+                for (;;) {
+                    unsigned long long v;
+                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w.cnt + j) : "memory");
+                    if (v >= w.need[j]) break;
+                    unsigned long long now;
+                    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+                    if (now - t0 > w.timeout_ns) {
+                        atomicExch(err, 2);
+                        ok = 0;
+                        break;
+                    }
+                    __nanosleep(128);
+                }
+            }
+            // the rows other ranks wrote are read next, also by the TMA
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0;
+}
+
+template <int U>
 __global__ void __launch_bounds__(256) k_spmm(int64_t rows, const int64_t* __restrict__ rowptr,
                                               const int32_t* __restrict__ colidx, const float* __restrict__ vals,
                                               const float* __restrict__ P, int64_t ldp, int64_t f, float* out,
-                                              int64_t ldo, int beta, int col_world, int64_t col_local) {
+                                              int64_t ldo, int beta, int col_world, int64_t col_local,
+                                              const __grid_constant__ SpWait wait, int* err) {
+    // rows other ranks wrote while this kernel may already run are read
+    // through L2 (ld.cg), not the read-only path
+    if (!spmm_wait_peers(wait, err)) return;
+    const bool peer = wait.cnt != nullptr;
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const bool vec = (f % 4) == 0 && (ldp % 4) == 0 && (ldo % 4) == 0 && (((uintptr_t)P | (uintptr_t)out) & 15) == 0;
@@ -344,20 +389,22 @@ __global__ void __launch_bounds__(256) k_spmm(int64_t rows, const int64_t* __res
                         u_l = (long long)u;
                         w_l = vals[eb + lane];
                     }
-                    for (int k = 0; k < ne; k += 4) {
-                        float4 p0[4], p1[4];
-                        float w[4];
+                    for (int k = 0; k < ne; k += U) {
+                        float4 p0[U], p1[U];
+                        float w[U];
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) {
+                        for (int t = 0; t < U; ++t) {
                             const long long u = __shfl_sync(0xffffffffu, u_l, (k + t) & 31);
                             w[t] = __shfl_sync(0xffffffffu, w_l, (k + t) & 31);
                             const bool ok = k + t < ne;
                             const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-                            p0[t] = ok && h0 ? __ldg(reinterpret_cast<const float4*>(P + u * ldp + j0)) : z;
-                            p1[t] = ok && h1 ? __ldg(reinterpret_cast<const float4*>(P + u * ldp + j1)) : z;
+                            const float4* q0 = reinterpret_cast<const float4*>(P + u * ldp + j0);
+                            const float4* q1 = reinterpret_cast<const float4*>(P + u * ldp + j1);
+                            p0[t] = ok && h0 ? (peer ? __ldcg(q0) : __ldg(q0)) : z;
+                            p1[t] = ok && h1 ? (peer ? __ldcg(q1) : __ldg(q1)) : z;
                         }
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) {
+                        for (int t = 0; t < U; ++t) {
                             if (k + t >= ne) break;
                             a0.x = fmaf(w[t], p0[t].x, a0.x); a0.y = fmaf(w[t], p0[t].y, a0.y);
                             a0.z = fmaf(w[t], p0[t].z, a0.z); a0.w = fmaf(w[t], p0[t].w, a0.w);
@@ -437,6 +484,160 @@ unsigned grid_for(tl_ctx* c, int64_t items, int per_block) {
     const int64_t cap = (int64_t)c->sm_count * 16;
     if (b > cap) b = cap;
     return (unsigned)(b < 1 ? 1 : b);
+}
+
+// ---------------------------------------------------------------------------
+// SpMM with the row gathers done by the TMA (f = 128 or 256).  The kernel
+// above is bound by the latency of its register-held gathers (each nonzero
+// reads a 1 KB row of P from L2; 24 warps per SM at 80 registers).  Here
+// every warp keeps a ring of slots of four P rows in shared memory: lane 0
+// fills them with cp.async.bulk.tensor tile::gather4 copies (four nonzeros
+// of one row per copy, completion counted on the slot's mbarrier) while the
+// lanes sum the slots already landed, so no registers hold gathers in
+// flight and a block of 48 registers per thread leaves room for 32 warps
+// per SM.  Rows are taken cyclically (warp w: rows w, w +
+// warps, ...) as one stream of four-nonzero batches; each element sums its
+// terms in nonzero order with the same fmaf sequence as k_spmm, so the two
+// kernels give identical results.
+constexpr int kSpMaxSlots = 16;   // ring slots per warp (runtime count up to this)
+constexpr int kSpMaxWarps = 8;    // warps per block (runtime count up to this)
+
+__device__ __forceinline__ uint32_t sp_smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool sp_wait(uint64_t* bar, uint32_t parity, int* err) {
+    const uint32_t addr = sp_smem_u32(bar);
+    unsigned long long t0 = 0;
+    for (unsigned it = 0;; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((it & 1023u) == 0) {
+            unsigned long long now;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > 2000000000ull) break;
+        }
+    }
+    if (err) atomicExch(err, 1);
+    return false;
+}
+
+template <int F>
+__global__ void __launch_bounds__(32 * kSpMaxWarps) k_spmm_tma(const __grid_constant__ CUtensorMap tmP, int64_t rows,
+                                                           const int64_t* __restrict__ rowptr,
+                                                           const int32_t* __restrict__ colidx,
+                                                           const float* __restrict__ vals, float* out, int64_t ldo,
+                                                           int beta, int col_world, int64_t col_local, int* err,
+                                                           int nslots, const __grid_constant__ SpWait wait) {
+    if (!spmm_wait_peers(wait, err)) return;
+    static_assert(F == 128 || F == 256, "row width");
+    const int kSpWarps = blockDim.x >> 5;
+    const int kSpSlots = nslots;
+    constexpr int SLOT = 4 * F;   // floats
+    extern __shared__ __align__(128) uint8_t sp_smem_raw[];
+    // the TMA writes 128-byte aligned slots (the launch adds 128 bytes of slack)
+    uint8_t* sp_smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sp_smem_raw) + 127) & ~uintptr_t(127));
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    float* ring = reinterpret_cast<float*>(sp_smem) + (size_t)wib * kSpSlots * SLOT;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sp_smem + (size_t)kSpWarps * kSpSlots * SLOT * 4) + wib * kSpSlots;
+    if (lane == 0) {
+        for (int k = 0; k < kSpSlots; ++k)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sp_smem_u32(&bars[k])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmP)) : "memory");
+        if (wait.cnt) asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+    __syncwarp();
+    const int64_t warps = (int64_t)gridDim.x * kSpWarps;
+    const int64_t first = (int64_t)blockIdx.x * kSpWarps + wib;
+    // producer (issues) and consumer (sums) positions in the batch stream;
+    // every lane keeps both, so control flow stays uniform
+    int64_t pv = first, pe = 0, pend = 0;
+    if (pv < rows) { pe = rowptr[pv]; pend = rowptr[pv + 1]; }
+    int64_t cv = first, ce = pe, cend = pend;
+    uint32_t issued = 0, consumed = 0;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    auto remap = [&](int64_t u) { return col_world > 1 ? (u % col_world) * col_local + u / col_world : u; };
+    while (cv < rows) {
+        // fill free slots with the next batches
+        while (issued - consumed < (uint32_t)kSpSlots && pv < rows) {
+            if (pe >= pend) {
+                pv += warps;
+                if (pv < rows) { pe = rowptr[pv]; pend = rowptr[pv + 1]; }
+                continue;
+            }
+            const int cnt = (int)(pend - pe < 4 ? pend - pe : 4);
+            if (lane == 0) {
+                int32_t u[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) u[t] = (int32_t)remap(colidx[pe + (t < cnt ? t : 0)]);
+                const int slot = (int)(issued % kSpSlots);
+                uint64_t* bar = &bars[slot];
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sp_smem_u32(bar)),
+                             "r"(SLOT * 4)
+                             : "memory");
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+                    "[%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(sp_smem_u32(ring + (size_t)slot * SLOT)),
+                    "l"(reinterpret_cast<uint64_t>(&tmP)), "r"(sp_smem_u32(bar)), "r"(0), "r"(u[0]), "r"(u[1]),
+                    "r"(u[2]), "r"(u[3])
+                    : "memory");
+            }
+            pe += cnt;
+            ++issued;
+        }
+        if (ce >= cend) {
+            // the row is summed: store it, then the next row of this warp
+            float* op = out + cv * ldo;
+            float4* o0 = reinterpret_cast<float4*>(op + lane * 4);
+            if (beta) { const float4 o = *o0; a0.x += o.x; a0.y += o.y; a0.z += o.z; a0.w += o.w; }
+            *o0 = a0;
+            if (F == 256) {
+                float4* o1 = reinterpret_cast<float4*>(op + 128 + lane * 4);
+                if (beta) { const float4 o = *o1; a1.x += o.x; a1.y += o.y; a1.z += o.z; a1.w += o.w; }
+                *o1 = a1;
+            }
+            a0 = make_float4(0.f, 0.f, 0.f, 0.f);
+            a1 = a0;
+            cv += warps;
+            if (cv < rows) { ce = rowptr[cv]; cend = rowptr[cv + 1]; }
+            continue;
+        }
+        const int cnt = (int)(cend - ce < 4 ? cend - ce : 4);
+        const int slot = (int)(consumed % kSpSlots);
+        if (!sp_wait(&bars[slot], (consumed / kSpSlots) & 1u, err)) return;
+        const float* rp = ring + (size_t)slot * SLOT;
+        float w[4];
+        float4 p0[4], p1[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            w[t] = t < cnt ? __ldg(vals + ce + t) : 0.f;
+            p0[t] = *reinterpret_cast<const float4*>(rp + t * F + lane * 4);
+            p1[t] = F == 256 ? *reinterpret_cast<const float4*>(rp + t * F + 128 + lane * 4) : p0[t];
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            if (t >= cnt) break;
+            a0.x = fmaf(w[t], p0[t].x, a0.x); a0.y = fmaf(w[t], p0[t].y, a0.y);
+            a0.z = fmaf(w[t], p0[t].z, a0.z); a0.w = fmaf(w[t], p0[t].w, a0.w);
+            if (F == 256) {
+                a1.x = fmaf(w[t], p1[t].x, a1.x); a1.y = fmaf(w[t], p1[t].y, a1.y);
+                a1.z = fmaf(w[t], p1[t].z, a1.z); a1.w = fmaf(w[t], p1[t].w, a1.w);
+            }
+        }
+        __syncwarp();   // every lane has read the slot: it may be refilled
+        ce += cnt;
+        ++consumed;
+    }
 }
 
 }  // namespace
@@ -608,13 +809,57 @@ tl_status launch_closure_left(tl_ctx* c, Tensor* R, Tensor* E, int* d_changed) {
 }
 
 tl_status launch_spmm(tl_ctx* c, int64_t rows, const int64_t* rowptr, const int32_t* colidx, const float* vals,
-                      const float* P, int64_t ldp, int64_t f, float* out, int64_t ldo, int beta, int relu_out,
-                      int col_world, int64_t col_local) {
+                      const float* P, int64_t p_rows, int64_t ldp, int64_t f, float* out, int64_t ldo, int beta,
+                      int relu_out, int col_world, int64_t col_local, const SpWait* wait) {
     (void)relu_out;
     if (rows <= 0) return TL_OK;
+    SpWait w{};
+    if (wait) {
+        w = *wait;
+        c->flags_armed = true;   // a wait that runs out sets the error word
+    }
+    const char* regs = getenv("TL_SPMM_REGS");
+    CUtensorMap map;
+    if ((f == 128 || f == 256) && ldo % 4 == 0 && ((uintptr_t)out & 15) == 0 && p_rows > 0 &&
+        p_rows < INT32_MAX && !(regs && (regs[0] == '1' || regs[0] == '8')) &&
+        make_gather_map(&map, P, f, p_rows, ldp)) {
+        // gathers by the TMA: a persistent grid, three blocks of four warps per SM
+        // ring slots per warp, warps per block and blocks per SM (TL_SPMM_SHAPE
+        // = "slots,warps,blocks" overrides, for measurements)
+        // (measured on the 2-layer GNN, n = 16384, f = 256: one slot per warp,
+        // eight warps per block, four blocks per SM was the fastest of the
+        // shapes tried, 0.062 ms per step against 0.075 ms for the register
+        // gathers; more slots per warp with fewer warps were slower)
+        int kSpSlots = 1, kSpWarps = 8, bps = 4;
+        if (const char* sh = getenv("TL_SPMM_SHAPE")) sscanf(sh, "%d,%d,%d", &kSpSlots, &kSpWarps, &bps);
+        kSpSlots = std::max(1, std::min(kSpSlots, kSpMaxSlots));
+        kSpWarps = std::max(1, std::min(kSpWarps, kSpMaxWarps));
+        bps = std::max(1, bps);
+        const size_t smem = (size_t)kSpWarps * kSpSlots * 4 * f * 4 + (size_t)kSpWarps * kSpSlots * 8 + 128;
+        if (smem > 227 * 1024) return fail(c, TL_ERR_INVALID, "spmm ring of %zu bytes", smem);
+        const int64_t grid = std::min<int64_t>((rows + kSpWarps - 1) / kSpWarps, (int64_t)c->sm_count * bps);
+        LaunchScope L(c, "spmm_csr", 0, 0);
+        c->flags_armed = true;
+        if (f == 256) {
+            TL_CK(c, cudaFuncSetAttribute(k_spmm_tma<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            k_spmm_tma<256><<<(unsigned)grid, 32 * kSpWarps, smem, c->stream>>>(map, rows, rowptr, colidx, vals, out,
+                                                                             ldo, beta, col_world, col_local,
+                                                                             c->d_flags + 8, kSpSlots, w);
+        } else {
+            TL_CK(c, cudaFuncSetAttribute(k_spmm_tma<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            k_spmm_tma<128><<<(unsigned)grid, 32 * kSpWarps, smem, c->stream>>>(map, rows, rowptr, colidx, vals, out,
+                                                                             ldo, beta, col_world, col_local,
+                                                                             c->d_flags + 8, kSpSlots, w);
+        }
+        return L.done();
+    }
     LaunchScope L(c, "spmm_csr", 0, 0);
-    k_spmm<<<grid_for(c, rows, 8), 256, 0, c->stream>>>(rows, rowptr, colidx, vals, P, ldp, f, out, ldo, beta, col_world,
-                                                       col_local);
+    if (regs && regs[0] == '8')   // eight nonzeros' gathers in flight per step
+        k_spmm<8><<<grid_for(c, rows, 8), 256, 0, c->stream>>>(rows, rowptr, colidx, vals, P, ldp, f, out, ldo, beta,
+                                                              col_world, col_local, w, c->d_flags + 8);
+    else
+        k_spmm<4><<<grid_for(c, rows, 8), 256, 0, c->stream>>>(rows, rowptr, colidx, vals, P, ldp, f, out, ldo, beta,
+                                                              col_world, col_local, w, c->d_flags + 8);
     return L.done();
 }
 

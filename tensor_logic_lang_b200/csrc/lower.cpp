@@ -452,6 +452,76 @@ Tensor* relu_successor(tl_ctx* c, const tl_equation* eq, const tl_equation* next
 }
 
 // ----------------------------------------------------------------------------
+// Row-sharded message passing with the all-gather fused into the GEMM: each
+// rank's P = [relu-per-term] X W for its rows is stored by the GEMM's
+// epilogue into its block of the gathered P on every rank (peer stores over
+// NVLink into a buffer every rank maps), each CTA counting its tile into
+// every rank's counters; the SpMM of the rank's own output rows waits for
+// every other rank's tile count and then reads the gathered P locally.
+// Gathered P alternates between two buffers by layer: a rank writes layer
+// k's buffer only after its layer k - 1 SpMM saw every rank's layer k - 1
+// tiles, so every rank has finished the SpMM of layer k - 2 (the last
+// reader of that buffer).  The decision depends only on quantities every
+// rank shares (sizes, the collective peer set-up), so all ranks take the
+// same path; otherwise the NCCL all-gather below runs.
+// ----------------------------------------------------------------------------
+constexpr int kGnnCounter = 64;   // word of the peer slot array where rank r's tile count is kept (+ r)
+
+static tl_status sparse_chain_fanned(tl_ctx* c, Tensor* S, Tensor* lhs, const float* xp, const float* wp, int64_t nu,
+                                     int64_t x_rows, int64_t g, int64_t f, bool relu, bool* handled) {
+    *handled = false;
+    const int world = c->world;
+    const int64_t per = (nu + world - 1) / world;
+    const int64_t min_rows = nu / world;            // the smallest share
+    const char* env = getenv("TL_GNN_NCCL");
+    if ((env && env[0] == '1') || world > kMaxPeers || f % 64 || f > 4096 || min_rows < 128 || g < 32 ||
+        (double)min_rows * f * g < (double)(1 << 25) || c->opts.precision != TL_PREC_TF32 || !tcgen05_available(c) ||
+        lhs->zero == false)
+        return TL_OK;
+    TL_TRY(comm_peer_setup(c));
+    if (c->peer_state != 1) return TL_OK;
+    const size_t half = (size_t)per * world * f * 4;
+    TL_TRY(comm_sym_setup(c, SYM_GNN, 2 * half));
+    if (c->sym[SYM_GNN].state != 1) return TL_OK;
+    const int par = (int)(c->gnn_layers & 1);
+    c->gnn_layers++;
+    auto gathered = [&](int q) {
+        return reinterpret_cast<float*>(static_cast<char*>(c->sym[SYM_GNN].peer[q]) + par * half);
+    };
+    GemmPlan gp;
+    memset(&gp, 0, sizeof gp);
+    gp.M = x_rows; gp.N = f; gp.K = g;   // this rank's rows of X: its block of P
+    gp.A = xp; gp.sam = g; gp.sak = 1;
+    gp.B = wp; gp.sbk = f; gp.sbn = 1;
+    gp.C = gathered(c->rank) + (int64_t)c->rank * per * f; gp.scm = f; gp.scn = 1;
+    gp.scale = 1.0f; gp.beta = 0; gp.relu_term = relu ? 1 : 0;
+    for (int q = 0; q < world; ++q) {
+        if (q == c->rank) continue;
+        gp.fan[q] = gathered(q) + (int64_t)c->rank * per * f;
+        gp.fan_cnt[q] = c->peer_slots[q] + kGnnCounter + c->rank;
+    }
+    gp.fan_n = world - 1;
+    TL_TRY(launch_gemm(c, gp));
+    // every other rank's tiles of this layer, counted cumulatively
+    SpWait w{};
+    w.cnt = c->peer_slots[c->rank] + kGnnCounter;
+    w.timeout_ns = (unsigned long long)std::max(c->opts.comm_timeout_ms, 1000) * 1000000ull;
+    for (int r = 0; r < world; ++r) {
+        if (r == c->rank) continue;
+        const int64_t r_rows = nu > r ? (nu - r + world - 1) / world : 0;
+        c->gnn_expect[r] += (unsigned long long)gemm_fan_tiles(r_rows, f);
+        w.need[r] = c->gnn_expect[r];
+    }
+    TL_TRY(alloc_dense_public(c, lhs));
+    TL_TRY(launch_spmm(c, lhs->local_rows(c->rank, world), S->rowptr, S->colidx, S->vals, gathered(c->rank),
+                       per * world, f, f, lhs->dense, f, 0, 0, world, per, &w));
+    mark_written_dense(lhs);
+    lhs->boolean = false;
+    *handled = true;
+    return TL_OK;
+}
+
+// ----------------------------------------------------------------------------
 // Pattern: H[v,f] (+)= [relu] (S[v,u] X[u,g] W[g,f]) with S sparse, S >= 0
 //   → P = [relu-per-term] X·W  (dense GEMM), then H (+)= S · P  (CSR SpMM).
 // relu(s·x·w) = s·relu(x·w) for s >= 0, so the per-term relu moves inside P.
@@ -497,6 +567,14 @@ tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, 
     // P rows for the local u rows (all rows when X is replicated)
     int64_t p_rows = sharded ? lrows_x : nu;
     int64_t gathered_rows_per_rank = sharded ? (nu + c->world - 1) / c->world : 0;
+    if (sharded && xp && wp) {
+        bool handled = false;
+        TL_TRY(sparse_chain_fanned(c, S, lhs, xp, wp, nu, lrows_x, g, f, relu, &handled));
+        if (handled) {
+            *done = true;
+            return TL_OK;
+        }
+    }
     size_t p_bytes = (size_t)p_rows * f * 4;
     size_t pg_bytes = sharded ? (size_t)gathered_rows_per_rank * c->world * f * 4 : 0;
     void* ws = nullptr;
@@ -524,7 +602,9 @@ tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, 
         float* Pg = Ppad + gathered_rows_per_rank * f;
         if (p_rows > 0)
             TL_CK(c, cudaMemcpyAsync(Ppad, P, p_bytes, cudaMemcpyDeviceToDevice, c->stream));
+        LaunchScope L(c, "nccl_allgather_P", (double)gathered_rows_per_rank * c->world * f * 4.0, 0, false);
         TL_TRY(comm_allgather(c, Ppad, Pg, (size_t)gathered_rows_per_rank * f * 4));
+        TL_TRY(L.done());
         Pfull = Pg;
         col_world = c->world;
         col_local = gathered_rows_per_rank;
@@ -533,7 +613,8 @@ tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, 
     if (beta) TL_TRY(ensure_dense(c, lhs));
     else TL_TRY(alloc_dense_public(c, lhs));
     int64_t out_rows = lhs->local_rows(c->rank, c->world);
-    TL_TRY(launch_spmm(c, out_rows, S->rowptr, S->colidx, S->vals, Pfull, f, f, lhs->dense, f, beta, 0,
+    const int64_t p_total = sharded ? gathered_rows_per_rank * c->world : nu;
+    TL_TRY(launch_spmm(c, out_rows, S->rowptr, S->colidx, S->vals, Pfull, p_total, f, f, lhs->dense, f, beta, 0,
                        col_world, col_local));
     mark_written_dense(lhs);
     lhs->boolean = false;

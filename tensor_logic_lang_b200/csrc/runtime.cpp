@@ -330,7 +330,8 @@ extern "C" tl_status tl_shutdown(tl_ctx* c) {
     for (auto e : c->event_pool) cudaEventDestroy(e);
     release_graphs(c);
     comm_peer_release(c);
-    comm_sym_release(c);
+    comm_sym_release(c, SYM_CLOSURE);
+    comm_sym_release(c, SYM_GNN);
     if (c->comm) comm_destroy(c);
     for (int i = 0; i < 4; ++i) cudaFree(c->ws[i]);
     cudaFree(c->aux);
@@ -350,15 +351,22 @@ extern "C" const char* tl_last_error(const tl_ctx* c) { return c ? c->err.c_str(
 namespace tl {
 // Device-side error words: [8] a tensor-core pipeline wait gave up.
 tl_status check_device_flags(tl_ctx* c) {
-    // only the tensor-core GEMM writes the error word: without one since the
-    // last read there is nothing to read (and no reason to wait for the stream)
+    // only the tensor-core GEMM and the message-passing SpMM write the error
+    // word (1: a pipeline wait ran out, 2: a wait for another rank's tiles
+    // ran out): without one since the last read there is nothing to read
+    // (and no reason to wait for the stream)
     if (!c->flags_armed) return TL_OK;
     c->flags_armed = false;
     TL_CK(c, cudaMemcpyAsync(c->h_flags + 8, c->d_flags + 8, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     TL_CK(c, cudaStreamSynchronize(c->stream));
     if (c->h_flags[8] != 0) {
+        const int what = c->h_flags[8];
         c->h_flags[8] = 0;
         TL_CK(c, cudaMemsetAsync(c->d_flags + 8, 0, sizeof(int), c->stream));
+        if (what == 2) {
+            if (c->world > 1) c->peer_state = -1;   // the ranks' tile counts may disagree now
+            return fail(c, TL_ERR_COMM, "a wait for another rank's fanned-out tiles timed out; results are invalid");
+        }
         return fail(c, TL_ERR_CUDA, "a tensor-core pipeline wait timed out; results are invalid");
     }
     return TL_OK;

@@ -1,6 +1,7 @@
 // Internal declarations of libtl_cuda (not part of the ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -16,6 +17,14 @@ namespace tl {
 
 constexpr int kMaxVars = 12;
 constexpr int kMaxPeers = 8;   // ranks of one box that exchange fixpoint flags over NVLink
+// a buffer of one size on every rank, every rank's copy mapped into this process
+struct SymBuf {
+    int state = 0;                 // 0 none, 1 ready, -1 unavailable
+    size_t bytes = 0;
+    void* own = nullptr;
+    void* peer[kMaxPeers] = {};
+};
+enum SymSlot { SYM_CLOSURE = 0, SYM_GNN = 1 };
 
 // ----------------------------------------------------------------------------
 // Device tensor with several interchangeable storages.
@@ -181,14 +190,17 @@ struct tl_ctx {
     int peer_state = 0;                              // 0 not tried, 1 ready, -1 unavailable
     unsigned long long* peer_slots[tl::kMaxPeers] = {};
     void* peer_own = nullptr;                        // this rank's slot array
-    // a buffer of one size on every rank, every rank's copy mapped into this
-    // process: the closed words and rows the sharded closure publishes for
-    // the other ranks' peer loads (comm_sym_setup)
-    int sym_state = 0;                               // 0 none, 1 ready, -1 unavailable
-    size_t sym_bytes = 0;
-    void* sym_own = nullptr;
-    void* sym_peer[tl::kMaxPeers] = {};
+    // buffers of one size on every rank, every rank's copy mapped into this
+    // process (comm_sym_setup): [SYM_CLOSURE] the closed words and rows the
+    // sharded closure publishes for the other ranks' peer loads,
+    // [SYM_GNN] the gathered per-node transform the GNN layers fan out to
+    tl::SymBuf sym[2];
     uint32_t sym_epoch = 0;                          // closed-word epoch of the sharded lazy sweep
+    // fanned-out GNN layers: their count, and per writing rank the tiles it
+    // has signalled into this rank's counters so far
+    uint64_t gnn_layers = 0;
+    unsigned long long gnn_expect[tl::kMaxPeers] = {};
+    int fix_mode = 0;   // the last fixpoint's lazy sweep: 0 one GPU, 1 peer rows, 2 replicate, 3 local, 4 bfs
 
     // profiling
     bool prof = false;
@@ -221,8 +233,11 @@ tl_status launch_end(tl_ctx* c, cudaEvent_t* ev);
 struct LaunchScope {
     tl_ctx* c;
     cudaEvent_t ev[2] = {nullptr, nullptr};
-    LaunchScope(tl_ctx* c_, const char* name, double bytes = 0, double flops = 0) : c(c_) {
+    // own = false: timed like a kernel of this library but not counted as one
+    // (a library collective)
+    LaunchScope(tl_ctx* c_, const char* name, double bytes = 0, double flops = 0, bool own = true) : c(c_) {
         launch_begin(c, name, bytes, flops, ev);
+        if (!own) c->launches--;
     }
     tl_status done() { return launch_end(c, ev); }
 };
@@ -316,8 +331,18 @@ struct GemmPlan {
     int32_t epi_relu;    // additionally write relu(C) into D (fused next equation)
     int32_t precise;     // fp32-class accuracy (3xTF32) on the tensor cores
     float* D; int64_t sdm, sdn;
+    // fan-out (an all-gather fused into the epilogue): every output tile is
+    // also stored, with C's strides, at fan[q] in rank q's memory (peer
+    // stores over NVLink; null for this rank), and each CTA then adds 1 to
+    // fan_cnt[q] with release at system scope.  Needs the tensor-core path
+    // with its TMA-store epilogue, no split K, beta = 0 and no fused relu;
+    // tiles are TC_BM x 64 (gemm_fan_tiles counts them).
+    float* fan[kMaxPeers];
+    unsigned long long* fan_cnt[kMaxPeers];
+    int32_t fan_n;
 };
 tl_status launch_gemm(tl_ctx* c, const GemmPlan& p);
+int64_t gemm_fan_tiles(int64_t M, int64_t N);
 bool tcgen05_available(tl_ctx* c);
 // S = scale Q K^T, A = softmax over the rows of S, O = A V: row-major fp32,
 // Q, K, V and O with 64 columns, n_q and n_k multiples of 128 (k_gemm.cu)
@@ -329,10 +354,19 @@ struct AttnPlan {
 };
 tl_status launch_attention(tl_ctx* c, const AttnPlan& p);
 
-// CSR SpMM out[v, j] (+)= sum_e val[e] * P[col[e], j]
+// Before a SpMM reads rows other ranks fanned out into P: per writing rank
+// the count its tiles must have reached in this rank's counter array (0:
+// no wait), read with acquire at system scope, bounded by timeout_ns.
+struct SpWait {
+    const unsigned long long* cnt;
+    unsigned long long need[kMaxPeers];
+    unsigned long long timeout_ns;
+};
+// CSR SpMM out[v, j] (+)= sum_e val[e] * P[col[e], j]; P has p_rows rows
 tl_status launch_spmm(tl_ctx* c, int64_t rows, const int64_t* rowptr, const int32_t* colidx,
-                      const float* vals, const float* P, int64_t ldp, int64_t f, float* out,
-                      int64_t ldo, int beta, int relu_out, int col_shard_world, int64_t col_local_rows);
+                      const float* vals, const float* P, int64_t p_rows, int64_t ldp, int64_t f, float* out,
+                      int64_t ldo, int beta, int relu_out, int col_shard_world, int64_t col_local_rows,
+                      const SpWait* wait = nullptr);
 
 // closure
 tl_status launch_csr_to_dense(tl_ctx* c, Tensor* t);
@@ -358,11 +392,13 @@ tl_status fix_resolve(tl_ctx* c);
 uint64_t next_csr_stamp();
 // multi-GPU fixpoint flags over peer memory (comm.cpp); collective over all ranks
 tl_status comm_peer_setup(tl_ctx* c);
+// tensor map for tile::gather4 row gathers of a row-major fp32 matrix (k_gemm.cu)
+bool make_gather_map(CUtensorMap* map, const float* base, int64_t cols, int64_t rows, int64_t row_stride);
 void comm_peer_release(tl_ctx* c);
 // the symmetric buffer (collective; every rank passes the same size): on
-// return sym_state is 1 on every rank or -1 on every rank
-tl_status comm_sym_setup(tl_ctx* c, size_t bytes);
-void comm_sym_release(tl_ctx* c);
+// return sym[slot].state is 1 on every rank or -1 on every rank
+tl_status comm_sym_setup(tl_ctx* c, int slot, size_t bytes);
+void comm_sym_release(tl_ctx* c, int slot);
 tl_status comm_barrier(tl_ctx* c);
 // captured program runs (lower.cpp)
 void release_graphs(tl_ctx* c);

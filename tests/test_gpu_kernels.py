@@ -368,3 +368,32 @@ def test_attention_block_accumulating_scores(ctx, oracle_lib):
     ref = both(ctx, oracle_lib, src, data)
     for n in ("S", "A", "O"):
         assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
+
+
+@pytest.mark.parametrize("n,f", [(16384, 256), (16384, 128), (700, 64)])
+def test_spmm_tma_gathers_match_register_gathers(ctx, oracle_lib, monkeypatch, n, f):
+    # the message-passing SpMM gathers rows of P by tile::gather4 copies for
+    # f = 128 / 256 (TL_SPMM_REGS=1 forces the register-gather kernel).  Both
+    # sum each element's terms in nonzero order, so with the same P they give
+    # identical results; P's GEMM has one CTA per output tile at n = 16384
+    # (no split K, whose atomic adds would reorder sums), so both runs see
+    # the same P.  Both match the oracle.
+    from tensor_logic_lang_b200 import configs
+    from tensor_logic_lang_b200 import inputs as gen
+    p, d, sp, _ = configs.program(configs.gnn, n=n, f=f)
+    monkeypatch.setenv("TL_SPMM_REGS", "1")
+    ctx.run(p)
+    regs = (ctx.tensor_f32("H1"), ctx.tensor_f32("H2"))
+    monkeypatch.delenv("TL_SPMM_REGS")
+    ctx.run(p)
+    tma = (ctx.tensor_f32("H1"), ctx.tensor_f32("H2"))
+    if n >= 16384:
+        np.testing.assert_array_equal(tma[0], regs[0])
+        np.testing.assert_array_equal(tma[1], regs[1])
+    rows, cols, _ = sp["Adj"]
+    rowptr, colidx = gen.csr_from_coo(n, rows, cols)
+    h1 = oracle_lib.gnn_layer(rowptr, colidx, d["H0"], d["W1"])
+    h2 = oracle_lib.gnn_layer(rowptr, colidx, h1, d["W2"])
+    for got in (regs, tma):
+        assert_close(got[0], h1, TOL_TF32, "H1")
+        assert_close(got[1], h2, TOL_TF32, "H2")

@@ -58,7 +58,9 @@ def _closure_worker(rank, world, nid, n, kind, mode, q):
         ctx.close()
 
 
-def _gnn_worker(rank, world, nid, n, f, q):
+def _gnn_worker(rank, world, nid, n, f, mode, q):
+    if mode == "nccl":
+        os.environ["TL_GNN_NCCL"] = "1"
     from tensor_logic_lang_b200.runtime import Context
     ctx = Context(device=rank, rank=rank, world_size=world, nccl_id=nid, comm_timeout_ms=60000)
     try:
@@ -66,6 +68,7 @@ def _gnn_worker(rank, world, nid, n, f, q):
             ctx.set_sharding(name, abi.SHARD_ROWS)
         p, _, _, _ = configs.program(configs.gnn, n=n, f=f)
         ctx.run(p)
+        ctx.run(p)          # a second run: the next pair of gathered buffers and tile counts
         rows = shard.local_count(n, rank, world)
         q.put((rank, "gnn", ctx.tensor("H1", rows=rows), ctx.tensor("H2", rows=rows)))
     finally:
@@ -116,10 +119,18 @@ def test_sharded_closure(oracle_lib, n, kind, mode):
             assert 2 <= got_sweeps.pop() <= sweeps
 
 
+GNN_CASES = [(4096, 128, "fanned"), (16384, 256, "fanned"), (4096, 128, "nccl"), (3001, 64, "fanned")]
+
+
 @pytest.mark.skipif(_world() < 2, reason="needs two GPUs")
-def test_sharded_gnn(oracle_lib):
-    world, n, f = _world(), 4096, 128
-    out = _run(_gnn_worker, world, n, f)
+@pytest.mark.parametrize("n,f,mode", GNN_CASES, ids=[f"n{c[0]}-f{c[1]}-{c[2]}" for c in GNN_CASES])
+def test_sharded_gnn(oracle_lib, n, f, mode):
+    # fanned: each rank's GEMM stores its block of P into every rank's
+    # gathered copy over NVLink and counts its tiles there; nccl: the
+    # all-gather runs as a separate NCCL collective (n = 3001 has shares of
+    # unequal size)
+    world = _world()
+    out = _run(_gnn_worker, world, n, f, mode)
     h1 = shard.assemble([o[2] for o in out], n)
     h2 = shard.assemble([o[3] for o in out], n)
     _, d, sp, _ = configs.gnn(n=n, f=f)
