@@ -647,9 +647,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     for (int i = 0; i < 8; ++i) {
                         const int r = i * 4 + (lane >> 3), c4 = lane & 7;
                         const int64_t grow = (int64_t)m0 + q * 32 + r;
-                        if (grow >= epi.M) continue;
+                        const int64_t gcol = (int64_t)n0 + ch * 32 + c4 * 4;   // N is a multiple of 4
+                        if (grow >= epi.M || gcol >= epi.N) continue;
                         const float4 v = *reinterpret_cast<const float4*>(sc + r * 128 + ((c4 ^ (r & 7)) << 4));
-                        const int64_t off = grow * epi.scm + (int64_t)n0 + ch * 32 + c4 * 4;
+                        const int64_t off = grow * epi.scm + gcol;
 #pragma unroll
                         for (int j = 0; j < kMaxPeers; ++j)
                             if (epi.fan[j]) *reinterpret_cast<float4*>(epi.fan[j] + off) = v;
@@ -1070,10 +1071,14 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
 __global__ void __launch_bounds__(256)
     k_attn_rows(const float* __restrict__ opart, const float* __restrict__ mpart, const float* __restrict__ lpart,
                 int n_kt, int64_t n_q, float* __restrict__ O, int64_t lo, const float* __restrict__ S,
-                float* __restrict__ A, int64_t n_k) {
+                float* __restrict__ A, int64_t n_k, int parts) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_q; r += warps) {
+    // `parts` warps per row: each takes the row's statistics (a few tiles'
+    // m and l) and one slice of its A; the first also writes its O
+    for (int64_t wr = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wr < n_q * parts; wr += warps) {
+        const int64_t r = wr / parts;
+        const int part = (int)(wr - r * parts);
         float m = -INFINITY, lt = 0.f;
         for (int t = lane; t < n_kt; t += 32) {
             const float mt = mpart[t * n_q + r];
@@ -1090,6 +1095,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
         const float inv = 1.0f / l;
+        if (part == 0) {
         // 8 tiles' loads in flight at a time
         float o0 = 0.f, o1 = 0.f;
         for (int t0 = 0; t0 < n_kt; t0 += 8) {
@@ -1110,20 +1116,24 @@ __global__ void __launch_bounds__(256)
             }
         }
         *reinterpret_cast<float2*>(O + r * lo + 2 * lane) = make_float2(o0 * inv, o1 * inv);
+        }
+        // this warp's slice of the row: float4 columns [j_lo, j_hi)
         const int64_t q4 = n_k / 4;
+        const int64_t per = (q4 + parts - 1) / parts;
+        const int64_t j_lo = part * per, j_hi = min(q4, j_lo + per);
         const float4* Sr = reinterpret_cast<const float4*>(S + r * n_k);
         float4* Ar = reinterpret_cast<float4*>(A + r * n_k);
-        for (int64_t j0 = lane; j0 < q4; j0 += 32 * 8) {
+        for (int64_t j0 = j_lo + lane; j0 < j_hi; j0 += 32 * 8) {
             float4 v[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const int64_t j = j0 + 32 * u;
-                v[u] = j < q4 ? Sr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[u] = j < j_hi ? Sr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const int64_t j = j0 + 32 * u;
-                if (j < q4)
+                if (j < j_hi)
                     Ar[j] = make_float4(__expf(v[u].x - mstar) * inv, __expf(v[u].y - mstar) * inv,
                                         __expf(v[u].z - mstar) * inv, __expf(v[u].w - mstar) * inv);
             }
@@ -1210,6 +1220,9 @@ tl_status launch_tc_bn(tl_ctx* c, bool am, bool bm, const CUtensorMap& ma, const
     return launch_tc_inst<BN, true, true>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
 }
 
+// Tile width of the tensor-core GEMM for N output columns.
+int tc_tile_n(int64_t N) { return N >= 256 && (N % 256 == 0 || N >= 1024) ? 256 : (N >= 128 ? 128 : 64); }
+
 bool env_flag(const char* name) {
     const char* v = getenv(name);
     return v && v[0] && v[0] != '0';
@@ -1233,7 +1246,10 @@ bool make_gather_map(CUtensorMap* map, const float* base, int64_t cols, int64_t 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int64_t gemm_fan_tiles(int64_t M, int64_t N) { return ((M + TC_BM - 1) / TC_BM) * ((N + 63) / 64); }
+int64_t gemm_fan_tiles(int64_t M, int64_t N) {
+    const int bn = tc_tile_n(N);
+    return ((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn);
+}
 
 bool tcgen05_available(tl_ctx* c) {
     int major = 0, minor = 0;
@@ -1370,9 +1386,12 @@ tl_status launch_attention(tl_ctx* c, const AttnPlan& p) {
     {
         LaunchScope L(c, "attention_combine",
                       (double)part * (AT_D + 2) * 4.0 + (double)p.n_q * AT_D * 4.0 + (double)p.n_q * p.n_k * 8.0);
-        const int64_t blocks = std::min<int64_t>((p.n_q + 7) / 8, (int64_t)c->sm_count * 8);
+        // enough warps to fill the GPU: a row split over up to 4 warps
+        int parts = 1;
+        while (parts < 4 && p.n_q * parts < (int64_t)c->sm_count * 48 && p.n_k / 4 >= 64 * parts * 2) parts *= 2;
+        const int64_t blocks = std::min<int64_t>((p.n_q * parts + 7) / 8, (int64_t)c->sm_count * 8);
         k_attn_rows<<<(unsigned)blocks, 256, 0, c->stream>>>(a.opart, a.mpart, a.lpart, n_kt, p.n_q, p.O, AT_D, p.S,
-                                                             p.A, p.n_k);
+                                                             p.A, p.n_k, parts);
         TL_TRY(L.done());
     }
     return TL_OK;
@@ -1392,7 +1411,7 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     const double macs = (double)p.M * p.N * p.K;
     bool tc = c->opts.precision == TL_PREC_TF32 && tcgen05_available(c) && p.M >= 128 && p.N >= 64 && p.K >= 32 &&
               macs >= (double)(1 << 25);
-    if (p.fan_n && (!tc || p.beta || p.epi_relu || p.N % 64))
+    if (p.fan_n && (!tc || p.beta || p.epi_relu || p.N % 4 || p.scn != 1))
         return fail(c, TL_ERR_UNSUPPORTED, "fanned-out GEMM needs the tensor-core path (M %lld, N %lld)",
                     (long long)p.M, (long long)p.N);
     if (!tc) return launch_simt(c, p);
@@ -1458,9 +1477,9 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     }
     // the maps span Ke; TMA reads zeros past it (the K tail of the last block)
     CUtensorMap ma, mb;
-    // a fanned-out GEMM takes 64-wide tiles: more CTAs for the few rows of a
-    // shard, and a tile count every rank can compute (gemm_fan_tiles)
-    const int BN = p.fan_n ? 64 : p.N >= 256 && (p.N % 256 == 0 || p.N >= 1024) ? 256 : (p.N >= 128 ? 128 : 64);
+    // the tile width depends on N alone, so every rank can count another
+    // rank's fanned-out tiles (gemm_fan_tiles)
+    const int BN = tc_tile_n(p.N);
     bool ok = pa.mn ? make_map(&ma, pa.dst, p.M, Ke, pa.ld, 32, true) : make_map(&ma, pa.dst, Ke, p.M, pa.ld, TC_BM, false);
     ok = ok && (pb.mn ? make_map(&mb, pb.dst, p.N, Ke, pb.ld, 32, true) : make_map(&mb, pb.dst, Ke, p.N, pb.ld, BN, false));
     if (!ok) return launch_simt(c, p);

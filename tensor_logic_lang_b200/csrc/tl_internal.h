@@ -335,8 +335,8 @@ struct GemmPlan {
     // also stored, with C's strides, at fan[q] in rank q's memory (peer
     // stores over NVLink; null for this rank), and each CTA then adds 1 to
     // fan_cnt[q] with release at system scope.  Needs the tensor-core path
-    // with its TMA-store epilogue, no split K, beta = 0 and no fused relu;
-    // tiles are TC_BM x 64 (gemm_fan_tiles counts them).
+    // with its TMA-store epilogue, no split K, beta = 0 and no fused relu
+    // (gemm_fan_tiles counts its tiles).
     float* fan[kMaxPeers];
     unsigned long long* fan_cnt[kMaxPeers];
     int32_t fan_n;

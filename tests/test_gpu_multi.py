@@ -90,8 +90,8 @@ def _run(target, world, *args):
     return sorted(out, key=lambda t: t[0])
 
 
-CLOSURE_CASES = [(8192, "dag", "peer"), (5000, "cyclic", "peer"), (8192, "dag", "replicate"),
-                 (5000, "cyclic", "local")]
+CLOSURE_CASES = [(8192, "dag", "replicate"), (5000, "cyclic", "replicate"), (8192, "dag", "peer"),
+                 (5000, "cyclic", "peer"), (5000, "cyclic", "local"), (4099, "dag", "bfs")]
 
 
 @pytest.mark.skipif(_world() < 2, reason="needs two GPUs")
@@ -146,6 +146,9 @@ def _skip_worker(rank, world, nid, mode, q, done):
     # a rank that skips the second fixpoint: it stays alive, with none of its
     # kernels or collectives in flight, until rank 0 has seen its wait run out
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    # peer: the scheme whose changed words cross GPUs inside the launch (the
+    # default replicated scheme needs no exchange, so nothing would wait)
+    os.environ["TL_CLOSURE_SHARDED"] = "peer"
     if mode == "nccl":
         os.environ["TL_NO_PEER_FLAGS"] = "1"
     from tensor_logic_lang_b200 import abi as A
