@@ -361,7 +361,7 @@ struct RowSearch {
 // node whose local row is closed (lazy sweep) is ORed in, not expanded.
 // budget > 0: returns false once more than that many bits were expanded (the
 // row goes to a team); true when the row is closed.
-template <int ITEMS, bool PEER>
+template <int ITEMS, bool PEER, bool COUNT = false>
 __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool own_first, bool dp, int budget,
                                            uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
@@ -411,8 +411,10 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
 #pragma unroll
             for (int k = 0; k < ITEMS; ++k) {
                 if (L[k] >= 0 && (uint32_t)(CW[k] >> 42) == a.epoch) {
-                    if (PEER && (uint32_t)L[k] % (uint32_t)a.world != (uint32_t)a.rank) S.n_or_remote++;
-                    else S.n_or_local++;
+                    if (COUNT) {
+                        if (PEER && (uint32_t)L[k] % (uint32_t)a.world != (uint32_t)a.rank) S.n_or_remote++;
+                        else S.n_or_local++;
+                    }
                     Y[k] = -1;   // closed: ORed in below
                 } else {
                     L[k] = -1;
@@ -420,7 +422,7 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
             }
 #pragma unroll
             for (int k = 0; k < ITEMS; ++k)
-                if (Y[k] >= 0) S.n_expanded++;
+                if (COUNT && Y[k] >= 0) S.n_expanded++;
         }
         __syncwarp();   // the taken slots may be refilled from here on
         S.head += take;
@@ -628,7 +630,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
 // that successor is then expanded instead, with the same result.  A row grew
 // if it ends with more bits than succ(x) has.  Once written, the row publishes
 // its closed word (release at GPU scope) and its pending word.
-template <bool PEER>
+template <bool PEER, bool COUNT>
 __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long long* next_row, int budget,
                                               uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
@@ -722,11 +724,11 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         // its successors' closed words, in flight during the search and write-back
         cw_next = closed_of(t_next);
 
-        if (closed) {
+        if (COUNT && closed) {
             if (PEER && (uint32_t)l0 % (uint32_t)a.world != (uint32_t)a.rank) c_orr++;
             else c_orl++;
         }
-        const bool done = search_row<1, PEER>(a, S, false, true, budget, row, spill, q, lane);
+        const bool done = search_row<1, PEER, COUNT>(a, S, false, true, budget, row, spill, q, lane);
         c_orl += S.n_or_local;
         c_orr += S.n_or_remote;
         c_exp += S.n_expanded;
@@ -788,6 +790,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         pub_w = lo_w < hi_w ? closed_word(a.epoch, lo_w, hi_w) : closed_word(a.epoch, 0, 0);
         publish();
     }
+    if (COUNT) {
     c_orl = __reduce_add_sync(0xffffffffu, c_orl);
     c_orr = __reduce_add_sync(0xffffffffu, c_orr);
     c_exp = __reduce_add_sync(0xffffffffu, c_exp);
@@ -795,6 +798,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         atomicAdd(&a.st->n_or_local, c_orl);
         atomicAdd(&a.st->n_or_remote, c_orr);
         atomicAdd(&a.st->n_expanded, c_exp);
+    }
     }
     return any;
 }
@@ -1035,7 +1039,8 @@ __device__ bool grid_barrier(const FixArgs& a, unsigned gen, int s, bool settle)
     return ok_s != 0;
 }
 
-template <bool PEER>
+// COUNT: the lazy sweep counts its work (profiling runs that ask for it)
+template <bool PEER, bool COUNT>
 __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs a) {
     extern __shared__ __align__(16) uint32_t smem_fix[];
     __shared__ int s_idx;
@@ -1056,7 +1061,7 @@ __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs
         __syncwarp();
         const int budget = a.team > 1 ? a.team_budget : 0;
         const bool grew = lazy && a.shortcut
-                              ? close_rows_dp<PEER>(a, &a.st->next_row[s & 1], a.dp_copy || PEER ? 0 : budget, row,
+                              ? close_rows_dp<PEER, COUNT>(a, &a.st->next_row[s & 1], a.dp_copy || PEER ? 0 : budget, row,
                                               spill, q, lane)
                               : close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, lazy, budget, row, spill, q,
                                            lane);
@@ -1257,16 +1262,21 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     const size_t per_warp = fix_smem_per_warp(words);
     const bool teams = getenv("TL_CLOSURE_TEAMS") != nullptr;
     if (c->fix_shape_words != words || c->fix_shape_teams != (int)teams) {
-        TL_CK(c, cudaFuncSetAttribute(k_closure_fix<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
-        TL_CK(c, cudaFuncSetAttribute(k_closure_fix<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
+        for (const void* fn : {(const void*)k_closure_fix<false, false>, (const void*)k_closure_fix<true, false>,
+                               (const void*)k_closure_fix<false, true>, (const void*)k_closure_fix<true, true>})
+            TL_CK(c, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
         int wpb = 1, per_sm = 0;
         for (int w = kFixWarps; w >= 1; w >>= 1) {
             if (per_warp * w > kSmemCap) continue;
             int b = 0;
-            int b2 = 0;
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_closure_fix<false>, 32 * w, per_warp * w);
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b2, k_closure_fix<true>, 32 * w, per_warp * w);
-            b = std::min(b, b2);   // one shape for both (every rank computes the same)
+            // one shape for every variant (and every rank computes the same)
+            b = INT32_MAX;
+            for (const void* fn : {(const void*)k_closure_fix<false, false>, (const void*)k_closure_fix<true, false>,
+                                   (const void*)k_closure_fix<false, true>, (const void*)k_closure_fix<true, true>}) {
+                int bb = 0;
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bb, fn, 32 * w, per_warp * w);
+                b = std::min(b, bb);
+            }
             if (b < 1) continue;
             if (teams) { wpb = w; per_sm = b; break; }
             if (b * w > per_sm * wpb) { wpb = w; per_sm = b; }
@@ -1349,7 +1359,12 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     {
         LaunchScope L(c, "closure_fixpoint", sweep_bytes);
         void* args[] = {&a};
-        const void* fn = peer_rows ? (const void*)k_closure_fix<true> : (const void*)k_closure_fix<false>;
+        // the work counters only in profiling runs that ask for them
+        // (TL_CLOSURE_COUNTS): they cost the sweep a few per cent
+        const bool count = c->prof && getenv("TL_CLOSURE_COUNTS") != nullptr;
+        const void* fn = peer_rows ? (count ? (const void*)k_closure_fix<true, true> : (const void*)k_closure_fix<true, false>)
+                                   : (count ? (const void*)k_closure_fix<false, true> : (const void*)k_closure_fix<false, false>);
+        c->fix_counted = count;
         TL_CK(c, cudaLaunchCooperativeKernel(fn, dim3((unsigned)grid), dim3(32 * wpb), args,
                                              per_warp * wpb, c->stream));
         TL_TRY(L.done());
@@ -1407,7 +1422,7 @@ tl_status fix_resolve(tl_ctx* c) {
             prev = h.t_settled[s];
         }
     }
-    if (c->fix_prof) {
+    if (c->fix_prof && c->fix_counted) {
         // the lazy sweep's work and the way its shortcuts were read
         auto count = [&](const char* what, double v) {
             KStat& k = c->stats[std::string("closure_fixpoint.n_") + what];

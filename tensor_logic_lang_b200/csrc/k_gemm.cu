@@ -1071,14 +1071,10 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
 __global__ void __launch_bounds__(256)
     k_attn_rows(const float* __restrict__ opart, const float* __restrict__ mpart, const float* __restrict__ lpart,
                 int n_kt, int64_t n_q, float* __restrict__ O, int64_t lo, const float* __restrict__ S,
-                float* __restrict__ A, int64_t n_k, int parts) {
+                float* __restrict__ A, int64_t n_k) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    // `parts` warps per row: each takes the row's statistics (a few tiles'
-    // m and l) and one slice of its A; the first also writes its O
-    for (int64_t wr = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; wr < n_q * parts; wr += warps) {
-        const int64_t r = wr / parts;
-        const int part = (int)(wr - r * parts);
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_q; r += warps) {
         float m = -INFINITY, lt = 0.f;
         for (int t = lane; t < n_kt; t += 32) {
             const float mt = mpart[t * n_q + r];
@@ -1095,7 +1091,6 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
         const float inv = 1.0f / l;
-        if (part == 0) {
         // 8 tiles' loads in flight at a time
         float o0 = 0.f, o1 = 0.f;
         for (int t0 = 0; t0 < n_kt; t0 += 8) {
@@ -1116,24 +1111,20 @@ __global__ void __launch_bounds__(256)
             }
         }
         *reinterpret_cast<float2*>(O + r * lo + 2 * lane) = make_float2(o0 * inv, o1 * inv);
-        }
-        // this warp's slice of the row: float4 columns [j_lo, j_hi)
         const int64_t q4 = n_k / 4;
-        const int64_t per = (q4 + parts - 1) / parts;
-        const int64_t j_lo = part * per, j_hi = min(q4, j_lo + per);
         const float4* Sr = reinterpret_cast<const float4*>(S + r * n_k);
         float4* Ar = reinterpret_cast<float4*>(A + r * n_k);
-        for (int64_t j0 = j_lo + lane; j0 < j_hi; j0 += 32 * 8) {
+        for (int64_t j0 = lane; j0 < q4; j0 += 32 * 8) {
             float4 v[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const int64_t j = j0 + 32 * u;
-                v[u] = j < j_hi ? Sr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[u] = j < q4 ? Sr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const int64_t j = j0 + 32 * u;
-                if (j < j_hi)
+                if (j < q4)
                     Ar[j] = make_float4(__expf(v[u].x - mstar) * inv, __expf(v[u].y - mstar) * inv,
                                         __expf(v[u].z - mstar) * inv, __expf(v[u].w - mstar) * inv);
             }
@@ -1386,12 +1377,9 @@ tl_status launch_attention(tl_ctx* c, const AttnPlan& p) {
     {
         LaunchScope L(c, "attention_combine",
                       (double)part * (AT_D + 2) * 4.0 + (double)p.n_q * AT_D * 4.0 + (double)p.n_q * p.n_k * 8.0);
-        // enough warps to fill the GPU: a row split over up to 4 warps
-        int parts = 1;
-        while (parts < 4 && p.n_q * parts < (int64_t)c->sm_count * 48 && p.n_k / 4 >= 64 * parts * 2) parts *= 2;
-        const int64_t blocks = std::min<int64_t>((p.n_q * parts + 7) / 8, (int64_t)c->sm_count * 8);
+        const int64_t blocks = std::min<int64_t>((p.n_q + 7) / 8, (int64_t)c->sm_count * 8);
         k_attn_rows<<<(unsigned)blocks, 256, 0, c->stream>>>(a.opart, a.mpart, a.lpart, n_kt, p.n_q, p.O, AT_D, p.S,
-                                                             p.A, p.n_k, parts);
+                                                             p.A, p.n_k);
         TL_TRY(L.done());
     }
     return TL_OK;

@@ -558,85 +558,90 @@ __global__ void __launch_bounds__(32 * kSpMaxWarps) k_spmm_tma(const __grid_cons
     __syncwarp();
     const int64_t warps = (int64_t)gridDim.x * kSpWarps;
     const int64_t first = (int64_t)blockIdx.x * kSpWarps + wib;
-    // producer (issues) and consumer (sums) positions in the batch stream;
-    // every lane keeps both, so control flow stays uniform
-    int64_t pv = first, pe = 0, pend = 0;
-    if (pv < rows) { pe = rowptr[pv]; pend = rowptr[pv + 1]; }
-    int64_t cv = first, ce = pe, cend = pend;
-    uint32_t issued = 0, consumed = 0;
-    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-    auto remap = [&](int64_t u) { return col_world > 1 ? (u % col_world) * col_local + u / col_world : u; };
-    while (cv < rows) {
-        // fill free slots with the next batches
-        while (issued - consumed < (uint32_t)kSpSlots && pv < rows) {
-            if (pe >= pend) {
-                pv += warps;
-                if (pv < rows) { pe = rowptr[pv]; pend = rowptr[pv + 1]; }
-                continue;
+    // A row's nonzeros are taken 32 at a time: lane i holds the i-th column
+    // (remapped to the gathered layout) and value, so a batch's four row
+    // indices and weights come by shuffles, not by loads on the path to the
+    // next copy.  Batches go into the ring in order; use u of the ring is
+    // slot u % nslots, phase (u / nslots) & 1.
+    uint32_t used = 0;
+    int64_t nx0 = 0, nx1 = 0;   // the next row's nonzero range, loaded a row ahead
+    if (first < rows) { nx0 = rowptr[first]; nx1 = rowptr[first + 1]; }
+    for (int64_t v = first; v < rows; v += warps) {
+        const int64_t e0 = nx0, e1 = nx1;
+        if (v + warps < rows) { nx0 = rowptr[v + warps]; nx1 = rowptr[v + warps + 1]; }
+        float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+        for (int64_t eb = e0; eb < e1; eb += 32) {
+            const int ne = (int)(e1 - eb < 32 ? e1 - eb : 32);
+            int32_t u_l = 0;
+            float w_l = 0.f;
+            if (lane < ne) {
+                const int64_t u = colidx[eb + lane];
+                u_l = (int32_t)(col_world > 1 ? (u % col_world) * col_local + u / col_world : u);
+                w_l = vals[eb + lane];
             }
-            const int cnt = (int)(pend - pe < 4 ? pend - pe : 4);
-            if (lane == 0) {
+            const int nb = (ne + 3) >> 2;
+            auto issue = [&](int b) {   // batch b of this chunk into the ring (uniform: every lane shuffles)
                 int32_t u[4];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) u[t] = (int32_t)remap(colidx[pe + (t < cnt ? t : 0)]);
-                const int slot = (int)(issued % kSpSlots);
-                uint64_t* bar = &bars[slot];
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sp_smem_u32(bar)),
-                             "r"(SLOT * 4)
-                             : "memory");
-                asm volatile(
-                    "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
-                    "[%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(sp_smem_u32(ring + (size_t)slot * SLOT)),
-                    "l"(reinterpret_cast<uint64_t>(&tmP)), "r"(sp_smem_u32(bar)), "r"(0), "r"(u[0]), "r"(u[1]),
-                    "r"(u[2]), "r"(u[3])
-                    : "memory");
-            }
-            pe += cnt;
-            ++issued;
-        }
-        if (ce >= cend) {
-            // the row is summed: store it, then the next row of this warp
-            float* op = out + cv * ldo;
-            float4* o0 = reinterpret_cast<float4*>(op + lane * 4);
-            if (beta) { const float4 o = *o0; a0.x += o.x; a0.y += o.y; a0.z += o.z; a0.w += o.w; }
-            *o0 = a0;
-            if (F == 256) {
-                float4* o1 = reinterpret_cast<float4*>(op + 128 + lane * 4);
-                if (beta) { const float4 o = *o1; a1.x += o.x; a1.y += o.y; a1.z += o.z; a1.w += o.w; }
-                *o1 = a1;
-            }
-            a0 = make_float4(0.f, 0.f, 0.f, 0.f);
-            a1 = a0;
-            cv += warps;
-            if (cv < rows) { ce = rowptr[cv]; cend = rowptr[cv + 1]; }
-            continue;
-        }
-        const int cnt = (int)(cend - ce < 4 ? cend - ce : 4);
-        const int slot = (int)(consumed % kSpSlots);
-        if (!sp_wait(&bars[slot], (consumed / kSpSlots) & 1u, err)) return;
-        const float* rp = ring + (size_t)slot * SLOT;
-        float w[4];
-        float4 p0[4], p1[4];
+                for (int t = 0; t < 4; ++t) {
+                    const int k = 4 * b + t;
+                    u[t] = __shfl_sync(0xffffffffu, u_l, k < ne ? k : 4 * b);
+                }
+                if (lane == 0) {
+                    const int slot = (int)((used + (uint32_t)b) % (uint32_t)kSpSlots);
+                    uint64_t* bar = &bars[slot];
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sp_smem_u32(bar)),
+                                 "r"(SLOT * 4)
+                                 : "memory");
+                    asm volatile(
+                        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+                        "[%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(sp_smem_u32(ring + (size_t)slot * SLOT)),
+                        "l"(reinterpret_cast<uint64_t>(&tmP)), "r"(sp_smem_u32(bar)), "r"(0), "r"(u[0]), "r"(u[1]),
+                        "r"(u[2]), "r"(u[3])
+                        : "memory");
+                }
+            };
+            const int ahead = nb < kSpSlots ? nb : kSpSlots;
+            for (int b = 0; b < ahead; ++b) issue(b);
+            for (int b = 0; b < nb; ++b) {
+                const uint32_t use = used + (uint32_t)b;
+                const int slot = (int)(use % (uint32_t)kSpSlots);
+                if (!sp_wait(&bars[slot], (use / (uint32_t)kSpSlots) & 1u, err)) return;
+                const float* rp = ring + (size_t)slot * SLOT;
+                const int cnt = ne - 4 * b < 4 ? ne - 4 * b : 4;
+                float w[4];
+                float4 p0[4], p1[4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            w[t] = t < cnt ? __ldg(vals + ce + t) : 0.f;
-            p0[t] = *reinterpret_cast<const float4*>(rp + t * F + lane * 4);
-            p1[t] = F == 256 ? *reinterpret_cast<const float4*>(rp + t * F + 128 + lane * 4) : p0[t];
-        }
+                for (int t = 0; t < 4; ++t) {
+                    w[t] = __shfl_sync(0xffffffffu, w_l, (4 * b + t) & 31);
+                    p0[t] = *reinterpret_cast<const float4*>(rp + t * F + lane * 4);
+                    p1[t] = F == 256 ? *reinterpret_cast<const float4*>(rp + t * F + 128 + lane * 4) : p0[t];
+                }
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            if (t >= cnt) break;
-            a0.x = fmaf(w[t], p0[t].x, a0.x); a0.y = fmaf(w[t], p0[t].y, a0.y);
-            a0.z = fmaf(w[t], p0[t].z, a0.z); a0.w = fmaf(w[t], p0[t].w, a0.w);
-            if (F == 256) {
-                a1.x = fmaf(w[t], p1[t].x, a1.x); a1.y = fmaf(w[t], p1[t].y, a1.y);
-                a1.z = fmaf(w[t], p1[t].z, a1.z); a1.w = fmaf(w[t], p1[t].w, a1.w);
+                for (int t = 0; t < 4; ++t) {
+                    if (t >= cnt) break;
+                    a0.x = fmaf(w[t], p0[t].x, a0.x); a0.y = fmaf(w[t], p0[t].y, a0.y);
+                    a0.z = fmaf(w[t], p0[t].z, a0.z); a0.w = fmaf(w[t], p0[t].w, a0.w);
+                    if (F == 256) {
+                        a1.x = fmaf(w[t], p1[t].x, a1.x); a1.y = fmaf(w[t], p1[t].y, a1.y);
+                        a1.z = fmaf(w[t], p1[t].z, a1.z); a1.w = fmaf(w[t], p1[t].w, a1.w);
+                    }
+                }
+                __syncwarp();   // every lane has read the slot: it may be refilled
+                if (b + kSpSlots < nb) issue(b + kSpSlots);
             }
+            used += (uint32_t)nb;
         }
-        __syncwarp();   // every lane has read the slot: it may be refilled
-        ce += cnt;
-        ++consumed;
+        float* op = out + v * ldo;
+        float4* o0 = reinterpret_cast<float4*>(op + lane * 4);
+        if (beta) { const float4 o = *o0; a0.x += o.x; a0.y += o.y; a0.z += o.z; a0.w += o.w; }
+        *o0 = a0;
+        if (F == 256) {
+            float4* o1 = reinterpret_cast<float4*>(op + 128 + lane * 4);
+            if (beta) { const float4 o = *o1; a1.x += o.x; a1.y += o.y; a1.z += o.z; a1.w += o.w; }
+            *o1 = a1;
+        }
     }
 }
 
@@ -826,10 +831,12 @@ tl_status launch_spmm(tl_ctx* c, int64_t rows, const int64_t* rowptr, const int3
         // gathers by the TMA: a persistent grid, three blocks of four warps per SM
         // ring slots per warp, warps per block and blocks per SM (TL_SPMM_SHAPE
         // = "slots,warps,blocks" overrides, for measurements)
-        // (measured on the 2-layer GNN, n = 16384, f = 256: one slot per warp,
-        // eight warps per block, four blocks per SM was the fastest of the
-        // shapes tried, 0.062 ms per step against 0.075 ms for the register
-        // gathers; more slots per warp with fewer warps were slower)
+        // (measured on the 2-layer GNN, n = 16384, f = 256, SpMM time per step:
+        // one slot per warp, eight warps per block, four blocks per SM 0.055 ms;
+        // two slots 0.059-0.061 ms; four slots 0.081-0.101 ms; eight slots
+        // 0.130 ms; the register gathers 0.072 ms.  More copies in flight per
+        // SM queue behind each other: the gathers' rate per SM, not the bytes
+        // in flight, bounds the kernel)
         int kSpSlots = 1, kSpWarps = 8, bps = 4;
         if (const char* sh = getenv("TL_SPMM_SHAPE")) sscanf(sh, "%d,%d,%d", &kSpSlots, &kSpWarps, &bps);
         kSpSlots = std::max(1, std::min(kSpSlots, kSpMaxSlots));

@@ -200,6 +200,7 @@ struct tl_ctx {
     // has signalled into this rank's counters so far
     uint64_t gnn_layers = 0;
     unsigned long long gnn_expect[tl::kMaxPeers] = {};
+    bool fix_counted = false;   // the last fixpoint launch counted its lazy sweep's work
     int fix_mode = 0;   // the last fixpoint's lazy sweep: 0 one GPU, 1 peer rows, 2 replicate, 3 local, 4 bfs
 
     // profiling
