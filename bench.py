@@ -36,12 +36,12 @@ DEG_CLOSURE = 4
 METRIC = "closure_fixpoint_iters_per_s"
 # DRAM bytes one launch of the one-launch fixpoint moves on this workload at
 # N = 1: dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of
-# the current kernel (2.45 MB read, 78.79 MB written; the rest of the rows
+# the current kernel (2.36 MB read, 78.76 MB written; the rest of the rows
 # are still in L2 when the kernel ends), measured with
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
 #       --clock-control none -k regex:k_closure_fix -s 2 -c 1
 #       python bench.py --workload closure --steps 1 --warmup 3 --cpu-sample-s 0
-CLOSURE_TRAFFIC_1GPU = 81.24e6
+CLOSURE_TRAFFIC_1GPU = 81.12e6
 UNIT = "sweeps/s"
 
 
@@ -370,7 +370,9 @@ def closure_parity(dist, out_bits, sweeps, rows, cols):
     colptr, rowidx = gen.csr_from_coo(n, cols, rows)
     R = np.zeros((n, n // 32), dtype=np.uint32)
     np.bitwise_or.at(R, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
+    t1 = time.perf_counter()
     osw = oracle.closure_right(n, colptr, rowidx, R, threads=os.cpu_count() or 1)
+    t_closure = time.perf_counter() - t1
     want = row_digests(R)
     world = len(digests)
     bad = sum(1 for r, (dg, _) in enumerate(digests) for k, d in enumerate(dg) if d != want[k * world + r])
@@ -379,6 +381,7 @@ def closure_parity(dist, out_bits, sweeps, rows, cols):
     return {"closure": "bit-exact" if bad == 0 and checked == n and sw_ok else "MISMATCH",
             "rows_checked": checked, "rows_differing": bad, "sweeps": [sw for _, sw in digests],
             "oracle_sweeps": osw, "oracle_s": round(time.perf_counter() - t0, 2),
+            "closure_right_s": round(t_closure, 3),
             "how": "blake2b digest of every row gathered from every rank vs the f64 oracle's closure_right"}
 
 
@@ -543,14 +546,14 @@ def run_rowwise_configs(args, peaks):
 
 
 # ---------------------------------------------------------------------------- reference arm
-def literal_sample(seconds=12.0, threads=1):
+def literal_sample(seconds=12.0, threads=1, libname="liboracle.so", n=N_CLOSURE):
     """Time the literal reference sweep on sample rows, `threads` rows at a time on
-    as many host threads; returns sweeps/s of the whole relation."""
+    as many host threads, with the oracle built as `libname`; returns sweeps/s
+    of the whole n-node relation."""
     from oracle import oracle
     from tensor_logic_lang_b200 import configs
-    _, _, sparse, _ = configs.closure(n=N_CLOSURE, degree=DEG_CLOSURE)
+    _, _, sparse, _ = configs.closure(n=n, degree=DEG_CLOSURE)
     rows, cols, _ = sparse["Edge"]
-    n = N_CLOSURE
     W = n // 32
     E = np.zeros((n, W), dtype=np.uint32)
     np.bitwise_or.at(E, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
@@ -561,7 +564,7 @@ def literal_sample(seconds=12.0, threads=1):
             x = (done_rows + b) % 64
             R[b, cols[rows == x]] = 1.0            # Reach[x,:] = step(Edge[x,:])
         t0 = time.perf_counter()
-        oracle.closure_literal_rows(n, E, R, threads=threads)
+        oracle.closure_literal_rows(n, E, R, threads=threads, libname=libname)
         t += time.perf_counter() - t0
         done_rows += threads
     per_row = t / done_rows
@@ -637,6 +640,24 @@ def main():
         cpu = {"value": sps, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"literal x,z,y loop nest of one sweep (oracle/, -O2) on {rows_done} rows, "
                          f"{cores} at a time on {cores} threads ({secs:.1f} s), scaled by n rows per sweep"}
+        # one core, the oracle built -O2 and -O0 (the reference binary's clang
+        # line has no -O): a row of the literal sweep costs n^2 inner steps, so
+        # rows of a 4096-node relation are timed and scaled by (4096 / n)^3
+        small = 4096
+        scale = (small / N_CLOSURE) ** 3
+        single = {}
+        for lib, tag in (("liboracle.so", "O2"), ("liboracle_O0.so", "O0")):
+            v, r1, t1 = literal_sample(seconds=2.0, threads=1, libname=lib, n=small)
+            single[tag] = {"value": v * scale, "unit": UNIT, "cores": 1,
+                           "sample": f"{r1} rows of n={small} in {t1:.1f} s, scaled by (n/{small})^3 "
+                                     f"(an extrapolation)"}
+        cpu["single_core"] = single
+        # the same closure by a row-wise CPU algorithm (the oracle's sweep over
+        # predecessor lists, every host thread), timed in the parity check
+        if res["parity"] and res["parity"].get("closure_right_s"):
+            cpu["rowwise_cpu_closure"] = {
+                "value": res["sweeps"] / res["parity"]["closure_right_s"], "unit": UNIT, "cores": cores,
+                "sample": "oracle closure_right over the whole relation (-O2, OpenMP over rows)"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,

@@ -494,11 +494,10 @@ unsigned grid_for(tl_ctx* c, int64_t items, int per_block) {
 // fills them with cp.async.bulk.tensor tile::gather4 copies (four nonzeros
 // of one row per copy, completion counted on the slot's mbarrier) while the
 // lanes sum the slots already landed, so no registers hold gathers in
-// flight and a block of 48 registers per thread leaves room for 32 warps
-// per SM.  Rows are taken cyclically (warp w: rows w, w +
-// warps, ...) as one stream of four-nonzero batches; each element sums its
-// terms in nonzero order with the same fmaf sequence as k_spmm, so the two
-// kernels give identical results.
+// flight and 58 registers per thread leave room for 32 warps per SM.  Rows
+// are taken cyclically (warp w: rows w, w + warps, ...); each element sums
+// its terms in nonzero order with the same fmaf sequence as k_spmm, so the
+// two kernels give identical results.
 constexpr int kSpMaxSlots = 16;   // ring slots per warp (runtime count up to this)
 constexpr int kSpMaxWarps = 8;    // warps per block (runtime count up to this)
 
