@@ -355,6 +355,53 @@ __device__ __forceinline__ bool spmm_wait_peers(const SpWait& w, int* err) {
     return ok_s != 0;
 }
 
+// The all-gather of a row-sharded GNN layer as peer stores: this rank's
+// block of the gathered P (`len` floats at src, 16-byte aligned) is copied
+// into the same place of every other rank's copy (dst[q], null for this
+// rank), each block of threads storing a contiguous range with 128-bit
+// stores over NVLink; then one thread per block adds 1 to every other
+// rank's counter for this rank (release at system scope), after the
+// block's stores (barrier, then a system-scope fence).
+constexpr int kPushBlocks = 512;   // blocks of the push (every rank counts this many per layer)
+
+struct PushArgs {
+    const float* src;
+    int64_t len;                           // floats, a multiple of 4
+    float* dst[kMaxPeers];
+    unsigned long long* cnt[kMaxPeers];
+};
+
+__global__ void __launch_bounds__(256) k_fan_push(const __grid_constant__ PushArgs a) {
+    const int64_t n4 = a.len / 4;
+    const int64_t per = (n4 + gridDim.x - 1) / gridDim.x;
+    const int64_t b0 = (int64_t)blockIdx.x * per, b1 = min(n4, b0 + per);
+    const float4* s4 = reinterpret_cast<const float4*>(a.src);
+    for (int64_t i = b0 + threadIdx.x; i < b1; i += 4 * (int64_t)blockDim.x) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t j = i + (int64_t)u * blockDim.x;
+            v[u] = j < b1 ? s4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q = 0; q < kMaxPeers; ++q) {
+            if (!a.dst[q]) continue;
+            float4* d4 = reinterpret_cast<float4*>(a.dst[q]);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t j = i + (int64_t)u * blockDim.x;
+                if (j < b1) d4[j] = v[u];
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int q = 0; q < kMaxPeers; ++q)
+            if (a.cnt[q]) asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(a.cnt[q]), "l"(1ull) : "memory");
+    }
+}
+
 template <int U>
 __global__ void __launch_bounds__(256) k_spmm(int64_t rows, const int64_t* __restrict__ rowptr,
                                               const int32_t* __restrict__ colidx, const float* __restrict__ vals,
@@ -645,6 +692,22 @@ __global__ void __launch_bounds__(32 * kSpMaxWarps) k_spmm_tma(const __grid_cons
 }
 
 }  // namespace
+
+int64_t fan_push_blocks() { return kPushBlocks; }
+
+tl_status launch_fan_push(tl_ctx* c, const float* src, int64_t len, float* const* dst,
+                          unsigned long long* const* cnt) {
+    PushArgs a{};
+    a.src = src;
+    a.len = len;
+    for (int q = 0; q < kMaxPeers; ++q) {
+        a.dst[q] = dst[q];
+        a.cnt[q] = cnt[q];
+    }
+    LaunchScope L(c, "gnn_fan_push", (double)len * 4.0, 0);
+    k_fan_push<<<kPushBlocks, 256, 0, c->stream>>>(a);
+    return L.done();
+}
 
 tl_status launch_csr_to_dense(tl_ctx* c, Tensor* t) {
     const int64_t rows = t->csr_rows;

@@ -452,18 +452,19 @@ Tensor* relu_successor(tl_ctx* c, const tl_equation* eq, const tl_equation* next
 }
 
 // ----------------------------------------------------------------------------
-// Row-sharded message passing with the all-gather fused into the GEMM: each
-// rank's P = [relu-per-term] X W for its rows is stored by the GEMM's
-// epilogue into its block of the gathered P on every rank (peer stores over
-// NVLink into a buffer every rank maps), each CTA counting its tile into
-// every rank's counters; the SpMM of the rank's own output rows waits for
-// every other rank's tile count and then reads the gathered P locally.
-// Gathered P alternates between two buffers by layer: a rank writes layer
-// k's buffer only after its layer k - 1 SpMM saw every rank's layer k - 1
-// tiles, so every rank has finished the SpMM of layer k - 2 (the last
-// reader of that buffer).  The decision depends only on quantities every
-// rank shares (sizes, the collective peer set-up), so all ranks take the
-// same path; otherwise the NCCL all-gather below runs.
+// Row-sharded message passing with the all-gather done by this library over
+// NVLink: each rank's P = [relu-per-term] X W for its rows goes into its
+// block of the gathered P, and from there into the same block of every other
+// rank's copy (a buffer every rank maps) by peer stores: a push kernel after
+// the GEMM (default), or the GEMM's own epilogue (TL_GNN_FAN=epilogue).  The
+// storing blocks count themselves into every rank's counters; the SpMM of
+// the rank's own output rows waits for every other rank's count and then
+// reads the gathered P locally.  Gathered P alternates between two buffers
+// by layer: a rank writes layer k's buffer only after its layer k - 1 SpMM
+// saw every rank's layer k - 1 counts, so every rank has finished the SpMM
+// of layer k - 2 (the last reader of that buffer).  The decision depends
+// only on quantities every rank shares (sizes, the collective peer set-ups),
+// so all ranks take the same path; otherwise the NCCL all-gather below runs.
 // ----------------------------------------------------------------------------
 constexpr int kGnnCounter = 64;   // word of the peer slot array where rank r's tile count is kept (+ r)
 
@@ -495,13 +496,28 @@ static tl_status sparse_chain_fanned(tl_ctx* c, Tensor* S, Tensor* lhs, const fl
     gp.B = wp; gp.sbk = f; gp.sbn = 1;
     gp.C = gathered(c->rank) + (int64_t)c->rank * per * f; gp.scm = f; gp.scn = 1;
     gp.scale = 1.0f; gp.beta = 0; gp.relu_term = relu ? 1 : 0;
+    float* dst[kMaxPeers] = {};
+    unsigned long long* cnt[kMaxPeers] = {};
     for (int q = 0; q < world; ++q) {
         if (q == c->rank) continue;
-        gp.fan[q] = gathered(q) + (int64_t)c->rank * per * f;
-        gp.fan_cnt[q] = c->peer_slots[q] + kGnnCounter + c->rank;
+        dst[q] = gathered(q) + (int64_t)c->rank * per * f;
+        cnt[q] = c->peer_slots[q] + kGnnCounter + c->rank;
     }
-    gp.fan_n = world - 1;
+    // the epilogue fan-out (TL_GNN_FAN=epilogue) stores each tile to the
+    // peers from the GEMM itself; the default runs the GEMM as usual and then
+    // a push kernel whose blocks all store to the peers (faster at these
+    // sizes: the GEMM keeps split K and every SM issues peer stores)
+    const char* how = getenv("TL_GNN_FAN");
+    const bool epilogue = how && !strcmp(how, "epilogue");
+    if (epilogue) {
+        for (int q = 0; q < world; ++q) {
+            gp.fan[q] = dst[q];
+            gp.fan_cnt[q] = cnt[q];
+        }
+        gp.fan_n = world - 1;
+    }
     TL_TRY(launch_gemm(c, gp));
+    if (!epilogue) TL_TRY(launch_fan_push(c, gp.C, x_rows * f, dst, cnt));
     // every other rank's tiles of this layer, counted cumulatively
     SpWait w{};
     w.cnt = c->peer_slots[c->rank] + kGnnCounter;
@@ -509,7 +525,7 @@ static tl_status sparse_chain_fanned(tl_ctx* c, Tensor* S, Tensor* lhs, const fl
     for (int r = 0; r < world; ++r) {
         if (r == c->rank) continue;
         const int64_t r_rows = nu > r ? (nu - r + world - 1) / world : 0;
-        c->gnn_expect[r] += (unsigned long long)gemm_fan_tiles(r_rows, f);
+        c->gnn_expect[r] += (unsigned long long)(epilogue ? gemm_fan_tiles(r_rows, f) : fan_push_blocks());
         w.need[r] = c->gnn_expect[r];
     }
     TL_TRY(alloc_dense_public(c, lhs));

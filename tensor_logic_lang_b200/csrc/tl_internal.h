@@ -363,6 +363,12 @@ struct SpWait {
     unsigned long long need[kMaxPeers];
     unsigned long long timeout_ns;
 };
+// Copies len floats at src (this rank's block of a gathered tensor) to
+// dst[q] on every other rank q (peer memory; null for this rank), then adds
+// fan_push_blocks() to each cnt[q] (release at system scope)
+tl_status launch_fan_push(tl_ctx* c, const float* src, int64_t len, float* const* dst,
+                          unsigned long long* const* cnt);
+int64_t fan_push_blocks();
 // CSR SpMM out[v, j] (+)= sum_e val[e] * P[col[e], j]; P has p_rows rows
 tl_status launch_spmm(tl_ctx* c, int64_t rows, const int64_t* rowptr, const int32_t* colidx,
                       const float* vals, const float* P, int64_t p_rows, int64_t ldp, int64_t f, float* out,
