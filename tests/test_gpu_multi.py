@@ -61,8 +61,8 @@ def _closure_worker(rank, world, nid, n, kind, mode, q):
 def _gnn_worker(rank, world, nid, n, f, mode, q):
     if mode == "nccl":
         os.environ["TL_GNN_NCCL"] = "1"
-    if mode == "epilogue":
-        os.environ["TL_GNN_FAN"] = "epilogue"
+    if mode == "pushed":
+        os.environ["TL_GNN_FAN"] = "push"
     from tensor_logic_lang_b200.runtime import Context
     ctx = Context(device=rank, rank=rank, world_size=world, nccl_id=nid, comm_timeout_ms=60000)
     try:
@@ -121,16 +121,16 @@ def test_sharded_closure(oracle_lib, n, kind, mode):
             assert 2 <= got_sweeps.pop() <= sweeps
 
 
-GNN_CASES = [(4096, 128, "pushed"), (16384, 256, "pushed"), (4096, 128, "epilogue"), (4096, 128, "nccl"),
-             (3001, 64, "pushed")]
+GNN_CASES = [(4096, 128, "epilogue"), (16384, 256, "epilogue"), (4096, 128, "pushed"), (4096, 128, "nccl"),
+             (3001, 64, "epilogue")]
 
 
 @pytest.mark.skipif(_world() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("n,f,mode", GNN_CASES, ids=[f"n{c[0]}-f{c[1]}-{c[2]}" for c in GNN_CASES])
 def test_sharded_gnn(oracle_lib, n, f, mode):
-    # pushed: after each rank's GEMM, a kernel stores its block of P into
-    # every rank's gathered copy over NVLink and counts its blocks there;
-    # epilogue: the GEMM's epilogue does those stores; nccl: the all-gather
+    # epilogue: each rank's GEMM epilogue stores its block of P into every
+    # rank's gathered copy over NVLink and counts its tiles there; pushed: a
+    # kernel after the GEMM does those stores; nccl: the all-gather
     # runs as an NCCL collective (n = 3001, f = 64 has shares too small for
     # the tensor-core GEMM, so it takes the NCCL path in every mode)
     world = _world()
