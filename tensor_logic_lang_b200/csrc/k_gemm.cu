@@ -753,6 +753,19 @@ __device__ __forceinline__ float seg_op(int op, float x) {
     }
 }
 
+// One operand's row-wise copy (k_prep_rows below): its grid is gx x gy blocks.
+struct PrepRows {
+    const float* S;
+    int64_t src_rs, rows, len;
+    int nseg;
+    unsigned ops;
+    float sgn;
+    float* D;
+    int64_t dst_rs, dst_ss;
+    int vec, tpr_log2;
+    unsigned gx, gy;
+};
+
 // Row-wise segment copy: for each source row i (stride src_rs, len elements,
 // contiguous) and segment s, dst[i * dst_rs + s * dst_ss + j] = op_s(x[j]).
 // Serves both orientations: K-major copies of K-contiguous sources (rows = R)
@@ -761,18 +774,27 @@ __device__ __forceinline__ float seg_op(int op, float x) {
 // to the row, so short rows do not leave most threads idle); a 2-D grid (row
 // chunks x row groups) needs no index division; 128-bit loads and stores when
 // every stride and base is 16-byte aligned.
-__global__ void __launch_bounds__(256) k_prep_rows(const float* __restrict__ S, int64_t src_rs, int64_t rows,
-                                                   int64_t len, int nseg, unsigned ops, float sgn,
-                                                   float* __restrict__ D, int64_t dst_rs, int64_t dst_ss, int vec,
-                                                   int tpr_log2) {
+// Both operands of a GEMM go in one launch: blockIdx.z picks the operand,
+// and blocks past that operand's own gx x gy grid return.
+__global__ void __launch_bounds__(256) k_prep_rows(const __grid_constant__ PrepRows pr0,
+                                                   const __grid_constant__ PrepRows pr1) {
+    const PrepRows& a = blockIdx.z ? pr1 : pr0;
+    if (blockIdx.x >= a.gx || blockIdx.y >= a.gy) return;
+    const float* __restrict__ S = a.S;
+    float* __restrict__ D = a.D;
+    const int64_t src_rs = a.src_rs, rows = a.rows, len = a.len, dst_rs = a.dst_rs, dst_ss = a.dst_ss;
+    const int nseg = a.nseg;
+    const unsigned ops = a.ops;
+    const float sgn = a.sgn;
+    const int tpr_log2 = a.tpr_log2;
     const int tpr = 1 << tpr_log2, rpb = 256 >> tpr_log2;
     const int t = threadIdx.x & (tpr - 1);
-    const int64_t row_step = (int64_t)gridDim.y * rpb;
-    if (vec) {
+    const int64_t row_step = (int64_t)a.gy * rpb;
+    if (a.vec) {
         // up to four rows per thread (as the grid leaves them), their loads
         // issued before any store
         for (int64_t i0 = (int64_t)blockIdx.y * rpb + (threadIdx.x >> tpr_log2); i0 < rows; i0 += 4 * row_step) {
-            for (int64_t j = ((int64_t)blockIdx.x * tpr + t) * 4; j < len; j += (int64_t)gridDim.x * tpr * 4) {
+            for (int64_t j = ((int64_t)blockIdx.x * tpr + t) * 4; j < len; j += (int64_t)a.gx * tpr * 4) {
                 float4 x[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
@@ -786,9 +808,9 @@ __global__ void __launch_bounds__(256) k_prep_rows(const float* __restrict__ S, 
                     float4 y = x[u];
                     y.x *= sgn; y.y *= sgn; y.z *= sgn; y.w *= sgn;
                     float* dst = D + i * dst_rs;
-                    for (int s = 0; s < nseg; ++s) {
-                        const int op = (ops >> (4 * s)) & 15;
-                        *reinterpret_cast<float4*>(dst + s * dst_ss + j) =
+                    for (int sg = 0; sg < nseg; ++sg) {
+                        const int op = (ops >> (4 * sg)) & 15;
+                        *reinterpret_cast<float4*>(dst + sg * dst_ss + j) =
                             make_float4(seg_op(op, y.x), seg_op(op, y.y), seg_op(op, y.z), seg_op(op, y.w));
                     }
                 }
@@ -799,11 +821,9 @@ __global__ void __launch_bounds__(256) k_prep_rows(const float* __restrict__ S, 
     for (int64_t i = (int64_t)blockIdx.y * rpb + (threadIdx.x >> tpr_log2); i < rows; i += row_step) {
         const float* src = S + i * src_rs;
         float* dst = D + i * dst_rs;
-        {
-            for (int64_t j = (int64_t)blockIdx.x * tpr + t; j < len; j += (int64_t)gridDim.x * tpr) {
-                const float x = src[j] * sgn;
-                for (int s = 0; s < nseg; ++s) dst[s * dst_ss + j] = seg_op((ops >> (4 * s)) & 15, x);
-            }
+        for (int64_t j = (int64_t)blockIdx.x * tpr + t; j < len; j += (int64_t)a.gx * tpr) {
+            const float x = src[j] * sgn;
+            for (int sg = 0; sg < nseg; ++sg) dst[sg * dst_ss + j] = seg_op((ops >> (4 * sg)) & 15, x);
         }
     }
 }
@@ -1431,11 +1451,15 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     void* ws = nullptr;
     TL_TRY(workspace(c, need, &ws, WS_GEMM));
     uint8_t* wp = (uint8_t*)ws;
+    // the row-wise copies of both operands go in one launch; a source with
+    // neither K nor MN contiguous is copied through shared-memory tiles
+    PrepRows rw[2] = {};
+    int n_rows = 0;
+    double rows_bytes = 0;
     for (Prep* q : {&pa, &pb}) {
         q->dst = (float*)wp;
         wp += (((size_t)(q->mn ? Ke : q->R) * q->ld * 4) + 255) & ~size_t(255);
         const float* src = q == &pa ? p.A : p.B;
-        LaunchScope L(c, q->name, (double)q->R * p.K * 4.0 * (1 + nseg));
         if (q->mn || q->s_k == 1) {
             // rows of the contiguous dim: R rows of K (K-major) or K rows of R (MN-major)
             const int64_t rows = q->mn ? p.K : q->R, len = q->mn ? q->R : p.K;
@@ -1453,14 +1477,24 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
             const int64_t gx = std::min<int64_t>((per_row + 255) / 256, 64);
             int64_t row_groups = (rows + rpb - 1) / rpb;
             if (vec && gx * row_groups >= 4 * (int64_t)c->sm_count) row_groups = (rows + 4 * rpb - 1) / (4 * rpb);
-            dim3 g((unsigned)gx, (unsigned)std::min<int64_t>(row_groups, 65535));
-            k_prep_rows<<<g, 256, 0, c->stream>>>(src, src_rs, rows, len, nseg, q->ops, q->sgn, q->dst, q->ld, dst_ss,
-                                                  vec ? 1 : 0, tl);
+            PrepRows& r = rw[n_rows++];
+            r.S = src; r.src_rs = src_rs; r.rows = rows; r.len = len; r.nseg = nseg; r.ops = q->ops; r.sgn = q->sgn;
+            r.D = q->dst; r.dst_rs = q->ld; r.dst_ss = dst_ss; r.vec = vec ? 1 : 0; r.tpr_log2 = tl;
+            r.gx = (unsigned)gx;
+            r.gy = (unsigned)std::min<int64_t>(row_groups, 65535);
+            rows_bytes += (double)q->R * p.K * 4.0 * (1 + nseg);
         } else {
+            LaunchScope L(c, q->name, (double)q->R * p.K * 4.0 * (1 + nseg));
             dim3 g((unsigned)((q->R + 31) / 32), (unsigned)((p.K + 31) / 32));
             k_prep_transpose<<<g, dim3(32, 8), 0, c->stream>>>(src, q->s_r, q->s_k, q->R, p.K, nseg, q->ops, q->sgn,
                                                               q->dst, q->ld);
+            TL_TRY(L.done());
         }
+    }
+    if (n_rows) {
+        LaunchScope L(c, "gemm_prep", rows_bytes);
+        dim3 g(std::max(rw[0].gx, rw[1].gx), std::max(rw[0].gy, rw[1].gy), (unsigned)n_rows);
+        k_prep_rows<<<g, 256, 0, c->stream>>>(rw[0], rw[1]);
         TL_TRY(L.done());
     }
     // the maps span Ke; TMA reads zeros past it (the K tail of the last block)
