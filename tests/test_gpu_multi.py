@@ -201,3 +201,36 @@ def test_skipped_rank_ends_the_wait_with_comm_error(mode):
         assert p.exitcode == 0
     assert out[0][1] == out[1][1] == 2                  # the first run converged on both ranks
     assert out[0][2] == abi.TL_ERR_COMM and out[1][2] == abi.TL_OK
+
+
+def _grow_worker(rank, world, nid, sizes, q):
+    # the peer-row buffer is sized for the first relation, then grown (every
+    # rank unmaps its peers' buffers, a barrier, then a new mapping)
+    os.environ["TL_CLOSURE_SHARDED"] = "peer"
+    from tensor_logic_lang_b200 import lang
+    from tensor_logic_lang_b200.runtime import Context
+    ctx = Context(device=rank, rank=rank, world_size=world, nccl_id=nid, comm_timeout_ms=60000)
+    try:
+        ctx.set_sharding("Reach", abi.SHARD_ROWS)
+        out = []
+        for n in sizes:
+            rows, cols = _graph(n, "dag")
+            ctx.run(lang.Program(_closure_src(n), sparse_inputs={"Edge": (rows, cols, None)}))
+            out.append((ctx.bits("Reach", rows=shard.local_count(n, rank, world)), ctx.sweeps))
+        q.put((rank, "grow", out))
+    finally:
+        ctx.close()
+
+
+@pytest.mark.skipif(_world() < 2, reason="needs two GPUs")
+def test_sharded_closure_peer_buffer_grows(oracle_lib):
+    world, sizes = _world(), (2048, 8192)
+    out = _run(_grow_worker, world, sizes)
+    for k, n in enumerate(sizes):
+        rows, cols = _graph(n, "dag")
+        colptr, rowidx = gen.csr_from_coo(n, cols, rows)
+        R = np.zeros((n, (n + 31) // 32), dtype=np.uint32)
+        np.bitwise_or.at(R, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
+        sweeps = oracle_lib.closure_right(n, colptr, rowidx, R)
+        np.testing.assert_array_equal(shard.assemble([o[2][k][0] for o in out], n), R)
+        assert all(o[2][k][1] == sweeps for o in out)
