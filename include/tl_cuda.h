@@ -378,14 +378,14 @@ void* tl_stream(const tl_ctx* ctx);
 /*             whose copy of the scratch array the call uses                 */
 /*   sweeps_out  receives the sweep count (may be NULL)                      */
 /* The call is synchronous: after every sweep it copies the changed word to  */
-/* the host and waits for the stream, so it returns with d_reach final, and  */
-/* it must not be called while the stream is capturing.  It returns TL_OK    */
-/* when a sweep changed nothing or when the cap was reached (then            */
-/* *sweeps_out == max_sweeps and the relation may not be closed, as the      */
-/* reference stops silently at its cap).  The first call on a device looks   */
-/* up the scratch array's device address (cudaGetSymbolAddress).  Every call */
-/* shares the one array, so calls that overlap on the GPU (other streams,    */
-/* other host threads) race; serialise them.                                 */
+/* the host and waits for the stream, so it returns with d_reach final.  It   */
+/* returns TL_OK when a sweep changed nothing or when the cap was reached     */
+/* (then *sweeps_out == max_sweeps and the relation may not be closed, as    */
+/* the reference stops silently at its cap).  The first call on a device     */
+/* looks up the scratch array's device address (cudaGetSymbolAddress); make  */
+/* that first call before any stream capture.  Every call shares the one     */
+/* array, so calls that overlap on the GPU (other streams, other host        */
+/* threads) race; serialise them.                                            */
 /* ------------------------------------------------------------------------ */
 #define TL_NOALLOC_MAX_ROWS 65536
 tl_status tl_closure_noalloc(int64_t n, const int64_t* d_rowptr, const int32_t* d_colidx,

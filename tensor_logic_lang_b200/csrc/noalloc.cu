@@ -9,7 +9,6 @@
 //
 // The call is synchronous: after every sweep it copies the changed word to
 // the host and waits for the stream, so it returns with the result final.
-// For the same reason it must not be called on a stream that is capturing.
 // `stream` must belong to the current device (checked): the scratch address
 // is the current device's.
 //
@@ -19,7 +18,8 @@
 // Every GPU that loads the library holds the array until the process exits.
 // Host code cannot use the array's name as a device address; its address is
 // looked up once per device with cudaGetSymbolAddress, with that device
-// current, on the first call there.
+// current, on the first call there; that first call should come before any
+// stream capture.
 #include <mutex>
 
 #include "tl_internal.h"
