@@ -349,6 +349,18 @@ def run_closure(args, dist, peaks):
     return res
 
 
+def closure_parallelism(world):
+    """The bench line's description of how the closure's rows are split."""
+    if world == 1:
+        return "1 GPU"
+    scheme = os.environ.get("TL_CLOSURE_SHARDED", "replicate")
+    how = {"replicate": "every GPU closes every row in the first sweep and keeps its own",
+           "peer": "every GPU closes its own rows, reading other GPUs' closed rows over NVLink",
+           "local": "every GPU closes its own rows with shortcuts through its own rows only",
+           "bfs": "every GPU closes its own rows by breadth-first search"}.get(scheme, scheme)
+    return f"rows cyclic over {world} GPUs; {how}"
+
+
 def row_digests(bits):
     import hashlib
     return [hashlib.blake2b(r.tobytes(), digest_size=8).digest() for r in bits]
@@ -666,7 +678,7 @@ def main():
             "data": "synthetic (seeded random DAG, 4n distinct edges u<v)",
             "config": {"workload": f"transitive-closure fixpoint n={N_CLOSURE}, mean out-degree {DEG_CLOSURE}",
                        "n": N_CLOSURE, "edges": res["nnz"], "sweeps_per_step": res["sweeps"],
-                       "reach_pairs": res["reach_pairs"], "parallelism": f"rows cyclic over {world} GPU(s)",
+                       "reach_pairs": res["reach_pairs"], "parallelism": closure_parallelism(world),
                        "l2": "256 MiB buffer written between timed steps"},
             "gpu_launches": int(res["launches"]), "roofline": res["roofline"], "cpu_baseline": cpu,
             "e2e": res["e2e"], "clocks": res["clocks"],
