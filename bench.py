@@ -273,8 +273,11 @@ def run_closure(args, dist, peaks):
     from tensor_logic_lang_b200.runtime import Context, unique_id
     nid = dist.bcast_bytes(unique_id() if dist.rank == 0 else None) if dist.world > 1 else None
     ctx = Context(device=dist.local, rank=dist.rank, world_size=dist.world, nccl_id=nid)
+    # columns split (TL_CLOSURE_SHARDED=cols): every rank keeps all rows of its
+    # slice of the columns; otherwise rows cyclic over the ranks
+    col_split = dist.world > 1 and os.environ.get("TL_CLOSURE_SHARDED") == "cols"
     if dist.world > 1:
-        ctx.set_sharding("Reach", abi.SHARD_ROWS)
+        ctx.set_sharding("Reach", abi.SHARD_COLS if col_split else abi.SHARD_ROWS)
     full, resident, rows, cols = closure_program(dist, resident=True)
     ctx.run(full)                                # uploads Edge (CSR) once
     sweeps = ctx.sweeps
@@ -300,9 +303,10 @@ def run_closure(args, dist, peaks):
     # CSR (int64 row pointers, int32 columns).  The per-sweep fallback kernel
     # counts the same bytes per sweep.
     n = N_CLOSURE
-    local_rows = (n - dist.rank + dist.world - 1) // dist.world
+    local_rows = n if col_split else (n - dist.rank + dist.world - 1) // dist.world
+    local_words = n // 32 // dist.world if col_split else n // 32
     nnz = len(rows)
-    algo_bytes = 2.0 * local_rows * (n // 8) + n * 32.0 + (n + 1) * 8.0 + nnz * 4.0
+    algo_bytes = 2.0 * local_rows * local_words * 4 + n * 32.0 + (n + 1) * 8.0 + nnz * 4.0
     kname = "closure_fixpoint" if "closure_fixpoint" in prof else "closure_sweep"
     st = prof.get(kname, {"launches": 0, "total_ms": float("nan")})
     per_launch_ms = st["total_ms"] / max(1, st["launches"])
@@ -326,14 +330,14 @@ def run_closure(args, dist, peaks):
     # end to end: host COO -> CSR -> device, the fixpoint, full Reach bits back to the host
     e2e_total = 0.0
     h2d = rows.nbytes + cols.nbytes
-    d2h = local_rows * (n // 8)
+    d2h = local_rows * local_words * 4
     # pinned host buffer for the result (the step's device-to-host read)
-    out_bits = torch.empty((local_rows, n // 32), dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
+    out_bits = torch.empty((local_rows, local_words), dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
     for i in range(args.warmup + args.steps):
         dist.barrier()
         t0 = time.perf_counter()
         ctx.run(full)
-        ctx.bits("Reach", rows=local_rows, out=out_bits)
+        ctx.bits("Reach", rows=local_rows, out=out_bits, words=local_words)
         ctx.sync()
         t1 = time.perf_counter()
         if i >= args.warmup:
@@ -343,7 +347,7 @@ def run_closure(args, dist, peaks):
            "d2h_bytes_per_step": int(d2h)}
     reach_pairs = dist.sum(int(np.unpackbits(out_bits.view(np.uint8)).sum()))
     ctx.close()
-    parity = closure_parity(dist, out_bits, sweeps, rows, cols)
+    parity = closure_parity(dist, out_bits, sweeps, rows, cols, col_split)
     res = dict(value=value, ms=ms_max, sweeps=sweeps, launches=launches, roofline=roof, clocks=clk, e2e=e2e,
                reach_pairs=int(reach_pairs), nnz=nnz, kernels=prof, parity=parity)
     return res
@@ -358,6 +362,9 @@ def closure_parallelism(world):
            "peer": "every GPU closes its own rows, reading other GPUs' closed rows over NVLink",
            "local": "every GPU closes its own rows with shortcuts through its own rows only",
            "bfs": "every GPU closes its own rows by breadth-first search"}.get(scheme, scheme)
+    if scheme == "cols":
+        return (f"columns in {world} slices, one per GPU; every GPU closes every row of its slice, "
+                "with no exchange")
     return f"rows cyclic over {world} GPUs; {how}"
 
 
@@ -366,12 +373,13 @@ def row_digests(bits):
     return [hashlib.blake2b(r.tobytes(), digest_size=8).digest() for r in bits]
 
 
-def closure_parity(dist, out_bits, sweeps, rows, cols):
+def closure_parity(dist, out_bits, sweeps, rows, cols, col_split=False):
     """Bit-exact check of the relation every rank computed (its cyclic share
-    of the rows, from the last end-to-end step) against the f64 oracle's
-    closure: rank 0 gathers one 8-byte digest per row and compares it with
-    the digest of the oracle's row, and the sweep counts.  The oracle is the
-    checker here, run after the timed and end-to-end regions."""
+    of the rows, or its slice of the columns of every row, from the last
+    end-to-end step) against the f64 oracle's closure: rank 0 gathers one
+    8-byte digest per row and compares it with the digest of the oracle's
+    row (or row slice), and the sweep counts.  The oracle is the checker
+    here, run after the timed and end-to-end regions."""
     from tensor_logic_lang_b200 import inputs as gen
     digests = dist.gather((row_digests(out_bits), sweeps))
     if dist.rank != 0:
@@ -385,10 +393,18 @@ def closure_parity(dist, out_bits, sweeps, rows, cols):
     t1 = time.perf_counter()
     osw = oracle.closure_right(n, colptr, rowidx, R, threads=os.cpu_count() or 1)
     t_closure = time.perf_counter() - t1
-    want = row_digests(R)
     world = len(digests)
-    bad = sum(1 for r, (dg, _) in enumerate(digests) for k, d in enumerate(dg) if d != want[k * world + r])
-    checked = sum(len(dg) for dg, _ in digests)
+    if col_split:
+        w = n // 32 // world
+        bad = 0
+        for r, (dg, _) in enumerate(digests):
+            want = row_digests(np.ascontiguousarray(R[:, r * w:(r + 1) * w]))
+            bad += sum(1 for k, d in enumerate(dg) if d != want[k])
+        checked = min(len(dg) for dg, _ in digests)
+    else:
+        want = row_digests(R)
+        bad = sum(1 for r, (dg, _) in enumerate(digests) for k, d in enumerate(dg) if d != want[k * world + r])
+        checked = sum(len(dg) for dg, _ in digests)
     sw_ok = all(sw == osw for _, sw in digests)
     return {"closure": "bit-exact" if bad == 0 and checked == n and sw_ok else "MISMATCH",
             "rows_checked": checked, "rows_differing": bad, "sweeps": [sw for _, sw in digests],

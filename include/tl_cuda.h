@@ -320,9 +320,16 @@ tl_status tl_program_output(tl_ctx* ctx, char* buf, int64_t buf_len, int64_t* ne
 /* Row sharding (closure and GNN message passing across the GPUs of a box). */
 /* A sharded rank-2 tensor keeps rows r with r % world_size == rank on this  */
 /* rank (cyclic rows balance the skewed reach sets of a DAG).               */
+/* Column sharding (TL_SHARD_COLS, a closure relation only): this rank keeps */
+/* columns [rank * c / world_size, (rank + 1) * c / world_size) of every     */
+/* row of an r x c relation (c a multiple of 128 * world_size), as bit rows; */
+/* the relation must start as step(Edge) right before its fixpoint, and it   */
+/* is downloaded with tl_tensor_download_bits.  No extension of the          */
+/* reference: its fixpoint (fixpoint.zig:46-98) has no distribution at all.  */
 /* ------------------------------------------------------------------------ */
 #define TL_SHARD_NONE 0
 #define TL_SHARD_ROWS 1
+#define TL_SHARD_COLS 2
 tl_status tl_set_sharding(tl_ctx* ctx, const char* name, int32_t mode);
 
 /* ------------------------------------------------------------------------ */

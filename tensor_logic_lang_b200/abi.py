@@ -55,6 +55,7 @@ PREC_TF32 = 0
 PREC_FP32 = 1
 SHARD_NONE = 0
 SHARD_ROWS = 1
+SHARD_COLS = 2
 
 
 class Index(C.Structure):

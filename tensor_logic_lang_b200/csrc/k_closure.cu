@@ -108,6 +108,15 @@ struct FixArgs {
     // over NVLink)
     int peer_dp;
     int64_t n_glob;                          // nodes of the relation (rows over all ranks)
+    // stored rows: rw words per row at word rw0 of the full-width row the
+    // warp builds in shared memory (rw = words, rw0 = 0 unless the columns
+    // are sharded: then this rank keeps columns [32 rw0, 32 (rw0 + rw)) of
+    // every row, and closed rows are read, ORed and published as such slices)
+    int64_t rw, rw0;
+    // columns sharded: whether the first sweep changes a row anywhere in the
+    // relation (some node two steps from a row's node is not one step from
+    // it), computed from the graph, so every rank sets the same changed word
+    const int* two_hop;
     unsigned long long* pclosed[kMaxPeers];
     uint32_t* prows[kMaxPeers];
     int shortcut;              // lazy rows OR closed rows in (and run in descending order)
@@ -200,7 +209,7 @@ __device__ __forceinline__ unsigned long long dp_closed_load(const FixArgs& a, i
 // The row of handle h (this rank's, or another rank's through peer memory).
 template <bool PEER>
 __device__ __forceinline__ const uint32_t* dp_row(const FixArgs& a, int32_t h) {
-    if (!PEER) return a.dpR + (int64_t)h * a.words;
+    if (!PEER) return a.dpR + (int64_t)h * a.rw;
     const uint32_t o = (uint32_t)h % (uint32_t)a.world, l = (uint32_t)h / (uint32_t)a.world;
     return a.prows[o] + (int64_t)l * a.words;
 }
@@ -276,16 +285,81 @@ __device__ __forceinline__ int harvest(uint32_t* spill, int64_t words, int64_t& 
     return stored;
 }
 
+// Columns sharded: row slice (at word rw0 of the shared row) |= the slices
+// of the closed rows held by the lanes in m (local row ly, nonzero words
+// [lo, hi) of the slice).  Each lane takes 16-byte group lane of every
+// 128-word piece; KPR pieces per row, so 8 / KPR source rows' loads are in
+// flight per round, with every index known at compile time.
+template <bool PEER, int KPR>
+__device__ __forceinline__ void or_slices(const FixArgs& a, unsigned m, int32_t ly, int lo, int hi, uint32_t* row,
+                                          int lane) {
+    constexpr int RPR = 8 / KPR;
+    const int rw = (int)a.rw;
+    uint32_t* dst = row + a.rw0;
+    while (m) {
+        int32_t sl[RPR];
+        int sa[RPR], sb[RPR];
+#pragma unroll
+        for (int j = 0; j < RPR; ++j) {
+            sl[j] = -1;
+            sa[j] = 0;
+            sb[j] = 0;
+            if (m) {
+                const int src = __ffs(m) - 1;
+                m &= m - 1;
+                sl[j] = __shfl_sync(0xffffffffu, ly, src);
+                sa[j] = max(__shfl_sync(0xffffffffu, lo, src), 0);
+                sb[j] = min(__shfl_sync(0xffffffffu, hi, src), rw);
+            }
+        }
+        uint4 v[RPR][KPR];
+#pragma unroll
+        for (int j = 0; j < RPR; ++j)
+#pragma unroll
+            for (int i = 0; i < KPR; ++i) {
+                const int w = i * 128 + lane * 4;
+                v[j][i] = (sl[j] >= 0 && w < rw && w + 4 > sa[j] && w < sb[j])
+                              ? __ldcg(reinterpret_cast<const uint4*>(dp_row<PEER>(a, sl[j])) + (w >> 2))
+                              : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+        for (int i = 0; i < KPR; ++i) {
+            uint4 o = v[0][i];
+#pragma unroll
+            for (int j = 1; j < RPR; ++j) {
+                o.x |= v[j][i].x; o.y |= v[j][i].y; o.z |= v[j][i].z; o.w |= v[j][i].w;
+            }
+            const int w = i * 128 + lane * 4;
+            if (w < rw && (o.x | o.y | o.z | o.w)) {
+                uint4 t = *reinterpret_cast<uint4*>(dst + w);
+                t.x |= o.x; t.y |= o.y; t.z |= o.z; t.w |= o.w;
+                *reinterpret_cast<uint4*>(dst + w) = t;
+            }
+        }
+        __syncwarp();
+    }
+}
+
 // row |= the closed rows held by the lanes (at most one per lane: local row
 // ly, nonzero words [lo, hi)).  Each lane ORs its own words (16-byte groups
 // lane, lane + 32, ... of every 1024-word chunk) of the source rows into the
 // shared row, two source rows' loads in flight at a time: no index search and
 // no shared-memory atomics.
-template <bool PEER>
+template <bool PEER, bool COLS = false>
 __device__ __forceinline__ void or_closed_rows(const FixArgs& a, bool has, int32_t ly, int lo, int hi,
                                                uint32_t* row, bool vec, int lane) {
-    const int words = (int)a.words;
     unsigned m = __ballot_sync(0xffffffffu, has);
+    if (COLS) {
+        // a slice of rw <= 1024 words: KPR 128-word pieces per row (kpr rounded
+        // up to a power of two), 8 / KPR rows' loads in flight per round
+        const int kpr = ((int)a.rw + 127) >> 7;
+        if (kpr == 1) or_slices<PEER, 1>(a, m, ly, lo, hi, row, lane);
+        else if (kpr == 2) or_slices<PEER, 2>(a, m, ly, lo, hi, row, lane);
+        else if (kpr <= 4) or_slices<PEER, 4>(a, m, ly, lo, hi, row, lane);
+        else or_slices<PEER, 8>(a, m, ly, lo, hi, row, lane);
+        return;
+    }
+    const int words = (int)a.words;
     if (!vec) {
         while (m) {
             const int src = __ffs(m) - 1;
@@ -361,7 +435,7 @@ struct RowSearch {
 // node whose local row is closed (lazy sweep) is ORed in, not expanded.
 // budget > 0: returns false once more than that many bits were expanded (the
 // row goes to a team); true when the row is closed.
-template <int ITEMS, bool PEER, bool COUNT = false>
+template <int ITEMS, bool PEER, bool COUNT = false, bool COLS = false>
 __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool own_first, bool dp, int budget,
                                            uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
@@ -500,7 +574,7 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
             for (int k = 0; k < ITEMS; ++k) {
                 const bool has = L[k] >= 0;
                 if (__any_sync(0xffffffffu, has))
-                    or_closed_rows<PEER>(a, has, L[k], (int)(CW[k] & ((1u << kClosedSpan) - 1u)),
+                    or_closed_rows<PEER, COLS>(a, has, L[k], (int)(CW[k] & ((1u << kClosedSpan) - 1u)),
                                    (int)((CW[k] >> kClosedSpan) & ((1u << kClosedSpan) - 1u)), row, vec, lane);
             }
             __syncwarp();
@@ -630,7 +704,7 @@ __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long*
 // that successor is then expanded instead, with the same result.  A row grew
 // if it ends with more bits than succ(x) has.  Once written, the row publishes
 // its closed word (release at GPU scope) and its pending word.
-template <bool PEER, bool COUNT>
+template <bool PEER, bool COUNT, bool COLS>
 __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long long* next_row, int budget,
                                               uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
     const int64_t words = a.words;
@@ -718,7 +792,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         nb = __shfl_sync(0xffffffffu, nb2, 0);
         t_next = slot_of(nb);
         __syncwarp();
-        or_closed_rows<PEER>(a, closed, l0, (int)(cw_now & ((1u << kClosedSpan) - 1u)),
+        or_closed_rows<PEER, COLS>(a, closed, l0, (int)(cw_now & ((1u << kClosedSpan) - 1u)),
                        (int)((cw_now >> kClosedSpan) & ((1u << kClosedSpan) - 1u)), row, vec, lane);
         __syncwarp();
         // its successors' closed words, in flight during the search and write-back
@@ -728,7 +802,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
             if (PEER && (uint32_t)l0 % (uint32_t)a.world != (uint32_t)a.rank) c_orr++;
             else c_orl++;
         }
-        const bool done = search_row<1, PEER, COUNT>(a, S, false, true, budget, row, spill, q, lane);
+        const bool done = search_row<1, PEER, COUNT, COLS>(a, S, false, true, budget, row, spill, q, lane);
         c_orl += S.n_or_local;
         c_orr += S.n_or_remote;
         c_exp += S.n_expanded;
@@ -744,7 +818,7 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         // write the row back (emptying the row space); its nonzero range and
         // popcount.  A copied row space also gives this rank's own rows to the
         // relation (its pending word marks the local row closed).
-        uint32_t* grow = a.dpR + r * words;
+        uint32_t* grow = a.dpR + r * a.rw;
         uint32_t* own = nullptr;
         int64_t lr = r;
         if (a.dp_copy) {
@@ -755,7 +829,23 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
             own = a.R + r * words;   // the published copy above, the relation here
         }
         int lo_w = INT32_MAX, hi_w = 0, pc = 0;
-        if (vec) {
+        if (COLS) {
+            // the slice goes out; the whole row space is emptied
+            const uint32_t* src = row + a.rw0;
+            for (int64_t w = lane * 4; w < a.rw; w += 128) {
+                const uint4 t = *reinterpret_cast<const uint4*>(src + w);
+                *reinterpret_cast<uint4*>(grow + w) = t;
+                const int c = __popc(t.x) + __popc(t.y) + __popc(t.z) + __popc(t.w);
+                if (c) {
+                    pc += c;
+                    lo_w = min(lo_w, (int)w);
+                    hi_w = (int)w + 4;
+                }
+            }
+            __syncwarp();
+            for (int64_t w = lane * 4; w < a.wpad; w += 128)
+                *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
+        } else if (vec) {
             for (int64_t w = lane * 4; w < words; w += 128) {
                 const uint4 t = *reinterpret_cast<const uint4*>(row + w);
                 *reinterpret_cast<uint4*>(row + w) = make_uint4(0u, 0u, 0u, 0u);
@@ -784,7 +874,9 @@ __device__ __forceinline__ bool close_rows_dp(const FixArgs& a, unsigned long lo
         lo_w = __reduce_min_sync(0xffffffffu, lo_w);
         hi_w = __reduce_max_sync(0xffffffffu, hi_w);
         pc = __reduce_add_sync(0xffffffffu, pc);
-        any = any || pc > n_init;
+        // with the columns sharded a row's growth may lie in another rank's
+        // slice: the changed word comes from the graph (two_hop) instead
+        if (!COLS) any = any || pc > n_init;
         pub_r = r;
         pub_p = lr;
         pub_w = lo_w < hi_w ? closed_word(a.epoch, lo_w, hi_w) : closed_word(a.epoch, 0, 0);
@@ -1040,7 +1132,7 @@ __device__ bool grid_barrier(const FixArgs& a, unsigned gen, int s, bool settle)
 }
 
 // COUNT: the lazy sweep counts its work (profiling runs that ask for it)
-template <bool PEER, bool COUNT>
+template <bool PEER, bool COUNT, bool COLS>
 __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs a) {
     extern __shared__ __align__(16) uint32_t smem_fix[];
     __shared__ int s_idx;
@@ -1061,11 +1153,14 @@ __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs
         __syncwarp();
         const int budget = a.team > 1 ? a.team_budget : 0;
         const bool grew = lazy && a.shortcut
-                              ? close_rows_dp<PEER, COUNT>(a, &a.st->next_row[s & 1], a.dp_copy || PEER ? 0 : budget, row,
+                              ? close_rows_dp<PEER, COUNT, COLS>(a, &a.st->next_row[s & 1],
+                                                                 a.dp_copy || PEER || COLS ? 0 : budget, row,
                                               spill, q, lane)
                               : close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, lazy, budget, row, spill, q,
                                            lane);
         if (lane == 0 && grew) *(volatile int*)&a.st->changed[s & 1] = 1;
+        if (COLS && lazy && blockIdx.x == 0 && threadIdx.x == 0 && *(volatile const int*)a.two_hop)
+            *(volatile int*)&a.st->changed[s & 1] = 1;
         if (a.team > 1 && a.team_budget > 0) {
             if (!grid_barrier(a, ++gen, s, false)) return;
             // rows handed over in this sweep, one per block at a time
@@ -1108,6 +1203,41 @@ __global__ void k_build_succ(const int64_t* __restrict__ rowptr, const int32_t* 
     }
 }
 
+// every instantiation the host launches (one launch shape fits all of them)
+const void* const kFixVariants[] = {
+    (const void*)k_closure_fix<false, false, false>, (const void*)k_closure_fix<true, false, false>,
+    (const void*)k_closure_fix<false, true, false>,  (const void*)k_closure_fix<true, true, false>,
+    (const void*)k_closure_fix<false, false, true>,  (const void*)k_closure_fix<false, true, true>};
+
+// Sets *flag when some node z two steps from a node x (x -> y -> z) is not
+// one step from it: exactly when a first sweep from step(E) adds a bit to
+// some row (fixpoint.zig:256-273 on R = step(E)).  Column lists are sorted
+// within a row (both CSR builds sort them).
+__global__ void k_two_hop(const int64_t* __restrict__ rowptr, const int32_t* __restrict__ colidx, int64_t e_rows,
+                          int* flag) {
+    for (int64_t x = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; x < e_rows; x += (int64_t)gridDim.x * blockDim.x) {
+        if (*(volatile int*)flag) return;
+        const int64_t b = rowptr[x], e = rowptr[x + 1];
+        for (int64_t i = b; i < e; ++i) {
+            const int32_t y = colidx[i];
+            if (y < 0 || y >= e_rows) continue;
+            for (int64_t j = rowptr[y]; j < rowptr[y + 1]; ++j) {
+                const int32_t z = colidx[j];
+                int64_t lo = b, hi = e;   // is z one of x's successors?
+                while (lo < hi) {
+                    const int64_t mid = (lo + hi) >> 1;
+                    if (colidx[mid] < z) lo = mid + 1;
+                    else hi = mid;
+                }
+                if (lo >= e || colidx[lo] != z) {
+                    atomicExch(flag, 1);
+                    return;
+                }
+            }
+        }
+    }
+}
+
 size_t fix_smem_per_warp(int64_t words) {
     const int64_t wpad = (words + 3) & ~int64_t(3);
     return (size_t)(2 * wpad + 4 + kFixQueue) * 4;
@@ -1144,13 +1274,19 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // the previous launch's result first (its control block shares the pinned slot)
     TL_TRY(fix_resolve(c));
     constexpr size_t kSmemCap = 200 * 1024;
-    const int64_t words = R->bits_words, rows = R->bits_rows;
+    // columns sharded: this rank stores a slice of every row; the warps still
+    // build full-width rows in shared memory (words is the full width)
+    const bool cols = R->shard == TL_SHARD_COLS && R->col_world > 1;
+    const int64_t words = cols ? (R->dims[1] + 31) / 32 : R->bits_words, rows = R->bits_rows;
     const int64_t wpad = (words + 3) & ~int64_t(3);
     // one table entry per bit position of a row (padding bits included)
     const int64_t nodes = words * 32;
-    if (fix_smem_per_warp(words) > kSmemCap || wpad * 32 >= INT32_MAX || E->nnz >= INT32_MAX) return TL_OK;
-    if (getenv("TL_CLOSURE_PER_SWEEP")) return TL_OK;
-    if (c->world > 1) {
+    if (fix_smem_per_warp(words) > kSmemCap || wpad * 32 >= INT32_MAX || E->nnz >= INT32_MAX) {
+        if (cols) return fail(c, TL_ERR_UNSUPPORTED, "column-sharded closure: relation too wide");
+        return TL_OK;
+    }
+    if (getenv("TL_CLOSURE_PER_SWEEP") && !cols) return TL_OK;
+    if (c->world > 1 && !cols) {
         TL_TRY(comm_peer_setup(c));
         if (c->peer_state != 1) return TL_OK;
     }
@@ -1159,19 +1295,23 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
         c->fix_coop = coop ? 1 : 0;
     }
-    if (!c->fix_coop) return TL_OK;
+    if (!c->fix_coop) {
+        if (cols) return fail(c, TL_ERR_UNSUPPORTED, "column-sharded closure needs a cooperative launch");
+        return TL_OK;
+    }
     *handled = true;
 
     // successor table, rebuilt when the CSR or the row width changed
     const int32_t sentinel = (int32_t)(wpad * 32);
     if (E->succ_stamp != E->csr_stamp || E->succ_nodes != nodes || E->succ_sentinel != sentinel || !E->succ) {
-        if (nodes * 2 > E->succ_cap) {
+        // the table, then one int4 whose first word is the graph's two-step flag
+        if (nodes * 2 + 1 > E->succ_cap) {
             TL_CK(c, cudaStreamSynchronize(c->stream));
             cudaFree(E->succ);
             E->succ = nullptr;
             E->succ_cap = 0;
-            TL_CK(c, cudaMalloc(&E->succ, (size_t)std::max<int64_t>(nodes * 2, 2) * sizeof(int4)));
-            E->succ_cap = std::max<int64_t>(nodes * 2, 2);
+            TL_CK(c, cudaMalloc(&E->succ, (size_t)(nodes * 2 + 1) * sizeof(int4)));
+            E->succ_cap = nodes * 2 + 1;
         }
         LaunchScope L(c, "closure_successor_table", (double)nodes * 32.0 + (double)E->nnz * 4.0);
         const int64_t blocks = std::min<int64_t>((nodes + 255) / 256, (int64_t)c->sm_count * 8);
@@ -1181,6 +1321,19 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         E->succ_stamp = E->csr_stamp;
         E->succ_nodes = nodes;
         E->succ_sentinel = sentinel;
+        E->two_hop_stamp = 0;
+    }
+    if (cols && E->two_hop_stamp != E->csr_stamp) {
+        // the graph's two-step flag (columns sharded only: on a graph that is
+        // its own closure the search is quadratic in the degrees)
+        LaunchScope L(c, "closure_two_hop", (double)E->nnz * 8.0);
+        int* two_hop = reinterpret_cast<int*>(E->succ + nodes * 2);
+        TL_CK(c, cudaMemsetAsync(two_hop, 0, sizeof(int), c->stream));
+        const int64_t rb = std::min<int64_t>((E->csr_rows + 255) / 256, (int64_t)c->sm_count * 8);
+        k_two_hop<<<(unsigned)std::max<int64_t>(rb, 1), 256, 0, c->stream>>>(E->rowptr, E->colidx, E->csr_rows,
+                                                                            two_hop);
+        TL_TRY(L.done());
+        E->two_hop_stamp = E->csr_stamp;
     }
 
     // fixpoint-long state: pending word per row (0: expand everything), then
@@ -1200,6 +1353,10 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // rows that step(E) left unwritten start from E's successor lists; their
     // sweep ORs in closed rows (closed words of this launch's epoch)
     const bool lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp;
+    if (cols && !(lazy && words < (int64_t(1) << kClosedSpan) && R->bits_words % 4 == 0 && R->bits_words <= 1024))
+        return fail(c, TL_ERR_UNSUPPORTED,
+                    "column-sharded closure: the relation must start as step(Edge) right before the fixpoint, "
+                    "with slices of a multiple of 128 columns up to 32768");
     const bool sharded = R->shard == TL_SHARD_ROWS && c->world > 1;
     const ShardedSweep mode = sharded_sweep_mode();
     const bool shortcut = lazy && words < (int64_t(1) << kClosedSpan) && !(sharded && mode == SWEEP_BFS);
@@ -1262,8 +1419,7 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     const size_t per_warp = fix_smem_per_warp(words);
     const bool teams = getenv("TL_CLOSURE_TEAMS") != nullptr;
     if (c->fix_shape_words != words || c->fix_shape_teams != (int)teams) {
-        for (const void* fn : {(const void*)k_closure_fix<false, false>, (const void*)k_closure_fix<true, false>,
-                               (const void*)k_closure_fix<false, true>, (const void*)k_closure_fix<true, true>})
+        for (const void* fn : kFixVariants)
             TL_CK(c, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap));
         int wpb = 1, per_sm = 0;
         for (int w = kFixWarps; w >= 1; w >>= 1) {
@@ -1271,8 +1427,7 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
             int b = 0;
             // one shape for every variant (and every rank computes the same)
             b = INT32_MAX;
-            for (const void* fn : {(const void*)k_closure_fix<false, false>, (const void*)k_closure_fix<true, false>,
-                                   (const void*)k_closure_fix<false, true>, (const void*)k_closure_fix<true, true>}) {
+            for (const void* fn : kFixVariants) {
                 int bb = 0;
                 cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bb, fn, 32 * w, per_warp * w);
                 b = std::min(b, bb);
@@ -1315,7 +1470,10 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.closed = static_cast<unsigned long long*>(c->fix_closed);
     a.epoch = c->fix_epoch;
     a.peer_dp = peer_rows ? 1 : 0;
-    c->fix_mode = !sharded ? 0 : peer_rows ? 1 : replicate ? 2 : shortcut ? 3 : 4;
+    a.rw = cols ? R->bits_words : words;
+    a.rw0 = cols ? (int64_t)R->col_rank * R->bits_words : 0;
+    a.two_hop = reinterpret_cast<const int*>(E->succ + nodes * 2);
+    c->fix_mode = cols ? 5 : !sharded ? 0 : peer_rows ? 1 : replicate ? 2 : shortcut ? 3 : 4;
     a.n_glob = R->dims[0];
     if (peer_rows) {
         for (int j = 0; j < c->world; ++j) {
@@ -1350,20 +1508,24 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // runs its fixpoint without waiting for the others.  A relation whose
     // lazy sweep does not run (rows written before, or another scheme)
     // exchanges them.
-    a.exchange = c->world > 1 && !(replicate && lazy) ? 1 : 0;
+    a.exchange = c->world > 1 && !(replicate && lazy) && !cols ? 1 : 0;
     for (int j = 0; j < kMaxPeers; ++j) a.slots[j] = c->peer_slots[j];
     a.token_base = c->world > 1 ? static_cast<unsigned long long*>(c->peer_own) + 2 * kMaxPeers : nullptr;
     a.timeout_ns = (unsigned long long)std::max(c->opts.comm_timeout_ms, 1000) * 1000000ull;
 
-    const double sweep_bytes = (double)rows * words * 8.0 + (double)nodes * 32.0;
+    const double sweep_bytes = (double)rows * a.rw * 8.0 + (double)nodes * 32.0;
     {
         LaunchScope L(c, "closure_fixpoint", sweep_bytes);
         void* args[] = {&a};
         // the work counters only in profiling runs that ask for them
         // (TL_CLOSURE_COUNTS): they cost the sweep a few per cent
         const bool count = c->prof && getenv("TL_CLOSURE_COUNTS") != nullptr;
-        const void* fn = peer_rows ? (count ? (const void*)k_closure_fix<true, true> : (const void*)k_closure_fix<true, false>)
-                                   : (count ? (const void*)k_closure_fix<false, true> : (const void*)k_closure_fix<false, false>);
+        const void* fn = cols ? (count ? (const void*)k_closure_fix<false, true, true>
+                                       : (const void*)k_closure_fix<false, false, true>)
+                         : peer_rows ? (count ? (const void*)k_closure_fix<true, true, false>
+                                              : (const void*)k_closure_fix<true, false, false>)
+                                     : (count ? (const void*)k_closure_fix<false, true, false>
+                                              : (const void*)k_closure_fix<false, false, false>);
         c->fix_counted = count;
         TL_CK(c, cudaLaunchCooperativeKernel(fn, dim3((unsigned)grid), dim3(32 * wpb), args,
                                              per_warp * wpb, c->stream));
@@ -1433,7 +1595,7 @@ tl_status fix_resolve(tl_ctx* c) {
         count("orr", h.n_or_remote);   // closed rows of other ranks ORed in
         count("exp", h.n_expanded);    // nodes expanded
         count(c->fix_mode == 1 ? "peer" : c->fix_mode == 2 ? "repl" : c->fix_mode == 3 ? "local" :
-              c->fix_mode == 4 ? "bfs" : "1gpu", 1);   // the scheme
+              c->fix_mode == 4 ? "bfs" : c->fix_mode == 5 ? "cols" : "1gpu", 1);   // the scheme
     }
     c->last_sweeps = h.sweeps;
     c->fix_last_changed = h.last_changed != 0;

@@ -191,6 +191,14 @@ static tl_status alloc_bits(tl_ctx* c, Tensor* t) {
     if (t->rank != 2) return fail(c, TL_ERR_UNSUPPORTED, "%s: bit storage needs rank 2", t->name.c_str());
     int64_t words = (t->dims[1] + 31) / 32;
     int64_t rows = dense_rows(c, t);
+    if (t->shard == TL_SHARD_COLS) {
+        // this rank's slice of the columns of every row
+        if (t->dims[1] % (128 * (int64_t)t->col_world))
+            return fail(c, TL_ERR_UNSUPPORTED, "%s: column sharding needs a multiple of %d columns", t->name.c_str(),
+                        128 * t->col_world);
+        words = t->dims[1] / 32 / t->col_world;
+        rows = t->dims[0];
+    }
     if (t->bits && t->bits_words == words && t->bits_rows == rows) return TL_OK;
     cudaFree(t->bits);
     t->bits = nullptr;
@@ -201,6 +209,9 @@ static tl_status alloc_bits(tl_ctx* c, Tensor* t) {
 }
 
 tl_status ensure_dense(tl_ctx* c, Tensor* t) {
+    if (t->shard == TL_SHARD_COLS)
+        return fail(c, TL_ERR_UNSUPPORTED, "%s: a column-sharded relation is read only as bit rows",
+                    t->name.c_str());
     TL_TRY(alloc_dense(c, t));
     if (t->dense_valid) return TL_OK;
     if (t->zero) {
@@ -218,6 +229,10 @@ tl_status ensure_dense(tl_ctx* c, Tensor* t) {
 }
 
 tl_status ensure_bits(tl_ctx* c, Tensor* t) {
+    // a column-sharded relation is written only by its closure fixpoint
+    if (t->shard == TL_SHARD_COLS && !(t->bits_valid && !t->lazy_src))
+        return fail(c, TL_ERR_UNSUPPORTED, "%s: a column-sharded relation must start as step(Edge) right before "
+                    "its fixpoint", t->name.c_str());
     TL_TRY(alloc_bits(c, t));
     if (t->bits_valid && t->lazy_src) {
         Tensor* src = t->lazy_src;
@@ -739,10 +754,24 @@ extern "C" tl_status tl_program_output(tl_ctx* c, char* buf, int64_t len, int64_
 }
 
 extern "C" tl_status tl_set_sharding(tl_ctx* c, const char* name, int32_t mode) {
-    if (!c || !name || (mode != TL_SHARD_NONE && mode != TL_SHARD_ROWS)) return TL_ERR_INVALID;
+    if (!c || !name || (mode != TL_SHARD_NONE && mode != TL_SHARD_ROWS && mode != TL_SHARD_COLS)) return TL_ERR_INVALID;
     auto& slot = c->tensors[name];
     if (!slot) { slot.reset(new tl_tensor()); slot->name = name; slot->defined = false; slot->owner = c; }
-    if (slot->shard != mode) { free_storage(slot.get()); slot->shard = mode; slot->zero = true; }
+    int col_rank = c->rank, col_world = c->world;
+    // TL_SHARD_COLS_OF="r/n": slice r of n on a one-GPU context (tests check
+    // the slices one by one against the whole relation)
+    if (const char* of = getenv("TL_SHARD_COLS_OF")) {
+        if (mode == TL_SHARD_COLS && c->world == 1 && sscanf(of, "%d/%d", &col_rank, &col_world) == 2 &&
+            !(col_world >= 1 && col_rank >= 0 && col_rank < col_world))
+            return TL_ERR_INVALID;
+    }
+    if (slot->shard != mode || slot->col_rank != col_rank || slot->col_world != col_world) {
+        free_storage(slot.get());
+        slot->shard = mode;
+        slot->col_rank = mode == TL_SHARD_COLS ? col_rank : 0;
+        slot->col_world = mode == TL_SHARD_COLS ? col_world : 1;
+        slot->zero = true;
+    }
     return TL_OK;
 }
 

@@ -44,6 +44,7 @@ struct Tensor {
     bool boolean = false;   // every value is 0 or 1
     bool is_sparse = false; // declared `sparse`
     int shard = TL_SHARD_NONE;
+    int col_rank = 0, col_world = 1;   // TL_SHARD_COLS: this rank's slice of the columns
 
     // fp32 dense row-major (local rows only when sharded)
     float* dense = nullptr;
@@ -86,6 +87,7 @@ struct Tensor {
     uint64_t succ_stamp = 0;    // csr_stamp it was built from (0: none)
     int64_t succ_nodes = 0;     // node count and sentinel it was built for
     int32_t succ_sentinel = 0;
+    uint64_t two_hop_stamp = 0; // csr_stamp of the two-step flag after the table (0: none)
 
     int64_t local_rows(int rank_, int world) const {
         if (shard != TL_SHARD_ROWS || world <= 1 || this->rank < 1) return this->rank >= 1 ? dims[0] : 1;

@@ -114,16 +114,18 @@ class Context:
         self.check(self.lib.tl_tensor_download_f32(t, out.ctypes.data_as(C.POINTER(C.c_float))), f"download {name}")
         return out
 
-    def bits(self, name, rows=None, out=None):
+    def bits(self, name, rows=None, out=None, words=None):
         """Bit rows (uint32 words) of a 0/1 rank-2 tensor (into `out` when given,
-        e.g. a pinned host buffer)."""
+        e.g. a pinned host buffer).  A row-sharded tensor gives its `rows`
+        local rows; a column-sharded one its slice of `words` words per row."""
         t = self._lookup(name)
         r, cols = self.shape(name)
         if rows is not None:
             r = rows
+        w = (cols + 31) // 32 if words is None else words
         if out is None:
-            out = np.empty((r, (cols + 31) // 32), dtype=np.uint32)
-        assert out.dtype == np.uint32 and out.flags.c_contiguous and out.shape == (r, (cols + 31) // 32)
+            out = np.empty((r, w), dtype=np.uint32)
+        assert out.dtype == np.uint32 and out.flags.c_contiguous and out.shape == (r, w)
         self.check(self.lib.tl_tensor_download_bits(t, out.ctypes.data_as(C.POINTER(C.c_uint32))), f"bits {name}")
         return out
 

@@ -46,13 +46,17 @@ def _closure_worker(rank, world, nid, n, kind, mode, q):
     from tensor_logic_lang_b200.runtime import Context
     ctx = Context(device=rank, rank=rank, world_size=world, nccl_id=nid, comm_timeout_ms=60000)
     try:
-        ctx.set_sharding("Reach", abi.SHARD_ROWS)
+        # "cols": this rank keeps its slice of the columns of every row
+        ctx.set_sharding("Reach", abi.SHARD_COLS if mode == "cols" else abi.SHARD_ROWS)
         rows, cols = _graph(n, kind)
         p = lang.Program(_closure_src(n), sparse_inputs={"Edge": (rows, cols, None)})
         out = []
         for _ in range(2):          # a second run: the next epoch of closed words
             ctx.run(p)
-            out.append((ctx.bits("Reach", rows=shard.local_count(n, rank, world)), ctx.sweeps))
+            if mode == "cols":
+                out.append((ctx.bits("Reach", words=n // 32 // world), ctx.sweeps))
+            else:
+                out.append((ctx.bits("Reach", rows=shard.local_count(n, rank, world)), ctx.sweeps))
         q.put((rank, "closure", out))
     finally:
         ctx.close()
@@ -93,14 +97,16 @@ def _run(target, world, *args):
 
 
 CLOSURE_CASES = [(8192, "dag", "replicate"), (5000, "cyclic", "replicate"), (8192, "dag", "peer"),
-                 (5000, "cyclic", "peer"), (5000, "cyclic", "local"), (4099, "dag", "bfs")]
+                 (5000, "cyclic", "peer"), (5000, "cyclic", "local"), (4099, "dag", "bfs"),
+                 (8192, "dag", "cols"), (5120, "cyclic", "cols")]
 
 
 @pytest.mark.skipif(_world() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("n,kind,mode", CLOSURE_CASES, ids=[f"{c[1]}{c[0]}-{c[2]}" for c in CLOSURE_CASES])
 def test_sharded_closure(oracle_lib, n, kind, mode):
-    # every lazy-sweep mode of a row-sharded relation against the oracle,
-    # bit for bit, on a DAG (2 sweeps) and on a graph with cycles
+    # every lazy-sweep mode of a row-sharded relation, and the column split,
+    # against the oracle, bit for bit, on a DAG (2 sweeps) and on a graph
+    # with cycles
     world = _world()
     out = _run(_closure_worker, world, n, kind, mode)
     rows, cols = _graph(n, kind)
@@ -109,7 +115,10 @@ def test_sharded_closure(oracle_lib, n, kind, mode):
     np.bitwise_or.at(R, (rows, cols >> 5), (np.uint32(1) << (cols & 31).astype(np.uint32)))
     sweeps = oracle_lib.closure_right(n, colptr, rowidx, R)
     for run in range(2):
-        got = shard.assemble([o[2][run][0] for o in out], n)
+        if mode == "cols":
+            got = np.concatenate([o[2][run][0] for o in out], axis=1)
+        else:
+            got = shard.assemble([o[2][run][0] for o in out], n)
         np.testing.assert_array_equal(got, R)
         got_sweeps = {o[2][run][1] for o in out}
         assert len(got_sweeps) == 1
