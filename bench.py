@@ -273,9 +273,10 @@ def run_closure(args, dist, peaks):
     from tensor_logic_lang_b200.runtime import Context, unique_id
     nid = dist.bcast_bytes(unique_id() if dist.rank == 0 else None) if dist.world > 1 else None
     ctx = Context(device=dist.local, rank=dist.rank, world_size=dist.world, nccl_id=nid)
-    # columns split (TL_CLOSURE_SHARDED=cols): every rank keeps all rows of its
-    # slice of the columns; otherwise rows cyclic over the ranks
-    col_split = dist.world > 1 and os.environ.get("TL_CLOSURE_SHARDED") == "cols"
+    # columns split (the default on several GPUs): every rank keeps all rows
+    # of its slice of the columns; TL_CLOSURE_SHARDED=replicate, peer, local
+    # or bfs deals the rows cyclically over the ranks instead
+    col_split = dist.world > 1 and closure_scheme() == "cols"
     if dist.world > 1:
         ctx.set_sharding("Reach", abi.SHARD_COLS if col_split else abi.SHARD_ROWS)
     full, resident, rows, cols = closure_program(dist, resident=True)
@@ -353,11 +354,17 @@ def run_closure(args, dist, peaks):
     return res
 
 
+def closure_scheme():
+    """How the closure is split over several GPUs: "cols" (slices of the
+    columns, no exchange) unless TL_CLOSURE_SHARDED names a row scheme."""
+    return os.environ.get("TL_CLOSURE_SHARDED", "cols")
+
+
 def closure_parallelism(world):
     """The bench line's description of how the closure's rows are split."""
     if world == 1:
         return "1 GPU"
-    scheme = os.environ.get("TL_CLOSURE_SHARDED", "replicate")
+    scheme = closure_scheme()
     how = {"replicate": "every GPU closes every row in the first sweep and keeps its own",
            "peer": "every GPU closes its own rows, reading other GPUs' closed rows over NVLink",
            "local": "every GPU closes its own rows with shortcuts through its own rows only",
