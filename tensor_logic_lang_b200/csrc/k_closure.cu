@@ -79,6 +79,8 @@ struct FixState {
     uint32_t n_or_local, n_or_remote, n_expanded;
 };
 constexpr int kFixMarks = 2;
+constexpr size_t kFixStateBytes = 128;   // one control block (two by launch parity; the pinned mirror)
+static_assert(sizeof(FixState) <= kFixStateBytes && sizeof(FixState) % 8 == 0, "control block");
 
 struct FixArgs {
     uint32_t* R;
@@ -121,6 +123,10 @@ struct FixArgs {
     uint32_t* prows[kMaxPeers];
     int shortcut;              // lazy rows OR closed rows in (and run in descending order)
     FixState* st;
+    FixState* st_next;     // the next launch's control block, emptied by this one
+    // the pinned host mirror of the control block: written by the block that
+    // settles the last sweep (no copy behind the launch)
+    unsigned long long* host_out;
     int team;                  // warps per block
     unsigned team_qmask;       // team queue positions - 1 (a power of two)
     int team_budget;           // rows handed to teams after this many queued bits (0: no teams)
@@ -1105,6 +1111,15 @@ __device__ bool grid_barrier(const FixArgs& a, unsigned gen, int s, bool settle)
                 // the last sweep of the launch moves the token base past it
                 if (a.exchange && !a.st->go) *a.token_base += (unsigned long long)(s + 1);
                 if (s < kFixMarks) a.st->t_settled[s] = global_ns();
+                if (!a.st->go) {
+                    // the launch's result to the host's pinned mirror (visible
+                    // to the host once the launch has completed)
+                    __threadfence();
+                    const volatile unsigned long long* src = reinterpret_cast<const volatile unsigned long long*>(a.st);
+                    volatile unsigned long long* dst = a.host_out;
+#pragma unroll
+                    for (int i = 0; i < (int)(sizeof(FixState) / 8); ++i) dst[i] = src[i];
+                }
             }
             a.st->bar_count = 0;
             __threadfence();
@@ -1141,6 +1156,10 @@ __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs
     uint32_t* spill = row + a.wpad + 4;
     uint32_t* q = spill + a.wpad;
     if (blockIdx.x == 0 && threadIdx.x == 0) a.st->t_start = global_ns();
+    // the next launch's control block (the one the launch before this used,
+    // whose result the host has read): emptied here, not by a host memset
+    if (blockIdx.x == 0 && threadIdx.x < sizeof(FixState) / 8)
+        reinterpret_cast<unsigned long long*>(a.st_next)[threadIdx.x] = 0ull;
     unsigned gen = 0;
     for (int s = 0; s < a.max_sweeps; ++s) {
         const bool lazy = a.lazy && s == 0;
@@ -1347,9 +1366,13 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         TL_CK(c, cudaMalloc(&c->aux, aux_need));
         c->aux_cap = aux_need;
     }
-    static_assert(sizeof(FixState) <= 128, "control block and its pinned mirror");
     static_assert(kFixWarps * 32 <= 1024, "block size");
-    if (!c->fix_state) TL_CK(c, cudaMalloc(&c->fix_state, 256));
+    // two control blocks, by launch parity: each launch empties the other
+    if (!c->fix_state) {
+        TL_CK(c, cudaMalloc(&c->fix_state, 2 * kFixStateBytes));
+        TL_CK(c, cudaMemsetAsync(c->fix_state, 0, 2 * kFixStateBytes, c->stream));
+        c->fix_slot = 0;
+    }
     // rows that step(E) left unwritten start from E's successor lists; their
     // sweep ORs in closed rows (closed words of this launch's epoch)
     const bool lazy = R->bits_valid && R->lazy_src == E && R->lazy_stamp == E->csr_stamp;
@@ -1411,7 +1434,6 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     // the lazy sweep with shortcuts writes every row's pending word before any
     // later sweep reads it; otherwise every row starts fully pending
     if (rows > 0 && !shortcut) TL_CK(c, cudaMemsetAsync(c->aux, 0, (size_t)rows * 4, c->stream));
-    TL_CK(c, cudaMemsetAsync(c->fix_state, 0, sizeof(FixState), c->stream));
 
     // shape: with teams (TL_CLOSURE_TEAMS) the largest block that fits, so a
     // heavy row gets the most warps; otherwise the split that keeps the most
@@ -1464,7 +1486,14 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     a.team = wpb;
     a.team_qmask = (unsigned)(qt - 1);
     a.team_budget = teams ? kHeavyBudget : 0;
-    a.st = (FixState*)c->fix_state;
+    // the pinned mirror reads "no result" until the launch writes it (the
+    // previous launch is resolved above, so nothing writes it meanwhile)
+    FixState* const mirror = reinterpret_cast<FixState*>(c->h_flags + 32);
+    mirror->sweeps = -1;
+    a.host_out = reinterpret_cast<unsigned long long*>(mirror);
+    FixState* const slots = static_cast<FixState*>(c->fix_state);
+    a.st = reinterpret_cast<FixState*>(reinterpret_cast<char*>(slots) + c->fix_slot * kFixStateBytes);
+    a.st_next = reinterpret_cast<FixState*>(reinterpret_cast<char*>(slots) + (1 - c->fix_slot) * kFixStateBytes);
     a.lazy = lazy ? 1 : 0;
     a.shortcut = shortcut ? 1 : 0;
     a.closed = static_cast<unsigned long long*>(c->fix_closed);
@@ -1529,16 +1558,17 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
         c->fix_counted = count;
         TL_CK(c, cudaLaunchCooperativeKernel(fn, dim3((unsigned)grid), dim3(32 * wpb), args,
                                              per_warp * wpb, c->stream));
+        c->fix_slot ^= 1;   // the launch empties the other block before it ends
         TL_TRY(L.done());
     }
-    // the control block comes back to pinned memory behind the launch; it is
-    // read at once only when the caller needs the sweep count or when
+    // the control block comes back to pinned memory from the kernel itself;
+    // it is read at once only when the caller needs the sweep count or when
     // profiling (the phase marks); otherwise when the context next syncs,
     // asks for the sweep count or launches another fixpoint
-    TL_CK(c, cudaMemcpyAsync(c->h_flags + 32, c->fix_state, sizeof(FixState), cudaMemcpyDeviceToHost, c->stream));
     if (!c->fix_event) TL_CK(c, cudaEventCreateWithFlags(&c->fix_event, cudaEventDisableTiming));
     TL_CK(c, cudaEventRecord(c->fix_event, c->stream));
     c->fix_pending = true;
+    c->fix_last_state = a.st;
     c->fix_prof = c->prof;
     c->fix_sweep_bytes = sweep_bytes;
     R->lazy_src = nullptr;   // every row is written now (or the status of the launch says why not)
@@ -1557,6 +1587,9 @@ tl_status fix_resolve(tl_ctx* c) {
     TL_CK(c, cudaEventSynchronize(c->fix_event));
     FixState h{};
     memcpy(&h, c->h_flags + 32, sizeof(FixState));
+    // a launch that ended without settling its last sweep (a wait that ran
+    // out) did not write the mirror: its control block holds the error
+    if (h.sweeps < 0) TL_CK(c, cudaMemcpy(&h, c->fix_last_state, sizeof(FixState), cudaMemcpyDeviceToHost));
     // algorithmic bytes of the launch: every sweep reads and writes the rows
     if (c->fix_prof && !c->pending.empty() && c->pending.back().name == "closure_fixpoint")
         c->pending.back().bytes = c->fix_sweep_bytes * std::max(h.sweeps, 1);

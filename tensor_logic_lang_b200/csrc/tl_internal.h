@@ -162,7 +162,9 @@ struct tl_ctx {
     void* aux = nullptr;        // state kept across the sweeps of one fixpoint
     size_t aux_cap = 0;
     int* h_flags = nullptr;     // pinned mirror
-    void* fix_state = nullptr;  // control block of the one-launch closure fixpoint
+    void* fix_state = nullptr;  // control blocks of the one-launch closure fixpoint (two, by launch parity)
+    int fix_slot = 0;           // the block the next launch uses
+    void* fix_last_state = nullptr;   // the block the last launch used
     // closed words of the lazy closure sweep: one per local row, tagged with
     // the launch's epoch so no launch has to clear them
     void* fix_closed = nullptr;
