@@ -1435,13 +1435,17 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     const bool split = p.relu_term != 0;
     const bool precise = !split && p.precise != 0;
     const float sgn = p.scale < 0.f ? -1.f : 1.f;
-    const int nseg = split ? 2 : precise ? 3 : 1;
-    const unsigned ops_a = split ? (OP_POS | OP_NEG << 4) : precise ? (OP_RN | OP_RN << 4 | OP_LO << 8) : OP_RN;
-    const unsigned ops_b = split ? (OP_POS | OP_NEG << 4) : precise ? (OP_RN | OP_LO << 4 | OP_RN << 8) : OP_RN;
+    // relu(s a b) = a+ (s b)+ + a- (s b)-; with a >= 0 it is a (s b)+, and
+    // with b >= 0 it is (s a)+ b: one K segment instead of two
+    const bool one_a = split && p.a_nonneg, one_b = split && !one_a && p.b_nonneg;
+    const bool split2 = split && !one_a && !one_b;
+    const int nseg = split2 ? 2 : precise ? 3 : 1;
+    const unsigned ops_a = split2 ? (OP_POS | OP_NEG << 4) : one_b ? OP_POS : precise ? (OP_RN | OP_RN << 4 | OP_LO << 8) : OP_RN;
+    const unsigned ops_b = split2 ? (OP_POS | OP_NEG << 4) : one_a ? OP_POS : precise ? (OP_RN | OP_LO << 4 | OP_RN << 8) : OP_RN;
     const int64_t Ke = nseg * p.K;
     struct Prep { int64_t R, s_r, s_k; unsigned ops; float sgn; bool mn; int64_t ld; float* dst; const char* name; };
-    Prep pa{p.M, p.sam, p.sak, ops_a, 1.f, use_mn && p.sak != 1 && p.sam == 1, 0, nullptr, "gemm_prep_a"};
-    Prep pb{p.N, p.sbn, p.sbk, ops_b, split ? sgn : 1.f, use_mn && p.sbk != 1 && p.sbn == 1, 0, nullptr,
+    Prep pa{p.M, p.sam, p.sak, ops_a, one_b ? sgn : 1.f, use_mn && p.sak != 1 && p.sam == 1, 0, nullptr, "gemm_prep_a"};
+    Prep pb{p.N, p.sbn, p.sbk, ops_b, split2 || one_a ? sgn : 1.f, use_mn && p.sbk != 1 && p.sbn == 1, 0, nullptr,
             "gemm_prep_b"};
     size_t need = 0;
     for (Prep* q : {&pa, &pb}) {

@@ -469,7 +469,8 @@ Tensor* relu_successor(tl_ctx* c, const tl_equation* eq, const tl_equation* next
 constexpr int kGnnCounter = 64;   // word of the peer slot array where rank r's tile count is kept (+ r)
 
 static tl_status sparse_chain_fanned(tl_ctx* c, Tensor* S, Tensor* lhs, const float* xp, const float* wp, int64_t nu,
-                                     int64_t x_rows, int64_t g, int64_t f, bool relu, bool* handled) {
+                                     int64_t x_rows, int64_t g, int64_t f, bool relu, bool x_nonneg, bool w_nonneg,
+                                     bool* handled) {
     *handled = false;
     const int world = c->world;
     const int64_t per = (nu + world - 1) / world;
@@ -496,6 +497,7 @@ static tl_status sparse_chain_fanned(tl_ctx* c, Tensor* S, Tensor* lhs, const fl
     gp.B = wp; gp.sbk = f; gp.sbn = 1;
     gp.C = gathered(c->rank) + (int64_t)c->rank * per * f; gp.scm = f; gp.scn = 1;
     gp.scale = 1.0f; gp.beta = 0; gp.relu_term = relu ? 1 : 0;
+    gp.a_nonneg = x_nonneg ? 1 : 0; gp.b_nonneg = w_nonneg ? 1 : 0;
     float* dst[kMaxPeers] = {};
     unsigned long long* cnt[kMaxPeers] = {};
     for (int q = 0; q < world; ++q) {
@@ -535,6 +537,7 @@ static tl_status sparse_chain_fanned(tl_ctx* c, Tensor* S, Tensor* lhs, const fl
                        per * world, f, f, lhs->dense, f, 0, 0, world, per, &w));
     mark_written_dense(lhs);
     lhs->boolean = false;
+    lhs->nonneg = relu && S->csr_nonneg;   // S >= 0 times P, a sum of relus
     *handled = true;
     return TL_OK;
 }
@@ -587,7 +590,7 @@ tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, 
     int64_t gathered_rows_per_rank = sharded ? (nu + c->world - 1) / c->world : 0;
     if (sharded && xp && wp) {
         bool handled = false;
-        TL_TRY(sparse_chain_fanned(c, S, lhs, xp, wp, nu, lrows_x, g, f, relu, &handled));
+        TL_TRY(sparse_chain_fanned(c, S, lhs, xp, wp, nu, lrows_x, g, f, relu, X->nonneg, W->nonneg, &handled));
         if (handled) {
             *done = true;
             return TL_OK;
@@ -609,6 +612,7 @@ tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, 
         gp.B = wp; gp.sbk = f; gp.sbn = 1;
         gp.C = P; gp.scm = f; gp.scn = 1;
         gp.scale = 1.0f; gp.beta = 0; gp.relu_term = relu ? 1 : 0;
+        gp.a_nonneg = X->nonneg ? 1 : 0; gp.b_nonneg = W->nonneg ? 1 : 0;
         if (p_rows > 0) TL_TRY(launch_gemm(c, gp));
     }
     const float* Pfull = P;
@@ -628,6 +632,7 @@ tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, 
         col_local = gathered_rows_per_rank;
     }
     int beta = lhs->zero ? 0 : 1;
+    const bool was_nonneg = lhs->nonneg;
     if (beta) TL_TRY(ensure_dense(c, lhs));
     else TL_TRY(alloc_dense_public(c, lhs));
     int64_t out_rows = lhs->local_rows(c->rank, c->world);
@@ -636,6 +641,8 @@ tl_status try_sparse_chain(tl_ctx* c, const tl_equation* eq, const Analysis& a, 
                        col_world, col_local));
     mark_written_dense(lhs);
     lhs->boolean = false;
+    // S >= 0 times P, a sum of relus (plus what was there, if that was >= 0)
+    lhs->nonneg = relu && S->csr_nonneg && (beta == 0 || was_nonneg);
     *done = true;
     return TL_OK;
 }
@@ -1006,6 +1013,7 @@ static tl_status generic_recursive(tl_ctx* c, const tl_equation* eq, int* d_chan
     p->atomic = lhs_injective(a, lhs) ? 0 : 1;
     p->recursive = 1;
     bool was_bool = lhs->boolean;
+    lhs->nonneg = false;   // written in place below
     if (p->n_out > 0 && p->n_inner > 0) TL_TRY(launch_generic(c, *p, d_changed));
     lhs->boolean = was_bool && eq->accum == TL_ACC_MAX && root_is_boolean(eq);
     return TL_OK;
@@ -1110,6 +1118,7 @@ static tl_status run_load(tl_ctx* c, const tl_statement* st) {
         // resident input: the device storage already holds this run's values
         if (!t->dense) return fail(c, TL_ERR_INVALID, "%s: resident load without device data", st->name);
         t->zero = false;
+        t->nonneg = false;   // values unknown to the host
         t->dense_valid = true;
         t->bits_valid = t->csr_valid = t->csc_valid = false;
         return TL_OK;
@@ -1132,6 +1141,7 @@ static tl_status run_sparse_load(tl_ctx* c, const tl_statement* st) {
         t->zero = false;
         t->csr_valid = true;
         t->boolean = t->csr_ones;
+        t->nonneg = t->csr_nonneg;
         t->dense_valid = t->bits_valid = false;
         t->csc_valid = t->colptr != nullptr;
         return TL_OK;
@@ -1349,7 +1359,7 @@ struct TensorSnap {
     int64_t dims[TL_MAX_RANK];
     int64_t total, dense_elems, bits_words, bits_rows, nnz, csr_cap, csr_rows, csc_cap, succ_cap, succ_nodes;
     uint8_t defined, zero, boolean, is_sparse, dense_valid, bits_valid, csr_valid, csc_valid, csr_nonneg, csr_ones,
-        csr_pos, pad[5];
+        csr_pos, nonneg, pad[4];
     const void *dense, *bits, *rowptr, *colidx, *vals, *colptr, *rowidx, *succ, *lazy_src;
     uint64_t csr_stamp, succ_stamp, lazy_stamp;
 };
@@ -1382,6 +1392,7 @@ std::vector<uint8_t> snapshot(tl_ctx* c) {
         z.defined = t->defined; z.zero = t->zero; z.boolean = t->boolean; z.is_sparse = t->is_sparse;
         z.dense_valid = t->dense_valid; z.bits_valid = t->bits_valid; z.csr_valid = t->csr_valid;
         z.csc_valid = t->csc_valid; z.csr_nonneg = t->csr_nonneg; z.csr_ones = t->csr_ones; z.csr_pos = t->csr_pos;
+        z.nonneg = t->nonneg;
         z.dense = t->dense; z.bits = t->bits; z.rowptr = t->rowptr; z.colidx = t->colidx; z.vals = t->vals;
         z.colptr = t->colptr; z.rowidx = t->rowidx; z.succ = t->succ; z.lazy_src = t->lazy_src;
         z.csr_stamp = t->csr_stamp; z.succ_stamp = t->succ_stamp; z.lazy_stamp = t->lazy_stamp;
@@ -1432,6 +1443,7 @@ void apply_snapshot(tl_ctx* c, const std::vector<uint8_t>& snap) {
         t->defined = z->defined; t->zero = z->zero; t->boolean = z->boolean; t->is_sparse = z->is_sparse;
         t->dense_valid = z->dense_valid; t->bits_valid = z->bits_valid; t->csr_valid = z->csr_valid;
         t->csc_valid = z->csc_valid; t->csr_nonneg = z->csr_nonneg; t->csr_ones = z->csr_ones; t->csr_pos = z->csr_pos;
+        t->nonneg = z->nonneg;
         t->nnz = z->nnz; t->csr_rows = z->csr_rows; t->csr_stamp = z->csr_stamp; t->succ_stamp = z->succ_stamp;
         t->succ_nodes = z->succ_nodes; t->succ_sentinel = z->succ_sentinel;
         t->lazy_src = const_cast<Tensor*>(static_cast<const Tensor*>(z->lazy_src));

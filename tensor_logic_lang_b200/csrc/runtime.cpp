@@ -264,6 +264,7 @@ tl_status alloc_bits_public(tl_ctx* c, Tensor* t) { return alloc_bits(c, t); }
 
 void mark_written_dense(Tensor* t) {
     t->lazy_src = nullptr;
+    t->nonneg = false;
     t->dense_valid = true;
     t->zero = false;
     t->bits_valid = t->csr_valid = t->csc_valid = false;
@@ -271,6 +272,7 @@ void mark_written_dense(Tensor* t) {
 
 void mark_written_bits(Tensor* t) {
     t->lazy_src = nullptr;
+    t->nonneg = true;   // 0/1 values
     t->bits_valid = true;
     t->zero = false;
     t->boolean = true;
@@ -488,7 +490,7 @@ static tl_status upload_common(tl_ctx* c, Tensor* t, const double* h64, const fl
     TL_TRY(staging(c, n * sizeof(float) + 16, &st));
     // the staging buffer is reused: wait for earlier copies out of it
     TL_CK(c, cudaStreamSynchronize(c->stream));
-    bool boolean = true;
+    bool boolean = true, nonneg = true;
     for (int64_t lr = 0; lr < lrows; ++lr) {
         int64_t gr = sharded ? lr * c->world + c->rank : lr;
         const int64_t src = gr * row_elems, dst = lr * row_elems;
@@ -496,12 +498,14 @@ static tl_status upload_common(tl_ctx* c, Tensor* t, const double* h64, const fl
             float v = h64 ? (float)h64[src + j] : h32[src + j];
             st[dst + j] = v;
             boolean = boolean && (v == 0.0f || v == 1.0f);
+            nonneg = nonneg && v >= 0.0f;
         }
     }
     if (t->rank == 0 || rows == 0) { /* scalar / empty */ }
     TL_CK(c, cudaMemcpyAsync(t->dense, st, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     mark_written_dense(t);
     t->boolean = boolean;
+    t->nonneg = nonneg;
     return TL_OK;
 }
 
@@ -587,8 +591,10 @@ extern "C" tl_status tl_tensor_set(tl_tensor* t, const int64_t* idx, double v) {
     TL_CK(c, cudaMemcpyAsync(t->dense + off, &f, 4, cudaMemcpyHostToDevice, c->stream));
     TL_CK(c, cudaStreamSynchronize(c->stream));
     bool b = t->boolean && (f == 0.0f || f == 1.0f);
+    const bool nn = t->nonneg && f >= 0.0f;
     mark_written_dense(t);
     t->boolean = b;
+    t->nonneg = nn;
     return TL_OK;
 }
 
@@ -615,6 +621,7 @@ extern "C" tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* 
         t->csr_valid = true;
         t->csr_stamp = next_csr_stamp();
         t->boolean = t->csr_nonneg && t->csr_ones;
+        t->nonneg = t->csr_nonneg;
         t->dense_valid = t->bits_valid = t->csc_valid = false;
         return TL_OK;
     }
@@ -725,6 +732,7 @@ extern "C" tl_status tl_sparse_upload(tl_tensor* t, int64_t nnz, const int64_t* 
     t->csr_pos = pos;
     t->csr_ones = ones;
     t->boolean = nonneg && ones;
+    t->nonneg = nonneg;
     t->dense_valid = t->bits_valid = t->csc_valid = false;
     return TL_OK;
 }

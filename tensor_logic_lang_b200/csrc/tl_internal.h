@@ -44,6 +44,10 @@ struct Tensor {
     bool boolean = false;   // every value is 0 or 1
     bool is_sparse = false; // declared `sparse`
     int shard = TL_SHARD_NONE;
+    // every dense value is >= 0: set only by a writer that knows it (an upload
+    // that saw the values, a message-passing chain with relu per term over a
+    // non-negative sparse operand); any other write clears it
+    bool nonneg = false;
     int col_rank = 0, col_world = 1;   // TL_SHARD_COLS: this rank's slice of the columns
 
     // fp32 dense row-major (local rows only when sharded)
@@ -333,6 +337,7 @@ struct GemmPlan {
     float scale;
     int32_t beta;        // 1: add into C, 0: overwrite
     int32_t relu_term;   // per-term relu
+    int32_t a_nonneg, b_nonneg;   // per-term relu: A (B) has no negative value, so one K segment suffices
     int32_t epi_relu;    // additionally write relu(C) into D (fused next equation)
     int32_t precise;     // fp32-class accuracy (3xTF32) on the tensor cores
     float* D; int64_t sdm, sdn;

@@ -370,6 +370,32 @@ def test_attention_block_accumulating_scores(ctx, oracle_lib):
         assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
 
 
+@pytest.mark.parametrize("signs", ["x_nonneg", "w_nonneg", "mixed"])
+def test_relu_per_term_with_a_nonnegative_operand(ctx, oracle_lib, signs):
+    # relu(x w) per term needs both sign halves of x and w (K doubled) unless
+    # one operand has no negative value: then x relu(w) or relu(x) w, one K
+    # segment.  H0 >= 0 (uploaded), W1 >= 0, or neither; H1 >= 0 always (a
+    # non-negative Adj times a sum of relus), so layer 2 takes the one-segment
+    # form in every case.  Both layers against the oracle.
+    from tensor_logic_lang_b200 import configs
+    from tensor_logic_lang_b200 import inputs as gen
+    from tensor_logic_lang_b200.lang import Program
+    n, f = 8192, 128
+    src, d, sp, _ = configs.gnn(n=n, f=f)
+    d = dict(d)
+    if signs == "x_nonneg":
+        d["H0"] = np.abs(d["H0"])
+    elif signs == "w_nonneg":
+        d["W1"] = np.abs(d["W1"])
+    ctx.run(Program(src, inputs=d, sparse_inputs=sp))
+    rows, cols, _ = sp["Adj"]
+    rowptr, colidx = gen.csr_from_coo(n, rows, cols)
+    h1 = oracle_lib.gnn_layer(rowptr, colidx, d["H0"], d["W1"])
+    h2 = oracle_lib.gnn_layer(rowptr, colidx, h1, d["W2"])
+    assert_close(ctx.tensor_f32("H1"), h1, TOL_TF32, "H1")
+    assert_close(ctx.tensor_f32("H2"), h2, TOL_TF32, "H2")
+
+
 @pytest.mark.parametrize("n,f", [(16384, 256), (16384, 128), (700, 64)])
 def test_spmm_tma_gathers_match_register_gathers(ctx, oracle_lib, monkeypatch, n, f):
     # the message-passing SpMM gathers rows of P by tile::gather4 copies for
