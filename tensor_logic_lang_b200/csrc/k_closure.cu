@@ -1295,7 +1295,7 @@ tl_status launch_closure_fixpoint(tl_ctx* c, Tensor* R, Tensor* E, int max_sweep
     constexpr size_t kSmemCap = 200 * 1024;
     // columns sharded: this rank stores a slice of every row; the warps still
     // build full-width rows in shared memory (words is the full width)
-    const bool cols = R->shard == TL_SHARD_COLS && R->col_world > 1;
+    const bool cols = col_split(R);
     const int64_t words = cols ? (R->dims[1] + 31) / 32 : R->bits_words, rows = R->bits_rows;
     const int64_t wpad = (words + 3) & ~int64_t(3);
     // one table entry per bit position of a row (padding bits included)

@@ -671,7 +671,7 @@ tl_status try_step_bits(tl_ctx* c, const tl_equation* eq, const Analysis& a, Ten
         *done = true;
         return TL_OK;
     }
-    if (lhs->shard == TL_SHARD_COLS)
+    if (col_split(lhs))
         return fail(c, TL_ERR_UNSUPPORTED, "%s: a column-sharded relation must start as step(Edge) right before "
                     "its fixpoint", lhs->name.c_str());
     TL_TRY(launch_csr_to_bits(c, E, lhs));

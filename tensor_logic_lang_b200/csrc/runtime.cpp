@@ -191,7 +191,7 @@ static tl_status alloc_bits(tl_ctx* c, Tensor* t) {
     if (t->rank != 2) return fail(c, TL_ERR_UNSUPPORTED, "%s: bit storage needs rank 2", t->name.c_str());
     int64_t words = (t->dims[1] + 31) / 32;
     int64_t rows = dense_rows(c, t);
-    if (t->shard == TL_SHARD_COLS) {
+    if (col_split(t)) {
         // this rank's slice of the columns of every row
         if (t->dims[1] % (128 * (int64_t)t->col_world))
             return fail(c, TL_ERR_UNSUPPORTED, "%s: column sharding needs a multiple of %d columns", t->name.c_str(),
@@ -209,7 +209,7 @@ static tl_status alloc_bits(tl_ctx* c, Tensor* t) {
 }
 
 tl_status ensure_dense(tl_ctx* c, Tensor* t) {
-    if (t->shard == TL_SHARD_COLS)
+    if (col_split(t))
         return fail(c, TL_ERR_UNSUPPORTED, "%s: a column-sharded relation is read only as bit rows",
                     t->name.c_str());
     TL_TRY(alloc_dense(c, t));
@@ -230,7 +230,7 @@ tl_status ensure_dense(tl_ctx* c, Tensor* t) {
 
 tl_status ensure_bits(tl_ctx* c, Tensor* t) {
     // a column-sharded relation is written only by its closure fixpoint
-    if (t->shard == TL_SHARD_COLS && !(t->bits_valid && !t->lazy_src))
+    if (col_split(t) && !(t->bits_valid && !t->lazy_src))
         return fail(c, TL_ERR_UNSUPPORTED, "%s: a column-sharded relation must start as step(Edge) right before "
                     "its fixpoint", t->name.c_str());
     TL_TRY(alloc_bits(c, t));
@@ -765,19 +765,26 @@ extern "C" tl_status tl_set_sharding(tl_ctx* c, const char* name, int32_t mode) 
     if (!c || !name || (mode != TL_SHARD_NONE && mode != TL_SHARD_ROWS && mode != TL_SHARD_COLS)) return TL_ERR_INVALID;
     auto& slot = c->tensors[name];
     if (!slot) { slot.reset(new tl_tensor()); slot->name = name; slot->defined = false; slot->owner = c; }
-    int col_rank = c->rank, col_world = c->world;
-    // TL_SHARD_COLS_OF="r/n": slice r of n on a one-GPU context (tests check
-    // the slices one by one against the whole relation)
-    if (const char* of = getenv("TL_SHARD_COLS_OF")) {
-        if (mode == TL_SHARD_COLS && c->world == 1 && sscanf(of, "%d/%d", &col_rank, &col_world) == 2 &&
-            !(col_world >= 1 && col_rank >= 0 && col_rank < col_world))
-            return TL_ERR_INVALID;
+    // columns: slice rank of world; TL_SHARD_COLS_OF="r/n" makes it slice r
+    // of n on a one-GPU context (tests check the slices one by one against
+    // the whole relation)
+    int col_rank = 0, col_world = 1;
+    if (mode == TL_SHARD_COLS) {
+        col_rank = c->rank;
+        col_world = c->world;
+        const char* of = getenv("TL_SHARD_COLS_OF");
+        if (of && c->world == 1) {
+            int r = -1, w = 0;
+            if (sscanf(of, "%d/%d", &r, &w) != 2 || w < 1 || r < 0 || r >= w) return TL_ERR_INVALID;
+            col_rank = r;
+            col_world = w;
+        }
     }
     if (slot->shard != mode || slot->col_rank != col_rank || slot->col_world != col_world) {
         free_storage(slot.get());
         slot->shard = mode;
-        slot->col_rank = mode == TL_SHARD_COLS ? col_rank : 0;
-        slot->col_world = mode == TL_SHARD_COLS ? col_world : 1;
+        slot->col_rank = col_rank;
+        slot->col_world = col_world;
         slot->zero = true;
     }
     return TL_OK;

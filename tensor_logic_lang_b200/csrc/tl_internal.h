@@ -99,6 +99,10 @@ struct Tensor {
     }
 };
 
+// the relation's columns are split over several slices (TL_SHARD_COLS with
+// more than one slice); one slice behaves as an unsharded tensor
+inline bool col_split(const Tensor* t) { return t->shard == TL_SHARD_COLS && t->col_world > 1; }
+
 // A captured CUDA graph of one program run (tl_program_run): replayed while
 // the statements and the context's host state at the start of a run (tensor
 // storages, flags, workspaces) are the same as when it was captured.
