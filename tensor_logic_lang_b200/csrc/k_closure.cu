@@ -10,10 +10,16 @@
 // where the last block to arrive settles the sweep: it reads the changed
 // word, on a multi-GPU context exchanges it with every other rank through
 // peer memory (one 8-byte store per peer over NVLink, then a wait for the
-// peers' stores), and decides whether another sweep runs.  The host reads
-// the sweep count once, after the launch.  Every wait is bounded by
-// %globaltimer; a wait that runs out records an error word and the kernel
-// returns.
+// peers' stores), and decides whether another sweep runs.  The block that
+// settles the last sweep writes the control block (sweep count, error word)
+// into the host's pinned mirror, which the host reads once, after the
+// launch.  Every wait is bounded by %globaltimer; a wait that runs out
+// records an error word and the kernel returns.
+//
+// With the columns split over ranks, a rank stores a slice of every row:
+// the warp still builds the full row in shared memory, ORs in and writes
+// back only the slice, and takes the first sweep's changed word from the
+// graph (k_two_hop), so no rank waits for another.
 //
 // Per row, a warp keeps the row in shared memory and closes it with a
 // breadth-first search over a successor table: node y's entry is one 32-byte
