@@ -97,7 +97,7 @@ def test_partition_helpers():
         assert layout[shard.gathered_row(u, world, per)] == u
 
 
-def _parity_worker(rank, world, port, n, rows, cols, swap, q):
+def _parity_worker(rank, world, port, n, rows, cols, swap, col_split, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     import bench
     from oracle import oracle
@@ -106,26 +106,33 @@ def _parity_worker(rank, world, port, n, rows, cols, swap, q):
     colptr, rowidx = gen.csr_from_coo(n, cols, rows)
     full = _bits(n, rows, cols)
     sweeps = oracle.closure_right(n, colptr, rowidx, full)
-    mine = np.ascontiguousarray(full[shard.global_rows(n, rank, world)])
+    if col_split:
+        # this rank's slice of the columns of every row
+        w = n // 32 // world
+        mine = np.ascontiguousarray(full[:, rank * w:(rank + 1) * w])
+    else:
+        mine = np.ascontiguousarray(full[shard.global_rows(n, rank, world)])
     if swap and rank == 1:
         mine[[3, 4]] = mine[[4, 3]]          # two rows in the wrong places, same pair count
-    res = bench.closure_parity(dist, mine, sweeps, rows, cols)
+    res = bench.closure_parity(dist, mine, sweeps, rows, cols, col_split)
     if rank == 0:
         q.put(res)
     dist.close()
 
 
 @pytest.mark.parametrize("swap", [False, True], ids=["exact", "rows_swapped"])
-def test_bench_closure_parity_over_gloo(oracle_lib, swap):
-    # bench.py's N > 1 parity leg: per-row digests gathered from every rank
-    # and compared with the oracle's rows; a swap of two rows on one rank
-    # keeps the pair count but must read as a mismatch
+@pytest.mark.parametrize("col_split", [False, True], ids=["rows", "columns"])
+def test_bench_closure_parity_over_gloo(oracle_lib, swap, col_split):
+    # bench.py's N > 1 parity leg: per-row digests (of a row, or of a row's
+    # column slice) gathered from every rank and compared with the oracle's;
+    # a swap of two rows on one rank keeps the pair count but must read as a
+    # mismatch
     n, world = 256, 2
     rows, cols = gen.random_dag(n, 3, 22)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_parity_worker, args=(r, world, port, n, rows, cols, swap, q))
+    procs = [ctx.Process(target=_parity_worker, args=(r, world, port, n, rows, cols, swap, col_split, q))
              for r in range(world)]
     for p in procs:
         p.start()
