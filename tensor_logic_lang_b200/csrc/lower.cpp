@@ -1297,6 +1297,114 @@ static tl_status try_attention(tl_ctx* c, const tl_equation* e1, const tl_equati
     return TL_OK;
 }
 
+// A small-batch head: H[b, h] = [relu](X[b, i] W1[i, h] s1), Z[b, o] =
+// H[b, h] W2[h, o] s2, Y[b, o.] = softmax(Z[b, o]) (either operand order in
+// each product), b <= 64 and o <= 32, H and Z defined fresh by these
+// statements: two launches (k_head.cu) instead of three latency-bound ones.
+static tl_status try_head(tl_ctx* c, const tl_equation* e1, const tl_equation* e2, const tl_equation* e3,
+                          bool* done) {
+    *done = false;
+    if (getenv("TL_NO_FUSED_HEAD")) return TL_OK;
+    if (e1->accum != TL_ACC_ASSIGN || e2->accum != TL_ACC_ASSIGN || e3->accum != TL_ACC_ASSIGN) return TL_OK;
+    auto name_is = [](const tl_index& ix, const char* n) { return !strcmp(ix.name, n); };
+    auto plain = [](const tl_ref& r) {
+        if (r.rank != 2) return false;
+        for (int k = 0; k < 2; ++k)
+            if (r.idx[k].kind != TL_IX_NAME) return false;
+        return true;
+    };
+    // e3: Y[b, o.] = softmax(Z[b, o])
+    if (e3->n_refs != 1 || e3->n_code != 2 || e3->code[0].op != TL_OP_REF || e3->code[0].arg != 0 ||
+        e3->code[1].op != TL_OP_NL || e3->code[1].arg != TL_NL_SOFTMAX)
+        return TL_OK;
+    const tl_ref& rz = e3->refs[0];
+    if (!plain(rz) || e3->lhs.rank != 2 || e3->lhs.idx[0].kind != TL_IX_NAME ||
+        (e3->lhs.idx[1].kind != TL_IX_NAME && e3->lhs.idx[1].kind != TL_IX_NORMALIZE))
+        return TL_OK;
+    const char* bn = rz.idx[0].name;
+    const char* on = rz.idx[1].name;
+    if (!strcmp(bn, on) || !name_is(e3->lhs.idx[0], bn) || !name_is(e3->lhs.idx[1], on)) return TL_OK;
+    // e2: Z[b, o] = H[b, h] W2[h, o] s2
+    GemmMatch m1, m2;
+    if (!match_product2(e2, &m2) || m2.relu_term || !plain(e2->lhs) || strcmp(e2->lhs.tensor, rz.tensor) ||
+        !name_is(e2->lhs.idx[0], bn) || !name_is(e2->lhs.idx[1], on))
+        return TL_OK;
+    const tl_ref* rh = &e2->refs[m2.ref_a];
+    const tl_ref* rw2 = &e2->refs[m2.ref_b];
+    if (strcmp(rh->tensor, e1->lhs.tensor)) std::swap(rh, rw2);
+    if (!plain(*rh) || !plain(*rw2) || strcmp(rh->tensor, e1->lhs.tensor) || !name_is(rh->idx[0], bn)) return TL_OK;
+    const char* hn = rh->idx[1].name;
+    if (!name_is(rw2->idx[0], hn) || !name_is(rw2->idx[1], on) || !strcmp(hn, bn) || !strcmp(hn, on)) return TL_OK;
+    // e1: H[b, h] = [relu](X[b, i] W1[i, h] s1)
+    if (!match_product2(e1, &m1) || !plain(e1->lhs) || !name_is(e1->lhs.idx[0], bn) || !name_is(e1->lhs.idx[1], hn))
+        return TL_OK;
+    const tl_ref* rx = &e1->refs[m1.ref_a];
+    const tl_ref* rw1 = &e1->refs[m1.ref_b];
+    if (!plain(*rx) || !plain(*rw1)) return TL_OK;
+    if (!name_is(rx->idx[0], bn)) std::swap(rx, rw1);
+    if (!name_is(rx->idx[0], bn)) return TL_OK;
+    const char* in = rx->idx[1].name;
+    if (!name_is(rw1->idx[0], in) || !name_is(rw1->idx[1], hn) || !strcmp(in, bn) || !strcmp(in, hn) ||
+        !strcmp(in, on))
+        return TL_OK;
+    const int64_t nb = domain_size(c, bn), ni = domain_size(c, in), nh = domain_size(c, hn), no = domain_size(c, on);
+    // (X's chunk of a block, at most 64 rows x 192 contracted indices, fits
+    // 48 KB of shared memory; a row of H fits 200 KB)
+    if (nb < 1 || nb > kHeadMaxRows || no < 1 || no > kHeadMaxCols || ni < 1 || ni > 12288 || nh < 1 ||
+        nh > 50 * 1024)
+        return TL_OK;
+    // inputs defined, outputs distinct, fresh and not read by these statements
+    const char* outs[3] = {e1->lhs.tensor, e2->lhs.tensor, e3->lhs.tensor};
+    const char* ins[3] = {rx->tensor, rw1->tensor, rw2->tensor};
+    for (int i = 0; i < 3; ++i) {
+        for (int j = 0; j < 3; ++j)
+            if (!strcmp(outs[i], ins[j]) || (i != j && !strcmp(outs[i], outs[j]))) return TL_OK;
+        if (std::find(c->sign_sensitive.begin(), c->sign_sensitive.end(), std::string(outs[i])) !=
+            c->sign_sensitive.end())
+            return TL_OK;
+    }
+    Tensor* tx = find_defined(c, rx->tensor);
+    Tensor* tw1 = find_defined(c, rw1->tensor);
+    Tensor* tw2 = find_defined(c, rw2->tensor);
+    auto shape_ok = [](const Tensor* t, int64_t r, int64_t cl) {
+        return t && t->rank == 2 && t->dims[0] == r && t->dims[1] == cl && t->shard != TL_SHARD_ROWS;
+    };
+    if (!shape_ok(tx, nb, ni) || !shape_ok(tw1, ni, nh) || !shape_ok(tw2, nh, no)) return TL_OK;
+    Tensor* out[3];
+    for (int i = 0; i < 3; ++i) {
+        const tl_equation* e = i == 0 ? e1 : i == 1 ? e2 : e3;
+        out[i] = find_defined(c, outs[i]);
+        if (!out[i]) TL_TRY(allocate_tensor(c, e->lhs.tensor, e->lhs.idx, e->lhs.rank, &out[i]));
+    }
+    if (!shape_ok(out[0], nb, nh) || !shape_ok(out[1], nb, no) || !shape_ok(out[2], nb, no) || !out[0]->zero ||
+        !out[1]->zero)
+        return TL_OK;
+    tl_status st;
+    HeadPlan p{};
+    p.X = read_ptr(c, tx, &st); TL_TRY(st);
+    p.W1 = read_ptr(c, tw1, &st); TL_TRY(st);
+    p.W2 = read_ptr(c, tw2, &st); TL_TRY(st);
+    if (!p.X || !p.W1 || !p.W2) return TL_OK;   // a zero operand: the one-by-one path keeps its meaning
+    for (int i = 0; i < 3; ++i) TL_TRY(alloc_dense_public(c, out[i]));
+    p.H = out[0]->dense;
+    p.Z = out[1]->dense;
+    p.Y = out[2]->dense;
+    p.b = nb; p.i = ni; p.h = nh; p.o = no;
+    p.relu_term = m1.relu_term ? 1 : 0;
+    p.sgn1 = m1.relu_term && m1.scale < 0.f ? -1.f : 1.f;
+    p.mag1 = m1.relu_term ? fabsf(m1.scale) : m1.scale;
+    p.s2 = m2.scale;
+    TL_TRY(launch_head(c, p));
+    for (int i = 0; i < 3; ++i) {
+        mark_written_dense(out[i]);
+        out[i]->boolean = false;
+    }
+    out[0]->nonneg = m1.relu_term;   // a sum of relus times |s1|
+    out[2]->nonneg = true;           // a softmax
+    *done = true;
+    return TL_OK;
+}
+
 // The statements of a run in order (non-recursive equations, declarations,
 // loads, backward); recursive equations are collected into `rec`.
 static tl_status run_statements(tl_ctx* c, const tl_statement* s, int n, const std::vector<tl_equation>& eqs,
@@ -1316,6 +1424,7 @@ static tl_status run_statements(tl_ctx* c, const tl_statement* s, int n, const s
                     TL_TRY(validate_code(c, &s[i + 1].eq));
                     TL_TRY(validate_code(c, &s[i + 2].eq));
                     TL_TRY(try_attention(c, &st->eq, &s[i + 1].eq, &s[i + 2].eq, &fused));
+                    if (!fused) TL_TRY(try_head(c, &st->eq, &s[i + 1].eq, &s[i + 2].eq, &fused));
                     if (fused) {
                         i += 2;
                         break;

@@ -367,6 +367,23 @@ struct AttnPlan {
     float scale;
 };
 tl_status launch_attention(tl_ctx* c, const AttnPlan& p);
+// A small-batch head, H = [relu per term](s1 X W1), Z = s2 H W2, Y = softmax
+// over the columns of Z: row-major fp32, b <= kHeadMaxRows rows, o <=
+// kHeadMaxCols columns of Z (k_head.cu)
+constexpr int kHeadMaxRows = 64, kHeadMaxCols = 32;
+struct HeadPlan {
+    const float *X, *W1, *W2;
+    float *H, *Z, *Y;
+    int64_t b, i, h, o;
+    int relu_term;
+    float sgn1, mag1;     // relu per term: relu(s1 t) = |s1| relu(sign(s1) t); else mag1 = s1
+    float s2;
+    // set by the launch: partial H of ks chunks of kc contracted indices
+    float* hpart;
+    int ks;
+    int64_t kc;
+};
+tl_status launch_head(tl_ctx* c, HeadPlan p);
 
 // Before a SpMM reads rows other ranks fanned out into P: per writing rank
 // the count its tiles must have reached in this rank's counter array (0:

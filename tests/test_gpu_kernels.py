@@ -370,6 +370,38 @@ def test_attention_block_accumulating_scores(ctx, oracle_lib):
         assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
 
 
+HEAD_CASES = [(32, 784, 256, 10, "relu(X[b,i] W1[i,h])"), (64, 20, 100, 32, "relu(X[b,i] W1[i,h] / 4)"),
+              (1, 300, 33, 1, "X[b,i] W1[i,h]"), (17, 1024, 600, 7, "relu(X[b,i] W1[i,h])")]
+
+
+@pytest.mark.parametrize("b,i,h,o,first", HEAD_CASES, ids=[f"b{c[0]}-i{c[1]}-h{c[2]}-o{c[3]}" for c in HEAD_CASES])
+def test_small_batch_head(ctx, oracle_lib, monkeypatch, b, i, h, o, first):
+    # H = [relu per term](X W1), Z = H W2, Y = softmax(Z) at batch <= 64 runs
+    # as two launches (k_head_h, k_head_zy); all three tensors against the
+    # oracle, and against the statement-by-statement kernels
+    src = (f"domain b: {b}\ndomain i: {i}\ndomain h: {h}\ndomain o: {o}\n"
+           "X[b,i] = 0\nload X \"x.bin\"\nW1[i,h] = 0\nload W1 \"w1.bin\"\nW2[h,o] = 0\nload W2 \"w2.bin\"\n"
+           f"H[b,h] = {first}\nZ[b,o] = H[b,h] W2[h,o]\nY[b,o.] = softmax(Z[b,o])\n")
+    rng = np.random.default_rng(b * 7 + i)
+    data = {"X": rng.uniform(-1, 1, (b, i)), "W1": rng.normal(0, np.sqrt(2 / i), (i, h)),
+            "W2": rng.normal(0, np.sqrt(2 / h), (h, o))}
+    p = lang.Program(src, inputs=data)
+    ctx.profile(True)
+    ctx.profile_reset()
+    ctx.run(p)
+    ctx.sync()
+    assert ctx.profile_read().get("head_hidden", {}).get("launches", 0) == 1
+    ctx.profile(False)
+    fused = {n: ctx.tensor(n) for n in ("H", "Z", "Y")}
+    ref = oracle_lib.OracleRun(p)
+    for n in ("H", "Z", "Y"):
+        assert_close(fused[n], ref.tensor(n), TOL_FP32, n)
+    monkeypatch.setenv("TL_NO_FUSED_HEAD", "1")
+    ctx.run(p)
+    for n in ("H", "Z", "Y"):
+        assert_close(fused[n], ctx.tensor(n), TOL_FP32, n + " (one statement at a time)")
+
+
 @pytest.mark.parametrize("signs", ["x_nonneg", "w_nonneg", "mixed"])
 def test_relu_per_term_with_a_nonnegative_operand(ctx, oracle_lib, signs):
     # relu(x w) per term needs both sign halves of x and w (K doubled) unless
