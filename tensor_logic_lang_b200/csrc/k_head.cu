@@ -44,6 +44,12 @@ __global__ void __launch_bounds__(HD_THREADS) k_head_h(const HeadPlan p) {
     const int64_t k0 = (int64_t)blockIdx.y * p.kc;
     const int kn = (int)std::min<int64_t>(p.kc, p.i - k0);
     const int nx = (int)p.b * kn;
+    const bool in = col < p.h;
+    const float* w1 = p.W1 + k0 * p.h + col;
+    // the first round of W1 is in flight while X is staged
+    float wv[HD_KB];
+#pragma unroll
+    for (int u = 0; u < HD_KB; ++u) wv[u] = (in && u < kn) ? w1[(int64_t)u * p.h] : 0.f;
     for (int t0 = 0; t0 < nx; t0 += HD_THREADS * HD_XPT) {
         float v[HD_XPT];
 #pragma unroll
@@ -62,12 +68,11 @@ __global__ void __launch_bounds__(HD_THREADS) k_head_h(const HeadPlan p) {
     float acc[HD_RPW];
 #pragma unroll
     for (int j = 0; j < HD_RPW; ++j) acc[j] = 0.f;
-    const bool in = col < p.h;
-    const float* w1 = p.W1 + k0 * p.h + col;
     for (int ks0 = 0; ks0 < kn; ks0 += HD_KB) {
-        float wv[HD_KB];
+        if (ks0 > 0) {
 #pragma unroll
-        for (int u = 0; u < HD_KB; ++u) wv[u] = (in && ks0 + u < kn) ? w1[(int64_t)(ks0 + u) * p.h] : 0.f;
+            for (int u = 0; u < HD_KB; ++u) wv[u] = (in && ks0 + u < kn) ? w1[(int64_t)(ks0 + u) * p.h] : 0.f;
+        }
 #pragma unroll
         for (int j = 0; j < HD_RPW; ++j) {
             const int r = w + 8 * j;
@@ -104,6 +109,18 @@ __global__ void __launch_bounds__(HD_THREADS) k_head_zy(const HeadPlan p) {
     const int64_t r = blockIdx.x;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t stride = p.b * p.h;   // between the chunks' partials of one element
+    // this warp's columns of Z are o = w, w + 8, w + 16, w + 24: their first
+    // 256 rows of W2 are in flight while the partials are added
+    constexpr int OPW = kHeadMaxCols / 8;
+    float w2[OPW][8];
+#pragma unroll
+    for (int q = 0; q < OPW; ++q)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int o = w + 8 * q;
+            const int64_t c = u * 32 + lane;
+            w2[q][u] = (o < p.o && c < p.h) ? p.W2[c * p.o + o] : 0.f;
+        }
     for (int64_t c = threadIdx.x; c < p.h; c += HD_THREADS) {
         const float* src = p.hpart + r * p.h + c;
         float v = 0.f;
@@ -119,14 +136,17 @@ __global__ void __launch_bounds__(HD_THREADS) k_head_zy(const HeadPlan p) {
         p.H[r * p.h + c] = v;
     }
     __syncthreads();
-    for (int o = w; o < p.o; o += 8) {
+#pragma unroll
+    for (int q = 0; q < OPW; ++q) {
+        const int o = w + 8 * q;
+        if (o >= p.o) break;
         float s = 0.f;
         for (int64_t c0 = 0; c0 < p.h; c0 += 32 * 8) {
             float wv[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 const int64_t c = c0 + u * 32 + lane;
-                wv[u] = c < p.h ? p.W2[c * p.o + o] : 0.f;
+                wv[u] = c0 == 0 ? w2[q][u] : (c < p.h ? p.W2[c * p.o + o] : 0.f);
             }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
