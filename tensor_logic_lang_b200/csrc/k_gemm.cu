@@ -1087,14 +1087,35 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
 // A warp per query row: the key tiles' statistics combined (m*, l*), the row
 // of O (lane l: columns 2l, 2l + 1), then the row of A = exp(S - m*) / l*
 // from the scores the tile kernel stored (n_k a multiple of 4; 128-bit loads
-// and stores, 8 in flight per lane).
+// and stores).  The row's first 1024 scores and first 16 tiles' partials are
+// loaded with its statistics, in one memory round trip; the rest 8 loads per
+// lane at a time.
 __global__ void __launch_bounds__(256)
     k_attn_rows(const float* __restrict__ opart, const float* __restrict__ mpart, const float* __restrict__ lpart,
                 int n_kt, int64_t n_q, float* __restrict__ O, int64_t lo, const float* __restrict__ S,
                 float* __restrict__ A, int64_t n_k) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t q4 = n_k / 4;
     for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_q; r += warps) {
+        const float4* Sr = reinterpret_cast<const float4*>(S + r * n_k);
+        float4* Ar = reinterpret_cast<float4*>(A + r * n_k);
+        // the row's first 1024 scores and its first 16 tiles' O and maxima are
+        // loaded together with the statistics below: one memory round trip
+        float4 sv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int64_t j = lane + 32 * u;
+            sv[u] = j < q4 ? Sr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float w0[16];
+        float2 v0[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            w0[u] = u < n_kt ? mpart[u * n_q + r] : -INFINITY;
+            v0[u] = u < n_kt ? *reinterpret_cast<const float2*>(opart + (u * n_q + r) * AT_D + 2 * lane)
+                             : make_float2(0.f, 0.f);
+        }
         float m = -INFINITY, lt = 0.f;
         for (int t = lane; t < n_kt; t += 32) {
             const float mt = mpart[t * n_q + r];
@@ -1111,9 +1132,15 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
         const float inv = 1.0f / l;
-        // 8 tiles' loads in flight at a time
         float o0 = 0.f, o1 = 0.f;
-        for (int t0 = 0; t0 < n_kt; t0 += 8) {
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            const float e = __expf(w0[u] - mstar);
+            o0 = fmaf(e, v0[u].x, o0);
+            o1 = fmaf(e, v0[u].y, o1);
+        }
+        // tiles past the first 16, 8 tiles' loads in flight at a time
+        for (int t0 = 16; t0 < n_kt; t0 += 8) {
             float w[8];
             float2 v[8];
 #pragma unroll
@@ -1131,10 +1158,14 @@ __global__ void __launch_bounds__(256)
             }
         }
         *reinterpret_cast<float2*>(O + r * lo + 2 * lane) = make_float2(o0 * inv, o1 * inv);
-        const int64_t q4 = n_k / 4;
-        const float4* Sr = reinterpret_cast<const float4*>(S + r * n_k);
-        float4* Ar = reinterpret_cast<float4*>(A + r * n_k);
-        for (int64_t j0 = lane; j0 < q4; j0 += 32 * 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int64_t j = lane + 32 * u;
+            if (j < q4)
+                Ar[j] = make_float4(__expf(sv[u].x - mstar) * inv, __expf(sv[u].y - mstar) * inv,
+                                    __expf(sv[u].z - mstar) * inv, __expf(sv[u].w - mstar) * inv);
+        }
+        for (int64_t j0 = lane + 32 * 8; j0 < q4; j0 += 32 * 8) {
             float4 v[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
