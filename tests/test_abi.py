@@ -52,6 +52,35 @@ def test_struct_layout_matches_c(tmp_path):
     assert got == want
 
 
+def header_defines():
+    text = open(HEADER).read()
+    return {m.group(1): int(m.group(2)) for m in re.finditer(r"^#define (TL_[A-Z0-9_]+)\s+(-?\d+)", text, re.M)}
+
+
+def test_header_constants_match_the_python_mirror():
+    # every numeric #define of the header against abi.py's copy
+    d = header_defines()
+    py = {k: getattr(abi, k) for k in dir(abi) if k.startswith("TL_") and isinstance(getattr(abi, k), int)}
+    prefixed = {"TL_IX_": "IX_", "TL_OP_": "OP_", "TL_STMT_": "STMT_", "TL_PREC_": "PREC_", "TL_SHARD_": "SHARD_"}
+    for k, v in d.items():
+        if k in py:
+            assert py[k] == v, k
+            continue
+        for hp, pp in prefixed.items():
+            if k.startswith(hp):
+                assert getattr(abi, pp + k[len(hp):]) == v, k
+                break
+        else:
+            if k.startswith("TL_NL_"):
+                assert abi.NL[k[len("TL_NL_"):].lower()] == v, k
+            elif k.startswith("TL_ACC_"):
+                sym = {"ASSIGN": "=", "ADD": "+=", "MUL": "*=", "MAX": "max=", "MIN": "min=", "AVG": "avg="}
+                assert abi.ACC[sym[k[len("TL_ACC_"):]]] == v, k
+            else:
+                raise AssertionError(f"{k} has no Python mirror")
+    assert d["TL_SHARD_COLS"] == abi.SHARD_COLS == 2
+
+
 def test_default_opts(lib):
     o = abi.InitOpts()
     lib.tl_default_opts(C.byref(o))
