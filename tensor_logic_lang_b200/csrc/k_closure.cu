@@ -598,15 +598,27 @@ __device__ __forceinline__ bool search_row(const FixArgs& a, RowSearch& S, bool 
 // step, ascending); true if a row grew.  Lazy rows start empty with their own
 // node queued.  budget > 0: a row still open after that many queued bits is
 // handed to the block's team (the row stays unwritten and pending).
+// split: the warps take 32 rows each in turn instead (warp g: rows 32 g, then
+// 32 (g + warps), ...), with no counter: for the sweeps after a shortcut sweep,
+// which find every row closed (or the few a team left) and only read the
+// pending words, so the counter's atomics would be most of their time.
 __device__ __forceinline__ bool close_rows(const FixArgs& a, unsigned long long* next_row, int grab, bool lazy,
-                                           int budget, uint32_t* row, uint32_t* spill, uint32_t* q, int lane) {
+                                           int budget, uint32_t* row, uint32_t* spill, uint32_t* q, int lane,
+                                           bool split = false) {
     const int64_t words = a.words;
     const bool vec = (words & 3) == 0;
     bool any = false;
-    for (;;) {
+    const int64_t wg = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    if (split) grab = 32;
+    for (int64_t it = 0;; ++it) {
         unsigned long long base = 0;
-        if (lane == 0) base = atomicAdd(next_row, (unsigned long long)grab);
-        base = __shfl_sync(0xffffffffu, base, 0);
+        if (split) {
+            base = (unsigned long long)((wg + it * nw) * 32);
+        } else {
+            if (lane == 0) base = atomicAdd(next_row, (unsigned long long)grab);
+            base = __shfl_sync(0xffffffffu, base, 0);
+        }
         if ((int64_t)base >= a.rows) break;
         const int64_t mine = (int64_t)base + lane;
         const int32_t my_pend = (lane < grab && mine < a.rows) ? a.pending[mine] : INT32_MAX;
@@ -1182,7 +1194,7 @@ __global__ void __launch_bounds__(32 * kFixWarps, 2) k_closure_fix(const FixArgs
                                                                  a.dp_copy || PEER || COLS ? 0 : budget, row,
                                               spill, q, lane)
                               : close_rows(a, &a.st->next_row[s & 1], s == 0 ? 1 : 32, lazy, budget, row, spill, q,
-                                           lane);
+                                           lane, s > 0 && a.lazy && a.shortcut);
         if (lane == 0 && grew) *(volatile int*)&a.st->changed[s & 1] = 1;
         if (COLS && lazy && blockIdx.x == 0 && threadIdx.x == 0 && *(volatile const int*)a.two_hop)
             *(volatile int*)&a.st->changed[s & 1] = 1;
