@@ -490,23 +490,29 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int BN>
+// NSEG = 2 (3xTF32 as hi/lo pairs): a stage holds the hi and lo tiles of A
+// and of B for one k-block, and the MMA warp issues hi*hi, hi*lo and lo*hi.
+template <int BN, int NSEG = 1>
 struct TcCfg {
-    static constexpr int A_BYTES = TC_BM * TC_BK * 4;      // 16 KB
+    static constexpr int A_BYTES = TC_BM * TC_BK * 4;      // 16 KB per segment
     static constexpr int B_BYTES = BN * TC_BK * 4;
-    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int STAGE = NSEG * (A_BYTES + B_BYTES);
     static constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
     static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
     static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 // A_MN / B_MN: operand stored MN-major (M or N is the contiguous dim).
-template <int BN, bool A_MN, bool B_MN>
+// P3 (3xTF32): tmA / tmB map the hi copies and tmA1 / tmB1 the lo copies,
+// each K long (zeros past it); every k-block of K takes three products.
+template <int BN, bool A_MN, bool B_MN, bool P3>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+              const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
               const __grid_constant__ TcEpi epi, int num_kb, int kb_per_split, int tma_store) {
-    using Cfg = TcCfg<BN>;
+    constexpr int NSEG = P3 ? 2 : 1;
+    using Cfg = TcCfg<BN, NSEG>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE);
@@ -545,21 +551,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int s = kb % Cfg::STAGES;
                 const uint32_t ph = (kb / Cfg::STAGES) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, epi.err)) break;
-                uint8_t* sa = smem + s * Cfg::STAGE;
-                uint8_t* sb = sa + Cfg::A_BYTES;
+                uint8_t* stage = smem + s * Cfg::STAGE;
                 mbar_expect_tx(&full[s], Cfg::STAGE);
                 const int k0 = (kb_first + kb) * TC_BK;
-                if (!A_MN) {
-                    tma_load_2d(sa, &tmA, &full[s], k0, m0);
-                } else {
 #pragma unroll
-                    for (int j = 0; j < TC_BM / 32; ++j) tma_load_2d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, k0);
-                }
-                if (!B_MN) {
-                    tma_load_2d(sb, &tmB, &full[s], k0, n0);
-                } else {
+                for (int g = 0; g < NSEG; ++g) {
+                    uint8_t* sa = stage + g * Cfg::A_BYTES;
+                    uint8_t* sb = stage + NSEG * Cfg::A_BYTES + g * Cfg::B_BYTES;
+                    const CUtensorMap* ma = g ? &tmA1 : &tmA;
+                    const CUtensorMap* mb = g ? &tmB1 : &tmB;
+                    if (!A_MN) {
+                        tma_load_2d(sa, ma, &full[s], k0, m0);
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, k0);
+                        for (int j = 0; j < TC_BM / 32; ++j) tma_load_2d(sa + j * 4096, ma, &full[s], m0 + 32 * j, k0);
+                    }
+                    if (!B_MN) {
+                        tma_load_2d(sb, mb, &full[s], k0, n0);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * 4096, mb, &full[s], n0 + 32 * j, k0);
+                    }
                 }
             }
         }
@@ -578,18 +590,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (lane == 0) {
-                const uint32_t sa = smem_u32(smem + s * Cfg::STAGE);
-                const uint32_t sb = sa + Cfg::A_BYTES;
+                const uint32_t stage = smem_u32(smem + s * Cfg::STAGE);
+                // (A segment, B segment) products: one, or hi*hi, hi*lo, lo*hi
+                constexpr int NP = P3 ? 3 : 1;
 #pragma unroll
-                for (int kk = 0; kk < TC_BK / 8; ++kk) {
-                    // K-major: advance 32 bytes inside the swizzled 128-byte row; SBO = 8 rows.
-                    // MN-major: 8 K rows of 128 bytes per MMA (two 4-row 32B-atom groups,
-                    // SBO = 512 bytes); LBO = the next 32-wide MN chunk (one 4 KB box).
-                    const uint64_t ad = A_MN ? umma_desc(sa + kk * 1024, 4096, 512, kLayoutSW128Base32B)
-                                             : umma_desc(sa + kk * 32, 16, 1024, kLayoutSW128);
-                    const uint64_t bd = B_MN ? umma_desc(sb + kk * 1024, 4096, 512, kLayoutSW128Base32B)
-                                             : umma_desc(sb + kk * 32, 16, 1024, kLayoutSW128);
-                    umma_tf32(tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                for (int pr = 0; pr < NP; ++pr) {
+                    const int ga = pr == 2 ? 1 : 0, gb = pr == 1 ? 1 : 0;
+                    const uint32_t sa = stage + ga * Cfg::A_BYTES;
+                    const uint32_t sb = stage + NSEG * Cfg::A_BYTES + gb * Cfg::B_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 8; ++kk) {
+                        // K-major: advance 32 bytes inside the swizzled 128-byte row; SBO = 8 rows.
+                        // MN-major: 8 K rows of 128 bytes per MMA (two 4-row 32B-atom groups,
+                        // SBO = 512 bytes); LBO = the next 32-wide MN chunk (one 4 KB box).
+                        const uint64_t ad = A_MN ? umma_desc(sa + kk * 1024, 4096, 512, kLayoutSW128Base32B)
+                                                 : umma_desc(sa + kk * 32, 16, 1024, kLayoutSW128);
+                        const uint64_t bd = B_MN ? umma_desc(sb + kk * 1024, 4096, 512, kLayoutSW128Base32B)
+                                                 : umma_desc(sb + kk * 32, 16, 1024, kLayoutSW128);
+                        umma_tf32(tmem, ad, bd, idesc, (kb > 0 || pr > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
                 umma_commit(&empty[s]);
             }
@@ -1233,33 +1252,43 @@ bool make_store_map(CUtensorMap* map, const float* base, int64_t cols, int64_t r
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, bool AM, bool BM>
+template <int BN, bool AM, bool BM, bool P3>
 tl_status launch_tc_inst(tl_ctx* c, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
-                         const CUtensorMap& md, int tma_store, const TcEpi& e, int64_t M, int64_t N, int num_kb,
-                         int kb_per_split, int splits) {
-    using Cfg = TcCfg<BN>;
+                         const CUtensorMap& md, const CUtensorMap& ma1, const CUtensorMap& mb1, int tma_store,
+                         const TcEpi& e, int64_t M, int64_t N, int num_kb, int kb_per_split, int splits) {
+    using Cfg = TcCfg<BN, P3 ? 2 : 1>;
+    static_assert(Cfg::STAGES >= 2, "two stages in flight");
     static bool attr_set = false;
     if (!attr_set) {
-        if (cudaFuncSetAttribute(k_gemm_tc<BN, AM, BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) !=
+        if (cudaFuncSetAttribute(k_gemm_tc<BN, AM, BM, P3>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) !=
             cudaSuccess)
             return fail(c, TL_ERR_CUDA, "cannot reserve %d bytes of shared memory", Cfg::SMEM);
         attr_set = true;
     }
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + TC_BM - 1) / TC_BM), (unsigned)splits);
     static_assert(Cfg::STAGES * Cfg::STAGE >= 4 * 16384, "epilogue tiles fit in the stage memory");
-    k_gemm_tc<BN, AM, BM><<<grid, TC_THREADS, Cfg::SMEM, c->stream>>>(ma, mb, mc, md, e, num_kb, kb_per_split,
-                                                                      tma_store);
+    k_gemm_tc<BN, AM, BM, P3><<<grid, TC_THREADS, Cfg::SMEM, c->stream>>>(ma, mb, mc, md, ma1, mb1, e, num_kb,
+                                                                          kb_per_split, tma_store);
     return TL_OK;
 }
 
 template <int BN>
-tl_status launch_tc_bn(tl_ctx* c, bool am, bool bm, const CUtensorMap& ma, const CUtensorMap& mb,
-                       const CUtensorMap& mc, const CUtensorMap& md, int ts, const TcEpi& e, int64_t M, int64_t N,
-                       int num_kb, int kb_per_split, int splits) {
-    if (!am && !bm) return launch_tc_inst<BN, false, false>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
-    if (am && !bm) return launch_tc_inst<BN, true, false>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
-    if (!am && bm) return launch_tc_inst<BN, false, true>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
-    return launch_tc_inst<BN, true, true>(c, ma, mb, mc, md, ts, e, M, N, num_kb, kb_per_split, splits);
+tl_status launch_tc_bn(tl_ctx* c, bool am, bool bm, bool p3, const CUtensorMap& ma, const CUtensorMap& mb,
+                       const CUtensorMap& mc, const CUtensorMap& md, const CUtensorMap& ma1, const CUtensorMap& mb1,
+                       int ts, const TcEpi& e, int64_t M, int64_t N, int num_kb, int kb_per_split, int splits) {
+#define TL_TC_INST(AMV, BMV, P3V) \
+    launch_tc_inst<BN, AMV, BMV, P3V>(c, ma, mb, mc, md, ma1, mb1, ts, e, M, N, num_kb, kb_per_split, splits)
+    if (p3) {
+        if (!am && !bm) return TL_TC_INST(false, false, true);
+        if (am && !bm) return TL_TC_INST(true, false, true);
+        if (!am && bm) return TL_TC_INST(false, true, true);
+        return TL_TC_INST(true, true, true);
+    }
+    if (!am && !bm) return TL_TC_INST(false, false, false);
+    if (am && !bm) return TL_TC_INST(true, false, false);
+    if (!am && bm) return TL_TC_INST(false, true, false);
+    return TL_TC_INST(true, true, false);
+#undef TL_TC_INST
 }
 
 // Tile width of the tensor-core GEMM for N output columns.
@@ -1470,9 +1499,15 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     // with b >= 0 it is (s a)+ b: one K segment instead of two
     const bool one_a = split && p.a_nonneg, one_b = split && !one_a && p.b_nonneg;
     const bool split2 = split && !one_a && !one_b;
-    const int nseg = split2 ? 2 : precise ? 3 : 1;
-    const unsigned ops_a = split2 ? (OP_POS | OP_NEG << 4) : one_b ? OP_POS : precise ? (OP_RN | OP_RN << 4 | OP_LO << 8) : OP_RN;
-    const unsigned ops_b = split2 ? (OP_POS | OP_NEG << 4) : one_a ? OP_POS : precise ? (OP_RN | OP_LO << 4 | OP_RN << 8) : OP_RN;
+    // 3xTF32 as hi/lo copies of A and B, K each (the stage pairs them:
+    // hi*hi + hi*lo + lo*hi), when every segment starts on a 16-byte boundary;
+    // else three concatenated segments [hi, hi, lo] x [hi, lo, hi]
+    const bool p3 = precise && p.K % 4 == 0 && !env_flag("TL_GEMM_NO_PAIRS");
+    const int nseg = split2 ? 2 : p3 ? 2 : precise ? 3 : 1;
+    const unsigned ops_a = split2 ? (OP_POS | OP_NEG << 4) : one_b ? OP_POS : p3 ? (OP_RN | OP_LO << 4)
+                           : precise ? (OP_RN | OP_RN << 4 | OP_LO << 8) : OP_RN;
+    const unsigned ops_b = split2 ? (OP_POS | OP_NEG << 4) : one_a ? OP_POS : p3 ? (OP_RN | OP_LO << 4)
+                           : precise ? (OP_RN | OP_LO << 4 | OP_RN << 8) : OP_RN;
     const int64_t Ke = nseg * p.K;
     struct Prep { int64_t R, s_r, s_k; unsigned ops; float sgn; bool mn; int64_t ld; float* dst; const char* name; };
     Prep pa{p.M, p.sam, p.sak, ops_a, one_b ? sgn : 1.f, use_mn && p.sak != 1 && p.sam == 1, 0, nullptr, "gemm_prep_a"};
@@ -1533,14 +1568,26 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
         TL_TRY(L.done());
     }
     // the maps span Ke; TMA reads zeros past it (the K tail of the last block)
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, ma1, mb1;
+    memset(&ma1, 0, sizeof ma1);
+    memset(&mb1, 0, sizeof mb1);
     // the tile width depends on N alone, so every rank can count another
     // rank's fanned-out tiles (gemm_fan_tiles)
     const int BN = tc_tile_n(p.N);
-    bool ok = pa.mn ? make_map(&ma, pa.dst, p.M, Ke, pa.ld, 32, true) : make_map(&ma, pa.dst, Ke, p.M, pa.ld, TC_BM, false);
-    ok = ok && (pb.mn ? make_map(&mb, pb.dst, p.N, Ke, pb.ld, 32, true) : make_map(&mb, pb.dst, Ke, p.N, pb.ld, BN, false));
+    // p3: one map per copy, K long, so a k-block past K reads zeros instead
+    // of the next copy; the lo copy starts K (K-major: columns, MN-major: rows) on
+    const int64_t kx = p3 ? p.K : Ke;
+    auto seg = [&](const Prep& q, int g) { return q.dst + (int64_t)g * p.K * (q.mn ? q.ld : 1); };
+    bool ok = pa.mn ? make_map(&ma, pa.dst, p.M, kx, pa.ld, 32, true) : make_map(&ma, pa.dst, kx, p.M, pa.ld, TC_BM, false);
+    ok = ok && (pb.mn ? make_map(&mb, pb.dst, p.N, kx, pb.ld, 32, true) : make_map(&mb, pb.dst, kx, p.N, pb.ld, BN, false));
+    if (p3) {
+        ok = ok && (pa.mn ? make_map(&ma1, seg(pa, 1), p.M, p.K, pa.ld, 32, true)
+                          : make_map(&ma1, seg(pa, 1), p.K, p.M, pa.ld, TC_BM, false));
+        ok = ok && (pb.mn ? make_map(&mb1, seg(pb, 1), p.N, p.K, pb.ld, 32, true)
+                          : make_map(&mb1, seg(pb, 1), p.K, p.N, pb.ld, BN, false));
+    }
     if (!ok) return launch_simt(c, p);
-    const int num_kb = (int)((Ke + TC_BK - 1) / TC_BK);
+    const int num_kb = (int)((kx + TC_BK - 1) / TC_BK);
     // split K only when the output tiles fill less than half of the SMs (each
     // split >= 4 k-blocks): the atomic epilogue of a split costs more than the
     // idle SMs of a grid that is already half a wave or more
@@ -1591,9 +1638,9 @@ tl_status launch_gemm(tl_ctx* c, const GemmPlan& p) {
     if (p.fan_n && !ts) return fail(c, TL_ERR_UNSUPPORTED, "fanned-out GEMM needs the TMA-store epilogue");
     LaunchScope L(c, "gemm_tcgen05_tf32", (double)(p.M * p.K + p.K * p.N + p.M * p.N * (1 + p.beta)) * 4.0,
                   2.0 * p.M * p.N * p.K);
-    if (BN == 256) TL_TRY(launch_tc_bn<256>(c, pa.mn, pb.mn, ma, mb, mc, md, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
-    else if (BN == 128) TL_TRY(launch_tc_bn<128>(c, pa.mn, pb.mn, ma, mb, mc, md, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
-    else TL_TRY(launch_tc_bn<64>(c, pa.mn, pb.mn, ma, mb, mc, md, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
+    if (BN == 256) TL_TRY(launch_tc_bn<256>(c, pa.mn, pb.mn, p3, ma, mb, mc, md, ma1, mb1, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
+    else if (BN == 128) TL_TRY(launch_tc_bn<128>(c, pa.mn, pb.mn, p3, ma, mb, mc, md, ma1, mb1, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
+    else TL_TRY(launch_tc_bn<64>(c, pa.mn, pb.mn, p3, ma, mb, mc, md, ma1, mb1, ts, e, p.M, p.N, num_kb, kb_per_split, splits));
     return L.done();
 }
 

@@ -370,6 +370,25 @@ def test_attention_block_accumulating_scores(ctx, oracle_lib):
         assert_close(ctx.tensor(n), ref.tensor(n), TOL_TF32, n)
 
 
+@pytest.mark.parametrize("i", [256, 250], ids=["pairs", "k_not_mult_4"])
+def test_fp32_class_gemm_hi_lo_pairs(ctx, oracle_lib, monkeypatch, i):
+    # Z1's sign feeds relu's gradient, so Z1 runs as 3xTF32: hi*hi + hi*lo +
+    # lo*hi.  With K a multiple of 4 a stage holds the hi and lo tiles of A and
+    # B and takes the three products (TL_GEMM_NO_PAIRS=1: three concatenated
+    # segments instead); both against the oracle and against each other
+    from tensor_logic_lang_b200 import configs
+    p, _, _, _ = configs.program(configs.mlp_train, b=256, i=i, h=1024, o=10)
+    ctx.run(p)
+    got = {n: ctx.tensor(n) for n in ("Z1", "dL_dW1", "dL_dW2")}
+    ref = oracle_lib.OracleRun(p)
+    for n in ("Z1", "dL_dW1", "dL_dW2"):
+        assert_close(got[n], ref.tensor(n), TOL_TF32, n)
+    monkeypatch.setenv("TL_GEMM_NO_PAIRS", "1")
+    ctx.run(p)
+    # both 3xTF32: fp32-class agreement on Z1
+    assert_close(got["Z1"], ctx.tensor("Z1"), 1e-5, "Z1 (concatenated segments)")
+
+
 HEAD_CASES = [(32, 784, 256, 10, "relu(X[b,i] W1[i,h])"), (64, 20, 100, 32, "relu(X[b,i] W1[i,h] / 4)"),
               (1, 300, 33, 1, "X[b,i] W1[i,h]"), (17, 1024, 600, 7, "relu(X[b,i] W1[i,h])")]
 
